@@ -1,0 +1,352 @@
+"""Autograd functions of the model: linear layers with their TP collectives,
+RMSNorm, attention, SwiGLU, embedding and the fused LM-head cross entropy.
+
+Weight gradients are accumulated straight into each parameter's fp32
+``main_grad`` (a view into the stage's flat gradient buffer) inside the
+backward, instead of being returned to autograd; this is what lets the
+optimizer, the norm and the data-parallel reduction work on one flat buffer.
+A weight without ``main_grad`` (a standalone layer) gets its gradient through
+autograd as usual.
+
+Collectives: each function names its communication ``mode``.
+
+* column linear: ``"f"`` (identity fwd, all-reduce bwd), ``"ag"`` (sequence
+  all-gather fwd, reduce-scatter bwd) or ``"none"``;
+* row linear: ``"g"`` (all-reduce fwd), ``"rs"`` (reduce-scatter fwd,
+  all-gather bwd) or ``"none"``.
+
+On CUDA with a TP group of more than one GPU, ``"ag"`` and ``"rs"`` run the
+fused all-gather->GEMM and GEMM->reduce-scatter kernels of
+:mod:`nano_megatron_b200.ops.fused_tp`; everywhere else they run the generic
+collectives of :mod:`nano_megatron_b200.parallel.mappings`.
+
+Parity: ``nano_megatron/tp_layers.py:34-132``, ``model.py:65-192`` and
+``cross_entropy.py:16-85`` (same values; the collectives are the adjoint pairs
+of ``mappings.py:83-134``).
+"""
+
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+from .. import ops
+from ..parallel import mappings as M
+from ..parallel.context import ParallelContext
+
+
+class WeightRef:
+    """A weight as the kernels see it: master data, compute copy, grad buffer.
+
+    ``data`` is the fp32 master (a Parameter or a region of the flat buffer
+    that several Parameters view), ``compute`` an optional persistent bf16
+    mirror kept in sync by the optimizer, ``main_grad`` the fp32 gradient
+    accumulator (None for standalone layers), ``params`` the Parameters that
+    ``data`` backs, in order.
+    """
+
+    __slots__ = ("data", "compute", "main_grad", "params")
+
+    def __init__(self, data, params, compute=None, main_grad=None):
+        self.data = data
+        self.params = tuple(params)
+        self.compute = compute
+        self.main_grad = main_grad
+
+    @classmethod
+    def of(cls, param: torch.nn.Parameter) -> "WeightRef":
+        return cls(param, (param,), getattr(param, "compute_copy", None),
+                   getattr(param, "main_grad", None))
+
+    def for_compute(self, dtype: torch.dtype) -> torch.Tensor:
+        if self.compute is not None and self.compute.dtype == dtype:
+            return self.compute
+        data = self.data.detach()
+        return data if data.dtype == dtype else data.to(dtype)
+
+    def accumulate(self, grad_fn, *args):
+        """Accumulate via ``grad_fn(*args, out)``; returns autograd grads for ``params``."""
+        if self.main_grad is not None:
+            grad_fn(*args, self.main_grad)
+            return (None,) * len(self.params)
+        if len(self.params) != 1:
+            raise RuntimeError("a fused weight needs a main_grad buffer")
+        out = torch.zeros(self.data.shape, dtype=torch.float32, device=self.data.device)
+        grad_fn(*args, out)
+        return (out.to(self.data.dtype),)
+
+
+# ---------------------------------------------------------------- comm glue
+def _use_fused(pctx: ParallelContext, x: torch.Tensor) -> bool:
+    return x.is_cuda and pctx.tp_size > 1 and pctx.resources.get("fused_tp", False)
+
+
+def _ag(x, pctx):
+    return M.all_gather_sequence(x, pctx.tp_group, pctx.tp_size)
+
+
+def _rs(x, pctx):
+    return M.reduce_scatter_sequence(x, pctx.tp_group, pctx.tp_size)
+
+
+def _ar(x, pctx):
+    return M._all_reduce(x.contiguous(), pctx.tp_group, pctx.tp_size)
+
+
+# ------------------------------------------------------------ column linear
+class _ColumnLinear(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, wref, pctx, mode, dtype, *params):
+        x = x if x.dtype == dtype else x.to(dtype)
+        w = wref.for_compute(dtype)
+        if mode == "ag" and _use_fused(pctx, x):
+            from ..ops import fused_tp
+            y = fused_tp.all_gather_matmul(x, w, pctx)
+        else:
+            X = _ag(x, pctx) if mode == "ag" else x
+            y = ops.mm_nn(X, w)
+        ctx.save_for_backward(x, w)
+        ctx.wref, ctx.pctx, ctx.mode = wref, pctx, mode
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        x, w = ctx.saved_tensors
+        pctx, mode, wref = ctx.pctx, ctx.mode, ctx.wref
+        dy = dy.contiguous()
+        if mode == "ag" and _use_fused(pctx, dy):
+            from ..ops import fused_tp
+            dx = fused_tp.matmul_reduce_scatter(dy, w, pctx, transpose_b=True)
+            X = fused_tp.all_gather(x, pctx)
+        else:
+            dX = ops.mm_nt(dy, w)
+            dx = _rs(dX, pctx) if mode == "ag" else (_ar(dX, pctx) if mode == "f" else dX)
+            X = _ag(x, pctx) if mode == "ag" else x
+        grads = wref.accumulate(ops.mm_tn_acc, X, dy)
+        return (dx, None, None, None, None, *grads)
+
+
+def column_linear(x, wref: WeightRef, pctx: ParallelContext, mode: str, dtype: torch.dtype):
+    return _ColumnLinear.apply(x, wref, pctx, mode, dtype, *wref.params)
+
+
+# --------------------------------------------------------------- row linear
+class _RowLinear(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, wref, pctx, mode, dtype, *params):
+        x = x if x.dtype == dtype else x.to(dtype)
+        w = wref.for_compute(dtype)
+        if mode == "rs" and _use_fused(pctx, x):
+            from ..ops import fused_tp
+            y = fused_tp.matmul_reduce_scatter(x, w, pctx, transpose_b=False)
+        else:
+            y = ops.mm_nn(x, w)
+            if mode == "rs":
+                y = _rs(y, pctx)
+            elif mode == "g":
+                y = _ar(y, pctx)
+        ctx.save_for_backward(x, w)
+        ctx.wref, ctx.pctx, ctx.mode = wref, pctx, mode
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        x, w = ctx.saved_tensors
+        pctx, mode, wref = ctx.pctx, ctx.mode, ctx.wref
+        dy = dy.contiguous()
+        if mode == "rs" and _use_fused(pctx, dy):
+            from ..ops import fused_tp
+            dY, dx = fused_tp.all_gather_matmul(dy, w, pctx, transpose_b=True, return_gathered=True)
+        else:
+            dY = _ag(dy, pctx) if mode == "rs" else dy
+            dx = ops.mm_nt(dY, w)
+        grads = wref.accumulate(ops.mm_tn_acc, x, dY)
+        return (dx, None, None, None, None, *grads)
+
+
+def row_linear(x, wref: WeightRef, pctx: ParallelContext, mode: str, dtype: torch.dtype):
+    return _RowLinear.apply(x, wref, pctx, mode, dtype, *wref.params)
+
+
+# ------------------------------------------------------------------ RMSNorm
+class _RMSNorm(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, weight, eps):
+        y, rstd = ops.rmsnorm(x, weight.detach(), eps)
+        ctx.save_for_backward(x, weight, rstd)
+        ctx.main_grad = getattr(weight, "main_grad", None)
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        x, weight, rstd = ctx.saved_tensors
+        main_grad = ctx.main_grad
+        dx, dw = ops.rmsnorm_bwd(dy.contiguous(), x, weight.detach(), rstd, main_grad)
+        return dx, (None if main_grad is not None else dw.to(weight.dtype)), None
+
+
+def rms_norm(x, weight, eps):
+    return _RMSNorm.apply(x, weight, eps)
+
+
+# ---------------------------------------------------------------- attention
+class _Attention(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, qkv, batch, heads, head_dim, cos, sin):
+        o, saved = ops.attention(qkv.contiguous(), batch, heads, head_dim, cos, sin)
+        ctx.save_for_backward(*saved)
+        ctx.meta = (batch, heads, head_dim)
+        ctx.rope = (cos, sin)
+        return o
+
+    @staticmethod
+    def backward(ctx, do):
+        batch, heads, head_dim = ctx.meta
+        cos, sin = ctx.rope
+        dqkv = ops.attention_bwd(do.contiguous(), ctx.saved_tensors, batch, heads, head_dim, cos, sin)
+        return dqkv, None, None, None, None, None
+
+
+def causal_attention(qkv, batch, heads, head_dim, cos, sin):
+    """RoPE + causal MHA over a fused ``[S*b, 3*h*d]`` QKV buffer -> ``[S*b, h*d]``."""
+    return _Attention.apply(qkv, batch, heads, head_dim, cos, sin)
+
+
+# ------------------------------------------------------------------- SwiGLU
+class _SwiGLU(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, gu):
+        ctx.save_for_backward(gu)
+        return ops.swiglu(gu.contiguous())
+
+    @staticmethod
+    def backward(ctx, da):
+        (gu,) = ctx.saved_tensors
+        return ops.swiglu_bwd(da.contiguous(), gu)
+
+
+def swiglu(gu):
+    return _SwiGLU.apply(gu)
+
+
+# ---------------------------------------------------------------- embedding
+class _Embedding(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, ids, wref, pctx, mode, vocab_start, vocab_end, out_dtype, *params):
+        y = ops.embedding(ids, wref.data.detach(), vocab_start, vocab_end)
+        if y.dtype != out_dtype and y.is_cuda:
+            y = y.to(out_dtype)
+        if pctx.tp_size > 1:
+            y = _rs(y, pctx) if mode == "rs" else _ar(y, pctx)
+        ctx.save_for_backward(ids)
+        ctx.wref, ctx.pctx, ctx.mode, ctx.vrange = wref, pctx, mode, (vocab_start, vocab_end)
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        (ids,) = ctx.saved_tensors
+        pctx, wref = ctx.pctx, ctx.wref
+        dy = dy.contiguous()
+        if pctx.tp_size > 1 and ctx.mode == "rs":
+            dy = _ag(dy, pctx)
+        grads = wref.accumulate(lambda d, i, out: ops.embedding_bwd(d, i, out, *ctx.vrange), dy, ids)
+        return (None, None, None, None, None, None, None, *grads)
+
+
+def vocab_embedding(ids, wref, pctx, mode, vocab_start, vocab_end, out_dtype):
+    return _Embedding.apply(ids, wref, pctx, mode, vocab_start, vocab_end, out_dtype, *wref.params)
+
+
+# -------------------------------------------------- cross-entropy statistics
+def merge_ce_stats(mx, se, tl, pctx: ParallelContext):
+    """Combine per-shard ``(max, sumexp, target logit)`` into global ``(M, S, target)``.
+
+    One all-gather of a ``[3, T]`` block replaces the reference's three
+    all-reduces (``cross_entropy.py:23,38,43``):
+    ``M = max_r m_r``, ``S = sum_r s_r * exp(m_r - M)``, ``target = sum_r t_r``.
+    """
+    if pctx.tp_size == 1:
+        return mx, se, tl
+    stats = torch.stack([mx, se, tl]).contiguous()
+    gathered = torch.empty((pctx.tp_size * 3, stats.shape[1]), dtype=stats.dtype, device=stats.device)
+    dist.all_gather_into_tensor(gathered, stats, group=pctx.tp_group)
+    gathered = gathered.view(pctx.tp_size, 3, -1)
+    gm = gathered[:, 0].max(dim=0).values
+    gs = (gathered[:, 1] * (gathered[:, 0] - gm).exp()).sum(0)
+    gt = gathered[:, 2].sum(0)
+    return gm, gs, gt
+
+
+class _LMHeadCE(torch.autograd.Function):
+    """Vocab-parallel LM head + cross entropy; returns the mean token loss."""
+
+    @staticmethod
+    def forward(ctx, x, labels, wref, pctx, mode, dtype, vocab_start, vocab_end, *params):
+        x = x if x.dtype == dtype else x.to(dtype)
+        w = wref.for_compute(dtype)  # [V/t, H]
+        X = _ag(x, pctx) if mode == "ag" else x
+        if X.is_cuda:
+            loss_tok, state = ops.cuda_ops().lm_head_ce_fwd(X, w, labels, vocab_start, vocab_end, pctx)
+        else:
+            logits = ops.mm_nt(X, w)
+            mx, se, tl, _ = ops.ce_local_stats(logits, labels, vocab_start, vocab_end)
+            gm, gs, gt = merge_ce_stats(mx, se, tl, pctx)
+            loss_tok = gs.log() + gm - gt
+            state = (logits, gm, gs)
+        ctx.save_for_backward(x, labels, w, *state)
+        ctx.wref, ctx.pctx, ctx.mode, ctx.vrange, ctx.dtype = wref, pctx, mode, (vocab_start, vocab_end), dtype
+        return loss_tok.mean()
+
+    @staticmethod
+    def backward(ctx, g):
+        x, labels, w, *state = ctx.saved_tensors
+        pctx, mode, wref = ctx.pctx, ctx.mode, ctx.wref
+        n = labels.numel()
+        X = _ag(x, pctx) if mode == "ag" else x
+        if X.is_cuda:
+            dlogits = ops.cuda_ops().lm_head_ce_grad(X, w, labels, ctx.vrange[0], state, g / n)
+        else:
+            logits, gm, gs = state
+            scale = (g / n).expand(n).float()
+            dlogits = ops.ce_grad(logits, labels, ctx.vrange[0], gm, gs, scale, ctx.dtype)
+        dX = ops.mm_nn(dlogits, w)
+        if mode == "ag":
+            dx = _rs(dX, pctx)
+        elif mode == "f":
+            dx = _ar(dX, pctx)
+        else:
+            dx = dX
+        grads = wref.accumulate(ops.mm_tn_acc, dlogits, X)
+        return (dx, None, None, None, None, None, None, None, *grads)
+
+
+def lm_head_cross_entropy(x, labels, wref, pctx, mode, dtype, vocab_start, vocab_end):
+    return _LMHeadCE.apply(x, labels, wref, pctx, mode, dtype, vocab_start, vocab_end, *wref.params)
+
+
+class _LMHeadLogits(torch.autograd.Function):
+    """``logits = AG(x) @ W^T`` for a vocab-sharded ``W [V/tp, H]`` (no loss)."""
+
+    @staticmethod
+    def forward(ctx, x, wref, pctx, mode, dtype, *params):
+        x = x if x.dtype == dtype else x.to(dtype)
+        w = wref.for_compute(dtype)
+        X = _ag(x, pctx) if mode == "ag" else x
+        ctx.save_for_backward(x, w)
+        ctx.wref, ctx.pctx, ctx.mode = wref, pctx, mode
+        return ops.mm_nt(X, w)
+
+    @staticmethod
+    def backward(ctx, dy):
+        x, w = ctx.saved_tensors
+        pctx, mode, wref = ctx.pctx, ctx.mode, ctx.wref
+        dy = dy.contiguous()
+        X = _ag(x, pctx) if mode == "ag" else x
+        dX = ops.mm_nn(dy, w)
+        dx = _rs(dX, pctx) if mode == "ag" else (_ar(dX, pctx) if mode == "f" else dX)
+        grads = wref.accumulate(ops.mm_tn_acc, dy, X)
+        return (dx, None, None, None, None, *grads)
+
+
+def lm_head_logits(x, wref, pctx, mode, dtype):
+    return _LMHeadLogits.apply(x, wref, pctx, mode, dtype, *wref.params)

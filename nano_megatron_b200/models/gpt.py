@@ -1,0 +1,261 @@
+"""One pipeline stage of a decoder-only GPT: RMSNorm, RoPE, causal MHA, SwiGLU.
+
+A stage builds only its own layers: the embedding on the first stage, the final
+norm and LM head on the last. A non-first stage takes a hidden state, a
+non-last stage returns one, so the pipeline schedule stays outside the model.
+
+Layout: activations are sequence-first and token-major. A stage boundary
+carries ``[s, b, H]`` (``s = S/tp`` under sequence parallelism); inside a
+stage the residual stream is the flattened ``[s*b, H]``. Token ids and labels
+are given batch-first ``[b, S]`` as in the reference and transposed once.
+
+Attention uses one fused ``[H, 3H/tp]`` QKV weight and the MLP one fused
+``[H, 2F/tp]`` gate|up weight; the separate ``q``/``k``/``v`` and ``gate``/``up``
+Parameters (reference state-dict keys and shapes) are column views of them.
+
+Parity: ``nano_megatron/model.py:35-281``.
+"""
+
+from __future__ import annotations
+
+import contextlib
+
+import torch
+import torch.nn as nn
+from torch.utils.checkpoint import checkpoint
+
+from ..parallel.context import ParallelContext
+from .. import ops
+from .buffers import FlatBuffers
+from .config import GPTConfig, divide
+from .functional import (WeightRef, causal_attention, column_linear,
+                         lm_head_cross_entropy, lm_head_logits, row_linear, swiglu)
+from .layers import (ColumnParallelLinear, RMSNorm, RowParallelLinear,
+                     VocabParallelEmbedding)
+
+
+def build_rope_cache(seq_len, head_dim, device, base=10000.0):
+    """fp32 ``(cos, sin)`` tables ``[seq_len, head_dim/2]``; ``base`` is RoPE theta."""
+    return ops.rope_cache(seq_len, head_dim, base, device)
+
+
+def layers_for_stage(n_layer: int, pp_size: int, pp_rank: int) -> tuple[int, int]:
+    """Contiguous, equal split of the layers over the pipeline stages."""
+    per_stage = divide(n_layer, pp_size)
+    return pp_rank * per_stage, (pp_rank + 1) * per_stage
+
+
+def _fused_ref(buffers: FlatBuffers | None, params) -> WeightRef:
+    if buffers is None:
+        raise RuntimeError("fused projections need the model's flat buffers")
+    region = buffers.region_of(params[0])
+    return WeightRef(region.data_block, params, region.compute_block, region.grad_block)
+
+
+class ParallelAttention(nn.Module):
+    """MHA sharded over heads; one fused QKV GEMM, one row-parallel output GEMM."""
+
+    def __init__(self, config: GPTConfig, ctx: ParallelContext):
+        super().__init__()
+        self.ctx = ctx
+        self.n_head_local = divide(config.n_head, ctx.tp_size)
+        self.head_dim = config.head_dim
+        self.sequence_parallel = config.sequence_parallel
+        std = config.init_std
+        h = config.n_embd
+        self.q = ColumnParallelLinear(h, h, ctx, bias=False, init_std=std)
+        self.k = ColumnParallelLinear(h, h, ctx, bias=False, init_std=std)
+        self.v = ColumnParallelLinear(h, h, ctx, bias=False, init_std=std)
+        self.proj = RowParallelLinear(h, h, ctx, bias=False, init_std=std)
+        self.flat_buffers: FlatBuffers | None = None
+
+    def fused_groups(self, prefix: str):
+        return [[f"{prefix}q.weight", f"{prefix}k.weight", f"{prefix}v.weight"]]
+
+    def forward(self, x, batch, cos, sin, dtype):
+        """``x [s*b, H]`` (already normed) -> ``[s*b, H]``."""
+        sp = self.sequence_parallel and self.ctx.tp_size > 1
+        qkv_ref = _fused_ref(self.flat_buffers, (self.q.weight, self.k.weight, self.v.weight))
+        qkv = column_linear(x, qkv_ref, self.ctx, "ag" if sp else "f", dtype)
+        o = causal_attention(qkv, batch, self.n_head_local, self.head_dim, cos, sin)
+        return row_linear(o, WeightRef.of(self.proj.weight), self.ctx, "rs" if sp else "g", dtype)
+
+
+class ParallelMLP(nn.Module):
+    """SwiGLU: fused gate|up column-parallel GEMM, row-parallel down GEMM."""
+
+    def __init__(self, config: GPTConfig, ctx: ParallelContext):
+        super().__init__()
+        self.ctx = ctx
+        self.sequence_parallel = config.sequence_parallel
+        h, f, std = config.n_embd, config.ffn_size, config.init_std
+        self.gate = ColumnParallelLinear(h, f, ctx, bias=False, init_std=std)
+        self.up = ColumnParallelLinear(h, f, ctx, bias=False, init_std=std)
+        self.down = RowParallelLinear(f, h, ctx, bias=False, init_std=std)
+        self.flat_buffers: FlatBuffers | None = None
+
+    def fused_groups(self, prefix: str):
+        return [[f"{prefix}gate.weight", f"{prefix}up.weight"]]
+
+    def forward(self, x, dtype):
+        sp = self.sequence_parallel and self.ctx.tp_size > 1
+        gu_ref = _fused_ref(self.flat_buffers, (self.gate.weight, self.up.weight))
+        gu = column_linear(x, gu_ref, self.ctx, "ag" if sp else "f", dtype)
+        return row_linear(swiglu(gu), WeightRef.of(self.down.weight), self.ctx,
+                          "rs" if sp else "g", dtype)
+
+
+class TransformerLayer(nn.Module):
+    """Pre-norm block: ``x + attn(norm(x))`` then ``x + mlp(norm(x))``."""
+
+    def __init__(self, config: GPTConfig, ctx: ParallelContext):
+        super().__init__()
+        self.attn_norm = RMSNorm(config.n_embd)
+        self.attn = ParallelAttention(config, ctx)
+        self.mlp_norm = RMSNorm(config.n_embd)
+        self.mlp = ParallelMLP(config, ctx)
+
+    def forward(self, x, batch, cos, sin, dtype):
+        x = x + self.attn(self.attn_norm(x), batch, cos, sin, dtype)
+        return x + self.mlp(self.mlp_norm(x), dtype)
+
+
+class ParallelLMHead(nn.Module):
+    """Vocab-sharded output projection ``[V/tp, H]`` (the embedding's layout, so they can tie)."""
+
+    def __init__(self, config: GPTConfig, ctx: ParallelContext):
+        super().__init__()
+        self.ctx = ctx
+        per_partition = divide(config.vocab_size, ctx.tp_size)
+        self.weight = nn.Parameter(torch.empty(per_partition, config.n_embd))
+        self.weight.tensor_parallel_sharded = True
+        self.sequence_parallel = config.sequence_parallel
+        nn.init.normal_(self.weight, std=config.init_std)
+
+
+class GPT(nn.Module):
+    def __init__(self, config: GPTConfig, ctx: ParallelContext | None = None,
+                 device: torch.device | str | None = None):
+        super().__init__()
+        ctx = ctx or ParallelContext.single()
+        self.config = config
+        self.ctx = ctx
+        self.first_stage = ctx.is_first_stage
+        self.last_stage = ctx.is_last_stage
+        config.activation_dtype  # validate before allocating parameters
+        for name in ("vocab_size", "n_layer", "n_head", "n_embd", "seq_len"):
+            if getattr(config, name) <= 0:
+                raise ValueError(f"{name} must be positive")
+        if config.ffn_hidden_size is not None and config.ffn_hidden_size <= 0:
+            raise ValueError("ffn_hidden_size must be positive")
+        divide(config.n_layer, ctx.pp_size)
+        divide(config.n_embd, ctx.tp_size)
+        divide(config.n_head, ctx.tp_size)
+        divide(config.vocab_size, ctx.tp_size)
+        divide(config.ffn_size, ctx.tp_size)
+        if config.head_dim % 2:
+            raise ValueError("RoPE requires an even attention head dimension")
+        if config.sequence_parallel:
+            divide(config.seq_len, ctx.tp_size)
+
+        with torch.device(device) if device is not None else contextlib.nullcontext():
+            start, end = layers_for_stage(config.n_layer, ctx.pp_size, ctx.pp_rank)
+            self.layers = nn.ModuleList([TransformerLayer(config, ctx) for _ in range(start, end)])
+            if self.first_stage:
+                self.embedding = VocabParallelEmbedding(config.vocab_size, config.n_embd, ctx,
+                                                        init_std=config.init_std)
+            if self.last_stage:
+                self.final_norm = RMSNorm(config.n_embd)
+                self.lm_head = ParallelLMHead(config, ctx)
+            # One stage: the tie is one shared tensor. Split across stages the
+            # two copies are kept equal by the tied-group broadcast/all-reduce.
+            if config.tie_word_embeddings and self.first_stage and self.last_stage:
+                self.lm_head.weight = self.embedding.weight
+            cos, sin = build_rope_cache(config.seq_len, config.head_dim, None, config.rope_theta)
+        self.register_buffer("rope_cos", cos, persistent=False)
+        self.register_buffer("rope_sin", sin, persistent=False)
+        self.flat_buffers: FlatBuffers | None = None
+        self._build_buffers()
+
+    # ---------------------------------------------------------- flat buffers
+    def _build_buffers(self) -> None:
+        groups = []
+        for name, module in self.named_modules():
+            if hasattr(module, "fused_groups"):
+                groups.extend(module.fused_groups(f"{name}." if name else ""))
+        compute = self.config.activation_dtype
+        on_cuda = next(self.parameters()).is_cuda
+        self.flat_buffers = FlatBuffers(self, groups, compute if on_cuda else None)
+        for module in self.modules():
+            if isinstance(module, (ParallelAttention, ParallelMLP)):
+                module.flat_buffers = self.flat_buffers
+
+    def _apply(self, fn, recurse=True):
+        # Moving or casting re-creates each parameter separately; rebuild the
+        # flat buffers so parameters stay views of one allocation.
+        result = super()._apply(fn, recurse)
+        if getattr(self, "flat_buffers", None) is not None:
+            self._build_buffers()
+        return result
+
+    def zero_grad(self, set_to_none: bool = True) -> None:
+        """Zero the flat gradient buffer; ``param.grad`` stays a view of it."""
+        self.flat_buffers.zero_grad()
+
+    def refresh_compute_copies(self) -> None:
+        self.flat_buffers.refresh_compute()
+
+    def load_state_dict(self, state_dict, strict: bool = True, assign: bool = False):
+        if assign:
+            raise ValueError("assign=True would detach parameters from the flat buffers")
+        result = super().load_state_dict(state_dict, strict=strict)
+        self.refresh_compute_copies()
+        return result
+
+    # --------------------------------------------------------------- forward
+    def vocab_range(self) -> tuple[int, int]:
+        per = divide(self.config.vocab_size, self.ctx.tp_size)
+        return self.ctx.tp_rank * per, (self.ctx.tp_rank + 1) * per
+
+    def _layer_call(self, layer, h, batch, dtype):
+        cos, sin = self.rope_cos, self.rope_sin
+        if self.config.recompute and self.training:
+            return checkpoint(layer, h, batch, cos, sin, dtype, use_reentrant=False)
+        return layer(h, batch, cos, sin, dtype)
+
+    def forward(self, x, labels=None):
+        """Token ids ``[b, S]`` on the first stage, hidden ``[s, b, H]`` elsewhere.
+
+        Returns the mean loss on the last stage when ``labels [b, S]`` is
+        given, the vocab-sharded logits ``[b, S, V/tp]`` when it is not, and
+        the hidden state ``[s, b, H]`` on every other stage.
+        """
+        cfg, ctx = self.config, self.ctx
+        dtype = cfg.activation_dtype
+        sp = cfg.sequence_parallel and ctx.tp_size > 1
+        if self.first_stage:
+            batch = x.shape[0]
+            ids = x.t().contiguous()  # [S, b]
+            h = self.embedding(ids, sequence_parallel=sp, out_dtype=dtype)
+            h = h.reshape(-1, cfg.n_embd)
+        else:
+            batch = x.shape[1]
+            h = x.reshape(-1, cfg.n_embd)
+        if h.dtype != dtype:
+            h = h.to(dtype)
+
+        for layer in self.layers:
+            h = self._layer_call(layer, h, batch, dtype)
+
+        if not self.last_stage:
+            return h.view(-1, batch, cfg.n_embd)
+
+        hn = self.final_norm(h)
+        head = WeightRef.of(self.lm_head.weight)
+        mode = "ag" if sp else "f"
+        if labels is None:
+            logits = lm_head_logits(hn, head, ctx, mode, dtype)
+            return logits.view(cfg.seq_len, batch, -1).transpose(0, 1)
+        start, end = self.vocab_range()
+        labels_sf = labels.t().reshape(-1)
+        return lm_head_cross_entropy(hn, labels_sf, head, ctx, mode, dtype, start, end)

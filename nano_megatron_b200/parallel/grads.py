@@ -1,0 +1,197 @@
+"""Gradient finalization, initial parameter sync and logical-norm clipping.
+
+After the pipeline backward:
+
+1. TP-replicated parameters (RMSNorm weights, replicated biases) are summed
+   over the TP group: averaged without sequence parallelism (every TP rank saw
+   the same tokens), kept as a SUM with it (ranks saw disjoint tokens). All
+   replicated gradients travel in ONE coalesced all-reduce.
+2. Tied embedding copies on the first and last pipeline stages are summed over
+   the tied group.
+3. Data-parallel replicas average their gradients. On a model with flat
+   buffers this is one all-reduce of the flat gradient buffer (or, with a
+   :class:`GradBucketer`, bucket by bucket overlapped with the last backward).
+
+Clipping uses the L2 norm of the logical unsharded model accumulated in
+fp64: TP shards add, replicated parameters count ``1/tp``, pipeline stages add,
+DP is never reduced, and a tied last-stage LM head is counted once.
+
+Parity: ``nano_megatron/grads.py:16-193``.
+"""
+
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+from .context import ParallelContext
+
+
+def _is_sharded(param) -> bool:
+    return getattr(param, "tensor_parallel_sharded", False)
+
+
+def _flat_buffers(model):
+    return getattr(model, "flat_buffers", None)
+
+
+def all_reduce_replicated_gradients(model, ctx: ParallelContext, *, sequence_parallel: bool = False) -> None:
+    """One coalesced all-reduce of every TP-replicated gradient."""
+    if ctx.tp_size == 1:
+        return
+    grads = [p.grad for p in model.parameters() if p.grad is not None and not _is_sharded(p)]
+    if not grads:
+        return
+    flat = torch.cat([g.reshape(-1) for g in grads])
+    dist.all_reduce(flat, group=ctx.tp_group)
+    if not sequence_parallel:
+        flat /= ctx.tp_size
+    offset = 0
+    for g in grads:
+        n = g.numel()
+        g.copy_(flat[offset: offset + n].view_as(g))
+        offset += n
+
+
+def all_reduce_data_parallel_gradients(model, ctx: ParallelContext) -> None:
+    """Average gradients over the DP group (flat buffer: one collective)."""
+    if ctx.dp_size == 1:
+        return
+    buffers = _flat_buffers(model)
+    if buffers is not None:
+        _dp_average(buffers.grad, ctx)
+        return
+    by_key: dict = {}
+    for p in model.parameters():
+        if p.grad is not None:
+            by_key.setdefault((p.grad.device, p.grad.dtype), []).append(p.grad)
+    for grads in by_key.values():
+        flat = torch.cat([g.reshape(-1) for g in grads])
+        _dp_average(flat, ctx)
+        offset = 0
+        for g in grads:
+            n = g.numel()
+            g.copy_(flat[offset: offset + n].view_as(g))
+            offset += n
+
+
+def _dp_average(flat: torch.Tensor, ctx: ParallelContext) -> None:
+    if flat.is_cuda:
+        # NCCL folds the 1/dp scale into the reduction (pre-multiplied sum).
+        dist.all_reduce(flat, op=dist.ReduceOp.AVG, group=ctx.dp_group)
+    else:
+        dist.all_reduce(flat, group=ctx.dp_group)
+        flat /= ctx.dp_size
+
+
+def all_reduce_embedding_gradients(model, ctx: ParallelContext) -> None:
+    """SUM the tied embedding / LM-head gradient copies over the tied group."""
+    if ctx.pp_size == 1 or ctx.tied_group is None:
+        return
+    if not (ctx.is_first_stage or ctx.is_last_stage):
+        return
+    module = getattr(model, "embedding" if ctx.is_first_stage else "lm_head", None)
+    if module is None or module.weight.grad is None:
+        return
+    dist.all_reduce(module.weight.grad, group=ctx.tied_group)
+
+
+def synchronize_tied_embeddings(model, ctx: ParallelContext) -> None:
+    """Broadcast the first stage's embedding into the last stage's LM head."""
+    if ctx.pp_size == 1 or ctx.tied_group is None:
+        return
+    if not (ctx.is_first_stage or ctx.is_last_stage):
+        return
+    module = getattr(model, "embedding" if ctx.is_first_stage else "lm_head", None)
+    if module is None:
+        return
+    dist.broadcast(module.weight.data, src=ctx.pp_ranks[0], group=ctx.tied_group)
+
+
+def synchronize_model_parameters(model, ctx: ParallelContext, *, tie_embeddings: bool = False) -> None:
+    """Make replicated parameters agree after rank-dependent initialization."""
+    if ctx.tp_size > 1:
+        for p in model.parameters():
+            if not _is_sharded(p):
+                dist.broadcast(p.data, src=ctx.tp_ranks[0], group=ctx.tp_group)
+    if ctx.dp_size > 1:
+        buffers = _flat_buffers(model)
+        if buffers is not None:
+            dist.broadcast(buffers.data, src=ctx.dp_ranks[0], group=ctx.dp_group)
+        else:
+            for p in model.parameters():
+                dist.broadcast(p.data, src=ctx.dp_ranks[0], group=ctx.dp_group)
+    if tie_embeddings:
+        synchronize_tied_embeddings(model, ctx)
+    refresh = getattr(model, "refresh_compute_copies", None)
+    if refresh is not None:
+        refresh()
+
+
+def finalize_gradients(model, ctx: ParallelContext, *, tie_embeddings: bool = False,
+                       sequence_parallel: bool = False, skip_data_parallel: bool = False) -> None:
+    """Replicated-TP, then tied, then DP reduction (``skip_data_parallel`` when a
+    bucketer already reduced the DP gradients during backward)."""
+    all_reduce_replicated_gradients(model, ctx, sequence_parallel=sequence_parallel)
+    if tie_embeddings:
+        all_reduce_embedding_gradients(model, ctx)
+    if not skip_data_parallel:
+        all_reduce_data_parallel_gradients(model, ctx)
+
+
+def _norm_terms(model, ctx: ParallelContext, tie_embeddings: bool):
+    """``(param, weight)`` pairs: each grad's squared norm counts ``weight`` times."""
+    terms = []
+    for name, p in model.named_parameters():
+        if p.grad is None:
+            continue
+        if tie_embeddings and ctx.pp_size > 1 and ctx.is_last_stage and name == "lm_head.weight":
+            continue  # the same logical parameter as the first stage's embedding
+        terms.append((p, 1.0 if _is_sharded(p) else 1.0 / ctx.tp_size))
+    return terms
+
+
+def grad_norm_squared(model, ctx: ParallelContext, *, tie_embeddings: bool = False) -> torch.Tensor:
+    """Logical-model squared gradient norm (fp64), reduced over TP then PP."""
+    params = list(model.parameters())
+    device = params[0].device if params else torch.device("cpu")
+    terms = _norm_terms(model, ctx, tie_embeddings)
+    if device.type == "cuda" and terms:
+        from .. import ops
+        total = ops.cuda_ops().weighted_sq_norm([p.grad for p, _ in terms], [w for _, w in terms])
+    else:
+        total = torch.zeros((), dtype=torch.float64, device=device)
+        for p, w in terms:
+            total += p.grad.detach().double().pow(2).sum() * w
+    if ctx.tp_size > 1:
+        dist.all_reduce(total, group=ctx.tp_group)
+    if ctx.pp_size > 1:
+        dist.all_reduce(total, group=ctx.pp_group)
+    return total
+
+
+def clip_coefficient(total_norm: torch.Tensor, max_norm: float) -> torch.Tensor:
+    """``min(1, max_norm / (norm + 1e-6))`` as a device tensor."""
+    return torch.clamp(max_norm / (total_norm + 1e-6), max=1.0)
+
+
+def clip_grad_norm(model, ctx: ParallelContext, max_norm: float, *, tie_embeddings: bool = False,
+                   apply: bool = True) -> torch.Tensor:
+    """Clip every gradient by the logical-model norm; return that norm (fp64).
+
+    With ``apply=False`` the gradients are left untouched and the caller
+    applies the coefficient itself (the fused optimizer does it on load).
+    """
+    if max_norm < 0:
+        raise ValueError(f"max_norm must be non-negative, got {max_norm}")
+    total_norm = grad_norm_squared(model, ctx, tie_embeddings=tie_embeddings).sqrt()
+    if apply:
+        coefficient = clip_coefficient(total_norm, max_norm)
+        buffers = _flat_buffers(model)
+        if buffers is not None:
+            buffers.grad.mul_(coefficient.to(buffers.grad.dtype))
+        else:
+            for p in model.parameters():
+                if p.grad is not None:
+                    p.grad.mul_(coefficient.to(dtype=p.grad.dtype))
+    return total_norm
