@@ -1,0 +1,96 @@
+// Python bindings of the sm_100a kernels (torch extension ``nano_megatron_b200._C``).
+//
+// Every entry point validates device, dtype, contiguity/strides and alignment,
+// then launches on the current torch CUDA stream. Shape logic that differs
+// per call site (which operand is transposed, what the output is) lives in
+// ``nano_megatron_b200/ops/cuda.py``.
+
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include "gemm.cuh"
+#include "kernels.cuh"
+
+namespace {
+
+void check_cuda(const at::Tensor& t, const char* name) {
+  TORCH_CHECK(t.is_cuda(), name, " must be a CUDA tensor");
+}
+
+void check_ok(cudaError_t e, const char* what) {
+  TORCH_CHECK(e == cudaSuccess, what, " failed: ", cudaGetErrorString(e));
+}
+
+int* err_ptr(const c10::optional<at::Tensor>& err) {
+  if (!err.has_value()) return nullptr;
+  TORCH_CHECK(err->is_cuda() && err->scalar_type() == at::kInt, "err must be a CUDA int32 tensor");
+  return err->data_ptr<int>();
+}
+
+int num_sms() {
+  static int n = 0;
+  if (n == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  }
+  return n;
+}
+
+long row_stride(const at::Tensor& t) {
+  TORCH_CHECK(t.dim() == 2 && t.stride(1) == 1, "expected a 2-D tensor with unit inner stride");
+  return t.stride(0);
+}
+
+// C (op)= A x B on tcgen05. A is [M,K] (a_mn=False) or [K,M] (a_mn=True);
+// B is [N,K] (b_mn=False) or [K,N] (b_mn=True); C is [M,N].
+// out_mode: 0 bf16 store, 1 fp32 store, 2 fp32 accumulate.
+void gemm(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, bool a_mn, bool b_mn, int64_t out_mode,
+          const c10::optional<at::Tensor>& err) {
+  check_cuda(A, "A");
+  check_cuda(B, "B");
+  check_cuda(C, "C");
+  TORCH_CHECK(A.scalar_type() == at::kBFloat16 && B.scalar_type() == at::kBFloat16, "A and B must be bf16");
+  TORCH_CHECK(out_mode == 0 ? C.scalar_type() == at::kBFloat16 : C.scalar_type() == at::kFloat,
+              "C dtype does not match out_mode");
+  const int M = a_mn ? A.size(1) : A.size(0);
+  const int K = a_mn ? A.size(0) : A.size(1);
+  const int N = b_mn ? B.size(1) : B.size(0);
+  const int Kb = b_mn ? B.size(0) : B.size(1);
+  TORCH_CHECK(K == Kb, "inner dimensions differ: ", K, " vs ", Kb);
+  TORCH_CHECK(C.size(0) == M && C.size(1) == N, "C has the wrong shape");
+  nmb::GemmArgs g{};
+  g.A = A.data_ptr();
+  g.B = B.data_ptr();
+  g.C = C.data_ptr();
+  g.lda = row_stride(A);
+  g.ldb = row_stride(B);
+  g.ldc = row_stride(C);
+  TORCH_CHECK(g.lda % 8 == 0 && g.ldb % 8 == 0, "bf16 row strides must be multiples of 8 elements");
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(g.A) % 16 == 0 && reinterpret_cast<uintptr_t>(g.B) % 16 == 0 &&
+                  reinterpret_cast<uintptr_t>(g.C) % 16 == 0,
+              "operands must be 16-byte aligned");
+  TORCH_CHECK(N % 8 == 0 && g.ldc % 8 == 0, "N and ldc must be multiples of 8");
+  g.M = M;
+  g.N = N;
+  g.K = K;
+  g.a_mn = a_mn;
+  g.b_mn = b_mn;
+  g.out = static_cast<nmb::OutMode>(out_mode);
+  g.err = err_ptr(err);
+  g.num_sms = num_sms();
+  const at::cuda::CUDAGuard guard(A.device());
+  check_ok(nmb::gemm_bf16(g, at::cuda::getCurrentCUDAStream()), "gemm_bf16");
+}
+
+}  // namespace
+
+void register_elementwise(pybind11::module& m);
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "nano_megatron_b200 sm_100a kernels";
+  m.def("gemm", &gemm, "tcgen05 bf16 GEMM", pybind11::arg("A"), pybind11::arg("B"), pybind11::arg("C"),
+        pybind11::arg("a_mn"), pybind11::arg("b_mn"), pybind11::arg("out_mode"), pybind11::arg("err") = pybind11::none());
+  register_elementwise(m);
+}

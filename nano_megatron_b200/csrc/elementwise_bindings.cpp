@@ -1,0 +1,163 @@
+// Bindings of the memory-bound kernels (kernels.cu).
+
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include "kernels.cuh"
+
+namespace {
+
+int dtype_tag(const at::Tensor& t) {
+  if (t.scalar_type() == at::kBFloat16) return 1;
+  TORCH_CHECK(t.scalar_type() == at::kFloat, "expected bf16 or fp32, got ", t.scalar_type());
+  return 0;
+}
+
+void need(const at::Tensor& t, const char* name) {
+  TORCH_CHECK(t.is_cuda() && t.is_contiguous(), name, " must be a contiguous CUDA tensor");
+}
+
+void ok(cudaError_t e, const char* what) { TORCH_CHECK(e == cudaSuccess, what, ": ", cudaGetErrorString(e)); }
+
+cudaStream_t stream() { return at::cuda::getCurrentCUDAStream(); }
+
+int* err_ptr(const c10::optional<at::Tensor>& err) {
+  return err.has_value() ? err->data_ptr<int>() : nullptr;
+}
+
+void rmsnorm_fwd(const at::Tensor& x, const at::Tensor& w, at::Tensor& y, at::Tensor& rstd, double eps) {
+  need(x, "x"); need(w, "w"); need(y, "y"); need(rstd, "rstd");
+  TORCH_CHECK(w.scalar_type() == at::kFloat && rstd.scalar_type() == at::kFloat, "w, rstd must be fp32");
+  const at::cuda::CUDAGuard g(x.device());
+  ok(nmb::rmsnorm_fwd(x.data_ptr(), w.data_ptr<float>(), y.data_ptr(), rstd.data_ptr<float>(), x.size(0), x.size(1),
+                      (float)eps, dtype_tag(x), stream()),
+     "rmsnorm_fwd");
+}
+
+int64_t rmsnorm_bwd_blocks(int64_t rows) { return nmb::rmsnorm_bwd_blocks((int)rows); }
+
+void rmsnorm_bwd(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& w, const at::Tensor& rstd, at::Tensor& dx,
+                 at::Tensor& partial) {
+  need(dy, "dy"); need(x, "x"); need(w, "w"); need(rstd, "rstd"); need(dx, "dx"); need(partial, "partial");
+  TORCH_CHECK(partial.size(0) >= nmb::rmsnorm_bwd_blocks(x.size(0)) && partial.size(1) == x.size(1),
+              "partial buffer too small");
+  const at::cuda::CUDAGuard g(x.device());
+  ok(nmb::rmsnorm_bwd(dy.data_ptr(), x.data_ptr(), w.data_ptr<float>(), rstd.data_ptr<float>(), dx.data_ptr(),
+                      partial.data_ptr<float>(), x.size(0), x.size(1), dtype_tag(x), stream()),
+     "rmsnorm_bwd");
+}
+
+void reduce_rows_add(const at::Tensor& partial, int64_t nrows, at::Tensor& out) {
+  need(partial, "partial");
+  TORCH_CHECK(out.is_cuda() && out.scalar_type() == at::kFloat && out.stride(-1) == 1, "out must be fp32 CUDA");
+  TORCH_CHECK(out.numel() == partial.size(1), "out size mismatch");
+  ok(nmb::reduce_rows_add(partial.data_ptr<float>(), out.data_ptr<float>(), (int)nrows, partial.size(1), stream()),
+     "reduce_rows_add");
+}
+
+void swiglu_fwd(const at::Tensor& gu, at::Tensor& a) {
+  need(gu, "gu"); need(a, "a");
+  ok(nmb::swiglu_fwd(gu.data_ptr(), a.data_ptr(), gu.size(0), a.size(1), dtype_tag(gu), stream()), "swiglu_fwd");
+}
+
+void swiglu_bwd(const at::Tensor& da, const at::Tensor& gu, at::Tensor& dgu) {
+  need(da, "da"); need(gu, "gu"); need(dgu, "dgu");
+  ok(nmb::swiglu_bwd(da.data_ptr(), gu.data_ptr(), dgu.data_ptr(), gu.size(0), da.size(1), dtype_tag(gu), stream()),
+     "swiglu_bwd");
+}
+
+void rope_inplace(at::Tensor& qkv, const at::Tensor& cos, const at::Tensor& sin, int64_t batch, int64_t heads,
+                  int64_t hd, double sign) {
+  need(qkv, "qkv"); need(cos, "cos"); need(sin, "sin");
+  TORCH_CHECK(qkv.size(1) == 3 * heads * hd, "qkv width mismatch");
+  TORCH_CHECK(cos.size(0) * batch >= qkv.size(0), "rope table shorter than the sequence");
+  ok(nmb::rope_inplace(qkv.data_ptr(), cos.data_ptr<float>(), sin.data_ptr<float>(), qkv.size(0), (int)batch,
+                       (int)heads, (int)hd, (float)sign, dtype_tag(qkv), stream()),
+     "rope_inplace");
+}
+
+void embedding_fwd(const at::Tensor& ids, const at::Tensor& w, at::Tensor& out, int64_t vstart, int64_t vend,
+                   int64_t vocab, const c10::optional<at::Tensor>& err) {
+  need(ids, "ids"); need(w, "w"); need(out, "out");
+  TORCH_CHECK(ids.scalar_type() == at::kLong && w.scalar_type() == at::kFloat, "ids int64, w fp32");
+  ok(nmb::embedding_fwd(ids.data_ptr<int64_t>(), w.data_ptr<float>(), out.data_ptr(), ids.numel(), w.size(1), vstart,
+                        vend, vocab, dtype_tag(out), err_ptr(err), stream()),
+     "embedding_fwd");
+}
+
+void embedding_bwd(const at::Tensor& dy, const at::Tensor& ids, at::Tensor& wgrad, int64_t vstart, int64_t vend) {
+  need(dy, "dy"); need(ids, "ids");
+  TORCH_CHECK(wgrad.is_cuda() && wgrad.is_contiguous() && wgrad.scalar_type() == at::kFloat, "wgrad fp32 contiguous");
+  ok(nmb::embedding_bwd(dy.data_ptr(), ids.data_ptr<int64_t>(), wgrad.data_ptr<float>(), ids.numel(), dy.size(1),
+                        vstart, vend, dtype_tag(dy), stream()),
+     "embedding_bwd");
+}
+
+void ce_stats(const at::Tensor& logits, const at::Tensor& target, at::Tensor& mx, at::Tensor& se, at::Tensor& tl,
+              int64_t vstart) {
+  TORCH_CHECK(logits.is_cuda() && logits.stride(1) == 1, "logits must be row-major CUDA");
+  need(target, "target"); need(mx, "mx"); need(se, "se"); need(tl, "tl");
+  ok(nmb::ce_stats(logits.data_ptr(), target.data_ptr<int64_t>(), mx.data_ptr<float>(), se.data_ptr<float>(),
+                   tl.data_ptr<float>(), logits.size(0), logits.size(1), logits.stride(0), vstart, dtype_tag(logits),
+                   stream()),
+     "ce_stats");
+}
+
+void ce_grad(const at::Tensor& logits, const at::Tensor& target, const at::Tensor& gmax, const at::Tensor& gsum,
+             const at::Tensor& gscale, double inv_n, at::Tensor& dlogits, int64_t vstart) {
+  TORCH_CHECK(logits.is_cuda() && logits.stride(1) == 1, "logits must be row-major CUDA");
+  need(target, "target"); need(gmax, "gmax"); need(gsum, "gsum"); need(dlogits, "dlogits");
+  TORCH_CHECK(gscale.is_cuda() && gscale.scalar_type() == at::kFloat, "gscale fp32 CUDA");
+  TORCH_CHECK(dlogits.scalar_type() == logits.scalar_type(), "dlogits dtype");
+  ok(nmb::ce_grad(logits.data_ptr(), target.data_ptr<int64_t>(), gmax.data_ptr<float>(), gsum.data_ptr<float>(),
+                  gscale.data_ptr<float>(), (float)inv_n, dlogits.data_ptr(), logits.size(0), logits.size(1),
+                  logits.stride(0), vstart, dtype_tag(logits), stream()),
+     "ce_grad");
+}
+
+void adamw_flat(at::Tensor& p, const at::Tensor& g, at::Tensor& m, at::Tensor& v,
+                const c10::optional<at::Tensor>& compute, const at::Tensor& scale, double lr, double beta1,
+                double beta2, double eps, double wd, int64_t step) {
+  need(p, "p"); need(g, "g"); need(m, "m"); need(v, "v");
+  TORCH_CHECK(p.numel() == g.numel() && p.numel() == m.numel() && p.numel() == v.numel(), "size mismatch");
+  __nv_bfloat16* c = nullptr;
+  if (compute.has_value()) {
+    need(*compute, "compute");
+    TORCH_CHECK(compute->scalar_type() == at::kBFloat16 && compute->numel() == p.numel(), "compute copy");
+    c = reinterpret_cast<__nv_bfloat16*>(compute->data_ptr());
+  }
+  const double bc1 = 1.0 - std::pow(beta1, (double)step);
+  const double bc2 = 1.0 - std::pow(beta2, (double)step);
+  ok(nmb::adamw_flat(p.data_ptr<float>(), g.data_ptr<float>(), m.data_ptr<float>(), v.data_ptr<float>(), c,
+                     scale.data_ptr<float>(), p.numel(), (float)lr, (float)beta1, (float)beta2, (float)eps, (float)wd,
+                     (float)bc1, (float)std::sqrt(bc2), stream()),
+     "adamw_flat");
+}
+
+void weighted_sq_norm(const at::Tensor& ptrs, const at::Tensor& numels, const at::Tensor& weights, at::Tensor& out) {
+  need(ptrs, "ptrs"); need(numels, "numels"); need(weights, "weights");
+  TORCH_CHECK(out.is_cuda() && out.scalar_type() == at::kDouble, "out fp64 CUDA");
+  ok(nmb::weighted_sq_norm(ptrs.data_ptr<int64_t>(), numels.data_ptr<int64_t>(), weights.data_ptr<double>(),
+                           ptrs.numel(), out.data_ptr<double>(), stream()),
+     "weighted_sq_norm");
+}
+
+}  // namespace
+
+void register_elementwise(pybind11::module& m) {
+  m.def("rmsnorm_fwd", &rmsnorm_fwd);
+  m.def("rmsnorm_bwd", &rmsnorm_bwd);
+  m.def("rmsnorm_bwd_blocks", &rmsnorm_bwd_blocks);
+  m.def("reduce_rows_add", &reduce_rows_add);
+  m.def("swiglu_fwd", &swiglu_fwd);
+  m.def("swiglu_bwd", &swiglu_bwd);
+  m.def("rope_inplace", &rope_inplace);
+  m.def("embedding_fwd", &embedding_fwd, pybind11::arg("ids"), pybind11::arg("w"), pybind11::arg("out"),
+        pybind11::arg("vstart"), pybind11::arg("vend"), pybind11::arg("vocab"), pybind11::arg("err") = pybind11::none());
+  m.def("embedding_bwd", &embedding_bwd);
+  m.def("ce_stats", &ce_stats);
+  m.def("ce_grad", &ce_grad);
+  m.def("adamw_flat", &adamw_flat);
+  m.def("weighted_sq_norm", &weighted_sq_norm);
+}

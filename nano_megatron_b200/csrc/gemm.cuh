@@ -1,0 +1,31 @@
+// Host interface of the tcgen05 GEMM (gemm.cu).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+namespace nmb {
+
+enum class OutMode : int { kBf16 = 0, kF32 = 1, kF32Accumulate = 2 };
+
+struct GemmArgs {
+  const void* A;   // bf16; [M][lda] if !a_mn (K-major), [K][lda] if a_mn (M-major)
+  const void* B;   // bf16; [N][ldb] if !b_mn (K-major), [K][ldb] if b_mn (N-major)
+  void* C;         // [M][ldc], bf16 or fp32 per `out`
+  long lda, ldb, ldc;  // row strides in elements
+  int M, N, K;
+  bool a_mn, b_mn;
+  OutMode out;
+  int* err;        // device error word (may be null)
+  int num_sms;
+};
+
+cudaError_t gemm_bf16(const GemmArgs& args, cudaStream_t stream);
+
+// 2-D bf16 TMA descriptor with 128-byte swizzle; `inner` is the contiguous dim.
+bool make_tmap_bf16_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint64_t row_stride_elems,
+                       uint32_t box_inner, uint32_t box_outer);
+
+}  // namespace nmb

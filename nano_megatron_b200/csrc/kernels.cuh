@@ -1,0 +1,50 @@
+// Host interfaces of the memory-bound kernels (kernels.cu): RMSNorm, SwiGLU,
+// RoPE, vocab-parallel embedding, cross-entropy statistics and gradient,
+// AdamW over a flat buffer, weighted squared norm.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+namespace nmb {
+
+// dtype tags: 0 = fp32, 1 = bf16
+cudaError_t rmsnorm_fwd(const void* x, const float* w, void* y, float* rstd, int rows, int cols, float eps,
+                        int dtype, cudaStream_t s);
+// dx and per-block weight-gradient partials ([partial_rows, cols] fp32, partial_rows = rmsnorm_bwd_blocks()).
+cudaError_t rmsnorm_bwd(const void* dy, const void* x, const float* w, const float* rstd, void* dx,
+                        float* dw_partial, int rows, int cols, int dtype, cudaStream_t s);
+int rmsnorm_bwd_blocks(int rows);
+// out[c] += sum_b partial[b, c]
+cudaError_t reduce_rows_add(const float* partial, float* out, int nrows, int cols, cudaStream_t s);
+
+cudaError_t swiglu_fwd(const void* gu, void* a, long rows, int ffn, int dtype, cudaStream_t s);
+cudaError_t swiglu_bwd(const void* da, const void* gu, void* dgu, long rows, int ffn, int dtype, cudaStream_t s);
+
+// In-place NeoX rotation of the q and k sections of qkv [rows, 3*heads*hd];
+// position = row / batch; sign = +1 forward, -1 inverse.
+cudaError_t rope_inplace(void* qkv, const float* cos, const float* sin, long rows, int batch, int heads, int hd,
+                         float sign, int dtype, cudaStream_t s);
+
+cudaError_t embedding_fwd(const int64_t* ids, const float* w, void* out, long rows, int hidden, long vstart,
+                          long vend, long vocab, int out_dtype, int* err, cudaStream_t s);
+cudaError_t embedding_bwd(const void* dy, const int64_t* ids, float* wgrad, long rows, int hidden, long vstart,
+                          long vend, int dtype, cudaStream_t s);
+
+cudaError_t ce_stats(const void* logits, const int64_t* target, float* mx, float* se, float* tl, long rows, int vl,
+                     long ld, long vstart, int dtype, cudaStream_t s);
+cudaError_t ce_grad(const void* logits, const int64_t* target, const float* gmax, const float* gsum,
+                    const float* gscale, float inv_n, void* dlogits, long rows, int vl, long ld, long vstart,
+                    int dtype, cudaStream_t s);
+
+cudaError_t adamw_flat(float* p, const float* g, float* m, float* v, __nv_bfloat16* compute, const float* scale,
+                       long n, float lr, float beta1, float beta2, float eps, float wd, float bc1, float bc2_sqrt,
+                       cudaStream_t s);
+
+// out += sum_i weight[i] * ||seg_i||^2 (fp32 segments, fp64 result)
+cudaError_t weighted_sq_norm(const int64_t* ptrs, const int64_t* numels, const double* weights, int nseg,
+                             double* out, cudaStream_t s);
+
+}  // namespace nmb

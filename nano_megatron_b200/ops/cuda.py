@@ -1,0 +1,243 @@
+"""CUDA implementations of the op layer, on the in-tree sm_100a extension.
+
+Importing this module loads ``nano_megatron_b200/_C*.so`` and raises if it is
+missing or was not built for this GPU: there is no silent fallback to
+PyTorch kernels on the CUDA path.
+
+GEMMs run the tcgen05 kernel of ``csrc/gemm.cu`` in bf16. fp32 GEMMs (the
+reference's ``--dtype float32`` path) run the exact-fp32 SIMT kernel of
+``csrc/attention.cu``'s companion (``gemm_f32``) when built; bf16 is the
+performance path.
+"""
+
+from __future__ import annotations
+
+import torch
+
+try:
+    from .. import _C  # noqa: F401
+except ImportError as exc:  # pragma: no cover - exercised only without a build
+    raise ImportError(
+        "nano_megatron_b200._C is not built; run `python setup.py build_ext --inplace` "
+        "(or __graft_entry__.build()) before using CUDA tensors") from exc
+
+from .. import _C as C  # noqa: E402
+
+_status: dict[int, torch.Tensor] = {}
+_partial_cache: dict[tuple, torch.Tensor] = {}
+
+ERROR_MESSAGES = {1: "an mbarrier wait timed out inside a kernel",
+                  2: "a cross-GPU flag wait timed out",
+                  3: "a token id is outside the vocabulary",
+                  4: "a kernel was launched with an unsupported shape"}
+
+
+def status_word(device: torch.device) -> torch.Tensor:
+    """The device's int32 error word that bounded waits and bounds checks write."""
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    t = _status.get(idx)
+    if t is None:
+        t = torch.zeros(4, dtype=torch.int32, device=torch.device("cuda", idx))
+        _status[idx] = t
+    return t
+
+
+def check_status(device: torch.device | None = None) -> None:
+    """Raise if any kernel on ``device`` reported an error since the last check (syncs)."""
+    device = device or torch.device("cuda", torch.cuda.current_device())
+    word = status_word(device)
+    code = int(word[0].item())
+    if code:
+        word.zero_()
+        raise RuntimeError(f"CUDA kernel error {code}: {ERROR_MESSAGES.get(code, 'unknown')}")
+
+
+def _dtype_ok(t: torch.Tensor) -> None:
+    if t.dtype not in (torch.bfloat16, torch.float32):
+        raise TypeError(f"unsupported dtype {t.dtype}")
+
+
+# --------------------------------------------------------------------- GEMM
+def _gemm(a, b, c, a_mn, b_mn, out_mode):
+    C.gemm(a, b, c, a_mn, b_mn, out_mode, status_word(a.device))
+
+
+def _f32_gemm(a, b, a_t, b_t):
+    """Exact fp32 product via the SIMT fp32 GEMM kernel."""
+    return C.gemm_f32(a, b, a_t, b_t)
+
+
+def mm_nn(a, b):
+    """``a[M,K] @ b[K,N]``."""
+    if a.dtype == torch.float32:
+        return _f32_gemm(a, b, False, False)
+    out = torch.empty((a.shape[0], b.shape[1]), dtype=a.dtype, device=a.device)
+    _gemm(a, b, out, False, True, 0)
+    return out
+
+
+def mm_nt(a, b):
+    """``a[M,K] @ b[N,K]^T``."""
+    if a.dtype == torch.float32:
+        return _f32_gemm(a, b, False, True)
+    out = torch.empty((a.shape[0], b.shape[0]), dtype=a.dtype, device=a.device)
+    _gemm(a, b, out, False, False, 0)
+    return out
+
+
+def mm_tn_acc(a, b, out):
+    """``out[K,N] += a[M,K]^T @ b[M,N]`` (fp32 ``out``)."""
+    if a.dtype == torch.float32:
+        out.add_(_f32_gemm(a, b, True, False))
+        return
+    if out.stride(-1) != 1:
+        raise ValueError("accumulator must have unit inner stride")
+    _gemm(a, b, out, True, True, 2)
+
+
+# ------------------------------------------------------------------ RMSNorm
+def rmsnorm(x, weight, eps):
+    _dtype_ok(x)
+    x = x.contiguous()
+    y = torch.empty_like(x)
+    rstd = torch.empty(x.shape[0], dtype=torch.float32, device=x.device)
+    C.rmsnorm_fwd(x, weight.contiguous().float(), y, rstd, float(eps))
+    return y, rstd
+
+
+def _partial(device, rows, cols):
+    key = (device.index, rows, cols)
+    buf = _partial_cache.get(key)
+    if buf is None:
+        buf = torch.empty((rows, cols), dtype=torch.float32, device=device)
+        _partial_cache[key] = buf
+    return buf
+
+
+def rmsnorm_bwd(dy, x, weight, rstd, wgrad_out):
+    dx = torch.empty_like(x)
+    nblk = C.rmsnorm_bwd_blocks(x.shape[0])
+    part = _partial(x.device, nblk, x.shape[1])
+    C.rmsnorm_bwd(dy.contiguous(), x, weight.contiguous().float(), rstd, dx, part)
+    if wgrad_out is not None:
+        C.reduce_rows_add(part, nblk, wgrad_out)
+        return dx, None
+    dw = torch.zeros(x.shape[1], dtype=torch.float32, device=x.device)
+    C.reduce_rows_add(part, nblk, dw)
+    return dx, dw
+
+
+# ---------------------------------------------------------------- attention
+def attention(qkv, batch, heads, head_dim, cos, sin):
+    """RoPE (in place on a copy of q/k) + causal flash attention."""
+    qkv = qkv.contiguous()
+    C.rope_inplace(qkv, cos, sin, batch, heads, head_dim, 1.0)
+    o, lse = C.flash_attn_fwd(qkv, batch, heads, head_dim)
+    return o, (qkv, o, lse)
+
+
+def attention_bwd(do, saved, batch, heads, head_dim, cos, sin):
+    qkv, o, lse = saved
+    dqkv = C.flash_attn_bwd(do.contiguous(), qkv, o, lse, batch, heads, head_dim)
+    C.rope_inplace(dqkv, cos, sin, batch, heads, head_dim, -1.0)
+    return dqkv
+
+
+# ------------------------------------------------------------------- SwiGLU
+def swiglu(gu):
+    a = torch.empty((gu.shape[0], gu.shape[1] // 2), dtype=gu.dtype, device=gu.device)
+    C.swiglu_fwd(gu.contiguous(), a)
+    return a
+
+
+def swiglu_bwd(da, gu):
+    dgu = torch.empty_like(gu)
+    C.swiglu_bwd(da.contiguous(), gu.contiguous(), dgu)
+    return dgu
+
+
+# ---------------------------------------------------------------- embedding
+def embedding(ids, weight, vocab_start, vocab_end, out_dtype=None, vocab_size=None):
+    ids = ids.contiguous()
+    out = torch.empty((ids.numel(), weight.shape[1]), dtype=out_dtype or weight.dtype, device=weight.device)
+    vocab = vocab_size if vocab_size is not None else 1 << 62
+    C.embedding_fwd(ids, weight.contiguous(), out, vocab_start, vocab_end, vocab, status_word(weight.device))
+    return out
+
+
+def embedding_bwd(dy, ids, wgrad_out, vocab_start, vocab_end):
+    C.embedding_bwd(dy.contiguous(), ids.contiguous(), wgrad_out, vocab_start, vocab_end)
+
+
+# ------------------------------------------------------------ cross entropy
+def ce_local_stats(logits, target, vocab_start, vocab_end):
+    n = logits.shape[0]
+    mx = torch.empty(n, dtype=torch.float32, device=logits.device)
+    se = torch.empty_like(mx)
+    tl = torch.empty_like(mx)
+    C.ce_stats(logits, target.contiguous(), mx, se, tl, vocab_start)
+    owned = (target >= vocab_start) & (target < vocab_end)
+    return mx, se, tl, owned
+
+
+def ce_grad(logits, target, vocab_start, gmax, gsum, scale, out_dtype):
+    """``scale`` may be a per-row tensor (generic path) or a device scalar."""
+    d = torch.empty(logits.shape, dtype=logits.dtype, device=logits.device)
+    if scale.numel() == 1:
+        C.ce_grad(logits, target.contiguous(), gmax, gsum, scale.float().reshape(1), 1.0, d, vocab_start)
+        return d if d.dtype == out_dtype else d.to(out_dtype)
+    C.ce_grad(logits, target.contiguous(), gmax, gsum, torch.ones(1, device=logits.device), 1.0, d,
+              vocab_start)
+    d = d * scale.unsqueeze(-1).to(d.dtype)
+    return d if d.dtype == out_dtype else d.to(out_dtype)
+
+
+def lm_head_ce_fwd(X, w, labels, vocab_start, vocab_end, pctx):
+    """LM-head logits + per-token loss. Returns ``(loss [T], state)``."""
+    from ..models.functional import merge_ce_stats
+    logits = mm_nt(X, w)
+    mx, se, tl, _ = ce_local_stats(logits, labels, vocab_start, vocab_end)
+    gm, gs, gt = merge_ce_stats(mx, se, tl, pctx)
+    loss = gs.log() + gm - gt
+    return loss, (logits, gm, gs)
+
+
+def lm_head_ce_grad(X, w, labels, vocab_start, state, g_over_n):
+    logits, gm, gs = state
+    d = torch.empty_like(logits)
+    C.ce_grad(logits, labels.contiguous(), gm, gs, g_over_n.float().reshape(1), 1.0, d, vocab_start)
+    return d
+
+
+# -------------------------------------------------------------- optimizer
+def adamw_flat(p, g, m, v, compute, scale, *, lr, beta1, beta2, eps, weight_decay, step):
+    C.adamw_flat(p, g, m, v, compute, scale.reshape(1), lr, beta1, beta2, eps, weight_decay, step)
+
+
+_norm_tables: dict[tuple, tuple] = {}
+_CHUNK = 1 << 24
+
+
+def weighted_sq_norm(tensors, weights):
+    """``sum_i w_i * ||t_i||^2`` in fp64 (fp32 tensors, any strides of views into one buffer)."""
+    device = tensors[0].device
+    key = tuple((t.data_ptr(), t.numel(), w) for t, w in zip(tensors, weights))
+    table = _norm_tables.get(key)
+    if table is None:
+        ptrs, numels, ws = [], [], []
+        # Views of the flat buffer may be column slices; merge by storage span.
+        for t, w in zip(tensors, weights):
+            if not t.is_contiguous():
+                raise ValueError("norm segments must be contiguous")
+            base, n = t.data_ptr(), t.numel()
+            for off in range(0, n, _CHUNK):
+                ptrs.append(base + off * 4)
+                numels.append(min(_CHUNK, n - off))
+                ws.append(w)
+        table = (torch.tensor(ptrs, dtype=torch.int64, device=device),
+                 torch.tensor(numels, dtype=torch.int64, device=device),
+                 torch.tensor(ws, dtype=torch.float64, device=device))
+        _norm_tables[key] = table
+    out = torch.zeros((), dtype=torch.float64, device=device)
+    C.weighted_sq_norm(*table, out)
+    return out

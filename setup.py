@@ -1,0 +1,46 @@
+"""Build the sm_100a CUDA extension in place:
+
+    python setup.py build_ext --inplace
+
+produces ``nano_megatron_b200/_C*.so`` next to the Python sources, so it
+travels with the repository (no JIT cache). Only sm_100a code is generated.
+"""
+
+import os
+
+from setuptools import setup
+from torch.utils.cpp_extension import BuildExtension, CUDAExtension
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+CSRC = os.path.join("nano_megatron_b200", "csrc")
+
+SOURCES = [
+    "bindings.cpp",
+    "elementwise_bindings.cpp",
+    "gemm.cu",
+    "kernels.cu",
+]
+
+NVCC_FLAGS = [
+    "-O3",
+    "-std=c++17",
+    "-gencode", "arch=compute_100a,code=sm_100a",
+    "-lineinfo",
+    "--expt-relaxed-constexpr",
+    "-Xptxas=-warn-spills",
+]
+
+setup(
+    name="nano_megatron_b200",
+    version="0.1.0",
+    packages=["nano_megatron_b200"],
+    ext_modules=[
+        CUDAExtension(
+            name="nano_megatron_b200._C",
+            sources=[os.path.join(CSRC, s) for s in SOURCES],
+            include_dirs=[os.path.join(HERE, CSRC)],
+            extra_compile_args={"cxx": ["-O3", "-std=c++17"], "nvcc": NVCC_FLAGS},
+        )
+    ],
+    cmdclass={"build_ext": BuildExtension.with_options(use_ninja=True)},
+)

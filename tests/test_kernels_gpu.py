@@ -1,0 +1,182 @@
+"""sm_100a kernels against plain-PyTorch fp32 references of the same op.
+
+Each test builds inputs on the GPU, runs our kernel through the op layer and
+compares with the fp32 torch computation of the same math (inputs rounded to
+the kernel's storage dtype first). Shapes include partial tiles.
+"""
+
+import math
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+if not torch.cuda.is_available():  # pragma: no cover
+    pytest.skip("needs a CUDA GPU", allow_module_level=True)
+
+from nano_megatron_b200.ops import cuda as KC  # noqa: E402
+from nano_megatron_b200.ops import reference as R  # noqa: E402
+
+DEV = torch.device("cuda", 0)
+
+
+def _rel(a, b):
+    return ((a.float() - b.float()).norm() / b.float().norm().clamp_min(1e-12)).item()
+
+
+@pytest.mark.parametrize("M,N,K", [(128, 256, 64), (512, 768, 1024), (300, 264, 200), (2048, 3072, 4096),
+                                   (8, 8, 8), (1000, 1032, 72)])
+def test_gemm_nn(M, N, K):
+    torch.manual_seed(0)
+    a = torch.randn(M, K, device=DEV).bfloat16()
+    b = torch.randn(K, N, device=DEV).bfloat16()
+    got = KC.mm_nn(a, b)
+    ref = a.float() @ b.float()
+    assert got.shape == (M, N) and got.dtype == torch.bfloat16
+    assert _rel(got, ref) < 5e-3, _rel(got, ref)
+
+
+@pytest.mark.parametrize("M,N,K", [(128, 256, 64), (512, 768, 1024), (300, 264, 200), (4096, 4096, 1024)])
+def test_gemm_nt(M, N, K):
+    torch.manual_seed(1)
+    a = torch.randn(M, K, device=DEV).bfloat16()
+    b = torch.randn(N, K, device=DEV).bfloat16()
+    got = KC.mm_nt(a, b)
+    ref = a.float() @ b.float().t()
+    assert _rel(got, ref) < 5e-3
+
+
+@pytest.mark.parametrize("M,N,K", [(128, 256, 64), (512, 768, 1024), (264, 392, 200), (4096, 1024, 2048)])
+def test_gemm_tn_accumulate(M, N, K):
+    """out[K,N] += a[M,K]^T b[M,N] in fp32 (weight-gradient accumulation)."""
+    torch.manual_seed(2)
+    a = torch.randn(M, K, device=DEV).bfloat16()
+    b = torch.randn(M, N, device=DEV).bfloat16()
+    out = torch.randn(K, N, device=DEV)
+    start = out.clone()
+    KC.mm_tn_acc(a, b, out)
+    ref = start + a.float().t() @ b.float()
+    assert _rel(out, ref) < 1e-5 * math.sqrt(M) + 1e-6
+    KC.mm_tn_acc(a, b, out)  # accumulates again
+    assert _rel(out, ref + a.float().t() @ b.float()) < 1e-4
+
+
+def test_gemm_strided_column_slice_accumulate():
+    """Accumulating into a column slice of a wider fp32 buffer (fused q|k|v grads)."""
+    torch.manual_seed(3)
+    a = torch.randn(256, 128, device=DEV).bfloat16()
+    b = torch.randn(256, 64, device=DEV).bfloat16()
+    big = torch.zeros(128, 192, device=DEV)
+    KC.mm_tn_acc(a, b, big[:, 64:128])
+    ref = a.float().t() @ b.float()
+    assert _rel(big[:, 64:128], ref) < 1e-5
+    assert big[:, :64].abs().max() == 0 and big[:, 128:].abs().max() == 0
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("rows,cols", [(1000, 256), (4096, 4096), (77, 2560)])
+def test_rmsnorm(dtype, rows, cols):
+    torch.manual_seed(4)
+    x = torch.randn(rows, cols, device=DEV).to(dtype)
+    w = torch.rand(cols, device=DEV) + 0.5
+    y, rstd = KC.rmsnorm(x, w, 1e-6)
+    yr, rr = R.rmsnorm(x, w, 1e-6)
+    tol = 1e-2 if dtype == torch.bfloat16 else 1e-5
+    assert _rel(y, yr) < tol and _rel(rstd, rr) < 1e-5
+    dy = torch.randn_like(x)
+    wg = torch.zeros(cols, device=DEV)
+    dx, _ = KC.rmsnorm_bwd(dy, x, w, rstd, wg)
+    wr = torch.zeros(cols, device=DEV)
+    dxr, _ = R.rmsnorm_bwd(dy, x, w, rr, wr)
+    assert _rel(dx, dxr) < tol and _rel(wg, wr) < (1e-2 if dtype == torch.bfloat16 else 1e-5)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_swiglu(dtype):
+    torch.manual_seed(5)
+    gu = torch.randn(333, 2 * 344, device=DEV).to(dtype)
+    a = KC.swiglu(gu)
+    assert _rel(a, R.swiglu(gu.float())) < (1e-2 if dtype == torch.bfloat16 else 1e-6)
+    da = torch.randn(333, 344, device=DEV).to(dtype)
+    d = KC.swiglu_bwd(da, gu)
+    assert _rel(d, R.swiglu_bwd(da.float(), gu.float())) < (1e-2 if dtype == torch.bfloat16 else 1e-5)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_rope_roundtrip(dtype):
+    from nano_megatron_b200 import _C
+    torch.manual_seed(6)
+    S, b, h, d = 64, 2, 4, 128
+    cos, sin = R.rope_cache(S, d, 500000.0, DEV)
+    qkv = torch.randn(S * b, 3 * h * d, device=DEV).to(dtype)
+    x = qkv.clone()
+    _C.rope_inplace(x, cos, sin, b, h, d, 1.0)
+    q, k, v = R.split_qkv(qkv.float(), b, h, d)
+    ref = torch.stack([R._rotate(q, cos, sin, 1.0), R._rotate(k, cos, sin, 1.0), v], dim=2).reshape(qkv.shape)
+    assert _rel(x, ref) < (1e-2 if dtype == torch.bfloat16 else 1e-6)
+    _C.rope_inplace(x, cos, sin, b, h, d, -1.0)
+    assert _rel(x, qkv) < (2e-2 if dtype == torch.bfloat16 else 1e-6)
+
+
+def test_embedding_and_bounds_flag():
+    torch.manual_seed(7)
+    V, H = 1000, 256
+    w = torch.randn(V // 2, H, device=DEV)
+    ids = torch.randint(0, V, (517,), device=DEV)
+    out = KC.embedding(ids, w, 500, 1000, torch.bfloat16, V)
+    ref = R.embedding(ids, w, 500, 1000)
+    assert _rel(out, ref) < 1e-2
+    dy = torch.randn(517, H, device=DEV)
+    g = torch.zeros_like(w)
+    KC.embedding_bwd(dy, ids, g, 500, 1000)
+    gr = torch.zeros_like(w)
+    R.embedding_bwd(dy, ids, gr, 500, 1000)
+    assert _rel(g, gr) < 1e-6
+    KC.check_status(DEV)
+    bad = ids.clone()
+    bad[3] = V + 5
+    KC.embedding(bad, w, 500, 1000, torch.bfloat16, V)
+    with pytest.raises(RuntimeError, match="vocabulary"):
+        KC.check_status(DEV)
+
+
+def test_cross_entropy_stats_and_grad():
+    torch.manual_seed(8)
+    T, V, start = 300, 1032, 1032
+    logits = (torch.randn(T, V, device=DEV) * 3).bfloat16()
+    target = torch.randint(0, 3 * V, (T,), device=DEV)
+    mx, se, tl, owned = KC.ce_local_stats(logits, target, start, start + V)
+    rm, rs, rt, ro = R.ce_local_stats(logits.float(), target, start, start + V)
+    assert _rel(mx, rm) < 1e-6 and _rel(se, rs) < 1e-5 and _rel(tl, rt) < 1e-6
+    gm, gs = rm + 0.5, rs * 2
+    scale = torch.tensor(0.37, device=DEV)
+    d = KC.ce_grad(logits, target, start, gm, gs, scale, torch.bfloat16)
+    dr = R.ce_grad(logits.float(), target, start, gm, gs, scale.expand(T), torch.float32)
+    assert _rel(d, dr) < 1e-2
+
+
+def test_adamw_flat_matches_reference():
+    torch.manual_seed(9)
+    n = 4096 + 64
+    p = torch.randn(n, device=DEV)
+    g = torch.randn(n, device=DEV)
+    m = torch.zeros(n, device=DEV)
+    v = torch.zeros(n, device=DEV)
+    comp = torch.empty(n, device=DEV, dtype=torch.bfloat16)
+    pr, mr, vr = p.clone(), m.clone(), v.clone()
+    for step in (1, 2, 3):
+        KC.adamw_flat(p, g, m, v, comp, torch.tensor(0.5, device=DEV), lr=1e-2, beta1=0.9, beta2=0.999,
+                     eps=1e-8, weight_decay=0.01, step=step)
+        R.adamw_(pr, g * 0.5, mr, vr, lr=1e-2, beta1=0.9, beta2=0.999, eps=1e-8, weight_decay=0.01, step=step)
+    assert _rel(p, pr) < 1e-6 and _rel(m, mr) < 1e-6 and _rel(v, vr) < 1e-6
+    assert torch.equal(comp, p.bfloat16())
+
+
+def test_weighted_sq_norm():
+    torch.manual_seed(10)
+    ts = [torch.randn(n, device=DEV) for n in (100, 5000, (1 << 24) + 17)]
+    ws = [1.0, 0.5, 0.25]
+    got = KC.weighted_sq_norm(ts, ws)
+    ref = sum(w * t.double().pow(2).sum() for t, w in zip(ts, ws))
+    assert abs(got.item() - ref.item()) / ref.item() < 1e-6
