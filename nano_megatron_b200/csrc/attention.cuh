@@ -1,0 +1,19 @@
+// Host interface of the causal flash-attention kernels (attention.cu).
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+namespace nmb {
+
+// qkv [S*batch, 3*heads*hd] -> out [S*batch, heads*hd], lse [batch*heads, S]
+cudaError_t flash_attn_fwd(const __nv_bfloat16* qkv, __nv_bfloat16* out, float* lse, int S, int batch, int heads,
+                           int head_dim, cudaStream_t stream);
+
+// dqkv [S*batch, 3*heads*hd] (every element written); dvec [batch*heads*S] and
+// dq_acc [batch*heads*S*hd] fp32 are scratch.
+cudaError_t flash_attn_bwd(const __nv_bfloat16* dout, const __nv_bfloat16* qkv, const __nv_bfloat16* out,
+                           const float* lse, float* dvec, float* dq_acc, __nv_bfloat16* dqkv, int S, int batch,
+                           int heads, int head_dim, cudaStream_t stream);
+
+}  // namespace nmb

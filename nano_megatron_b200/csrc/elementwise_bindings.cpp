@@ -4,6 +4,7 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
 
+#include "attention.cuh"
 #include "kernels.cuh"
 
 namespace {
@@ -130,8 +131,7 @@ void adamw_flat(at::Tensor& p, const at::Tensor& g, at::Tensor& m, at::Tensor& v
   const double bc1 = 1.0 - std::pow(beta1, (double)step);
   const double bc2 = 1.0 - std::pow(beta2, (double)step);
   ok(nmb::adamw_flat(p.data_ptr<float>(), g.data_ptr<float>(), m.data_ptr<float>(), v.data_ptr<float>(), c,
-                     scale.data_ptr<float>(), p.numel(), (float)lr, (float)beta1, (float)beta2, (float)eps, (float)wd,
-                     (float)bc1, (float)std::sqrt(bc2), stream()),
+                     scale.data_ptr<float>(), p.numel(), lr, beta1, beta2, eps, wd, bc1, std::sqrt(bc2), stream()),
      "adamw_flat");
 }
 
@@ -141,6 +141,39 @@ void weighted_sq_norm(const at::Tensor& ptrs, const at::Tensor& numels, const at
   ok(nmb::weighted_sq_norm(ptrs.data_ptr<int64_t>(), numels.data_ptr<int64_t>(), weights.data_ptr<double>(),
                            ptrs.numel(), out.data_ptr<double>(), stream()),
      "weighted_sq_norm");
+}
+
+std::vector<at::Tensor> flash_attn_fwd(const at::Tensor& qkv, int64_t batch, int64_t heads, int64_t hd) {
+  need(qkv, "qkv");
+  TORCH_CHECK(qkv.scalar_type() == at::kBFloat16, "flash attention runs in bf16");
+  TORCH_CHECK(qkv.size(1) == 3 * heads * hd && qkv.size(0) % batch == 0, "qkv shape");
+  const int S = qkv.size(0) / batch;
+  auto out = at::empty({qkv.size(0), heads * hd}, qkv.options());
+  auto lse = at::empty({batch * heads, S}, qkv.options().dtype(at::kFloat));
+  const at::cuda::CUDAGuard g(qkv.device());
+  ok(nmb::flash_attn_fwd(reinterpret_cast<const __nv_bfloat16*>(qkv.data_ptr()),
+                         reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), lse.data_ptr<float>(), S, batch, heads, hd,
+                         stream()),
+     "flash_attn_fwd");
+  return {out, lse};
+}
+
+at::Tensor flash_attn_bwd(const at::Tensor& dout, const at::Tensor& qkv, const at::Tensor& out, const at::Tensor& lse,
+                          int64_t batch, int64_t heads, int64_t hd) {
+  need(dout, "dout"); need(qkv, "qkv"); need(out, "out"); need(lse, "lse");
+  TORCH_CHECK(dout.scalar_type() == at::kBFloat16 && qkv.scalar_type() == at::kBFloat16, "bf16 only");
+  const int S = qkv.size(0) / batch;
+  auto dqkv = at::empty_like(qkv);
+  auto dvec = at::empty({batch * heads * S}, qkv.options().dtype(at::kFloat));
+  auto dq_acc = at::empty({batch * heads * S * hd}, qkv.options().dtype(at::kFloat));
+  const at::cuda::CUDAGuard g(qkv.device());
+  ok(nmb::flash_attn_bwd(reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr()),
+                         reinterpret_cast<const __nv_bfloat16*>(qkv.data_ptr()),
+                         reinterpret_cast<const __nv_bfloat16*>(out.data_ptr()), lse.data_ptr<float>(),
+                         dvec.data_ptr<float>(), dq_acc.data_ptr<float>(),
+                         reinterpret_cast<__nv_bfloat16*>(dqkv.data_ptr()), S, batch, heads, hd, stream()),
+     "flash_attn_bwd");
+  return dqkv;
 }
 
 }  // namespace
@@ -160,4 +193,6 @@ void register_elementwise(pybind11::module& m) {
   m.def("ce_grad", &ce_grad);
   m.def("adamw_flat", &adamw_flat);
   m.def("weighted_sq_norm", &weighted_sq_norm);
+  m.def("flash_attn_fwd", &flash_attn_fwd);
+  m.def("flash_attn_bwd", &flash_attn_bwd);
 }

@@ -104,7 +104,6 @@ __global__ void rmsnorm_fwd_kernel(const T* __restrict__ x, const float* __restr
 }
 
 constexpr int NORM_BWD_THREADS = 256;
-constexpr int NORM_MAX_CHUNKS = 16;  // cols <= 16 * 256 = 4096 kept in registers
 
 template <typename T, int CHUNKS>
 __global__ void __launch_bounds__(NORM_BWD_THREADS)
@@ -377,11 +376,9 @@ __global__ void ce_grad_kernel(const T* __restrict__ logits, const int64_t* __re
 // -------------------------------------------------------------------- AdamW
 __global__ void adamw_kernel(float4* __restrict__ p, const float4* __restrict__ g, float4* __restrict__ m,
                              float4* __restrict__ v, uint2* __restrict__ compute, const float* __restrict__ scale_ptr,
-                             long n4, float lr, float beta1, float beta2, float eps, float wd, float bc1,
-                             float bc2_sqrt) {
+                             long n4, float one_minus_b1, float beta2, float one_minus_b2, float eps, float decay,
+                             float step, float bc2_sqrt) {
   const float scale = scale_ptr[0];
-  const float decay = 1.f - lr * wd;
-  const float step = lr / bc1;
   for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n4; i += (long)gridDim.x * blockDim.x) {
     float4 pp = p[i], gg = g[i], mm = m[i], vv = v[i];
     float* pf = &pp.x; float* gf = &gg.x; float* mf = &mm.x; float* vf = &vv.x;
@@ -389,8 +386,8 @@ __global__ void adamw_kernel(float4* __restrict__ p, const float4* __restrict__ 
     for (int k = 0; k < 4; ++k) {
       const float gk = gf[k] * scale;
       pf[k] *= decay;
-      mf[k] += (gk - mf[k]) * (1.f - beta1);
-      vf[k] = vf[k] * beta2 + (1.f - beta2) * gk * gk;
+      mf[k] += (gk - mf[k]) * one_minus_b1;
+      vf[k] = vf[k] * beta2 + one_minus_b2 * gk * gk;
       const float denom = sqrtf(vf[k]) / bc2_sqrt + eps;
       pf[k] -= step * (mf[k] / denom);
     }
@@ -577,14 +574,14 @@ cudaError_t ce_grad(const void* logits, const int64_t* target, const float* gmax
 }
 
 cudaError_t adamw_flat(float* p, const float* g, float* m, float* v, __nv_bfloat16* compute, const float* scale, long n,
-                       float lr, float beta1, float beta2, float eps, float wd, float bc1, float bc2_sqrt,
+                       double lr, double beta1, double beta2, double eps, double wd, double bc1, double bc2_sqrt,
                        cudaStream_t s) {
   if (n % 4) return cudaErrorInvalidValue;
   const long n4 = n / 4;
   adamw_kernel<<<grid_for(n4, 256, 148 * 8), 256, 0, s>>>(
       reinterpret_cast<float4*>(p), reinterpret_cast<const float4*>(g), reinterpret_cast<float4*>(m),
-      reinterpret_cast<float4*>(v), reinterpret_cast<uint2*>(compute), scale, n4, lr, beta1, beta2, eps, wd, bc1,
-      bc2_sqrt);
+      reinterpret_cast<float4*>(v), reinterpret_cast<uint2*>(compute), scale, n4, (float)(1.0 - beta1), (float)beta2,
+      (float)(1.0 - beta2), (float)eps, (float)(1.0 - lr * wd), (float)(lr / bc1), (float)bc2_sqrt);
   return cudaGetLastError();
 }
 

@@ -40,7 +40,7 @@ cudaError_t ce_grad(const void* logits, const int64_t* target, const float* gmax
                     int dtype, cudaStream_t s);
 
 cudaError_t adamw_flat(float* p, const float* g, float* m, float* v, __nv_bfloat16* compute, const float* scale,
-                       long n, float lr, float beta1, float beta2, float eps, float wd, float bc1, float bc2_sqrt,
+                       long n, double lr, double beta1, double beta2, double eps, double wd, double bc1, double bc2_sqrt,
                        cudaStream_t s);
 
 // out += sum_i weight[i] * ||seg_i||^2 (fp32 segments, fp64 result)

@@ -193,7 +193,10 @@ def rms_norm(x, weight, eps):
 class _Attention(torch.autograd.Function):
     @staticmethod
     def forward(ctx, qkv, batch, heads, head_dim, cos, sin):
-        o, saved = ops.attention(qkv.contiguous(), batch, heads, head_dim, cos, sin)
+        if qkv.is_cuda:  # the QKV GEMM output is private to this op: rotate it in place
+            o, saved = ops.cuda_ops().attention(qkv, batch, heads, head_dim, cos, sin, inplace=True)
+        else:
+            o, saved = ops.attention(qkv.contiguous(), batch, heads, head_dim, cos, sin)
         ctx.save_for_backward(*saved)
         ctx.meta = (batch, heads, head_dim)
         ctx.rope = (cos, sin)
@@ -233,9 +236,11 @@ def swiglu(gu):
 class _Embedding(torch.autograd.Function):
     @staticmethod
     def forward(ctx, ids, wref, pctx, mode, vocab_start, vocab_end, out_dtype, *params):
-        y = ops.embedding(ids, wref.data.detach(), vocab_start, vocab_end)
-        if y.dtype != out_dtype and y.is_cuda:
-            y = y.to(out_dtype)
+        if ids.is_cuda:
+            vocab = (vocab_end - vocab_start) * pctx.tp_size
+            y = ops.cuda_ops().embedding(ids, wref.data.detach(), vocab_start, vocab_end, out_dtype, vocab)
+        else:
+            y = ops.embedding(ids, wref.data.detach(), vocab_start, vocab_end)
         if pctx.tp_size > 1:
             y = _rs(y, pctx) if mode == "rs" else _ar(y, pctx)
         ctx.save_for_backward(ids)

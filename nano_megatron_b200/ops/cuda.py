@@ -24,6 +24,16 @@ except ImportError as exc:  # pragma: no cover - exercised only without a build
 from .. import _C as C  # noqa: E402
 
 _status: dict[int, torch.Tensor] = {}
+
+# Number of our kernels launched so far (benchmarks read the difference
+# around a timed region; each wrapper adds the kernels it launches).
+LAUNCHES = [0]
+
+
+def _count(n: int = 1) -> None:
+    LAUNCHES[0] += n
+
+
 _partial_cache: dict[tuple, torch.Tensor] = {}
 
 ERROR_MESSAGES = {1: "an mbarrier wait timed out inside a kernel",
@@ -60,6 +70,7 @@ def _dtype_ok(t: torch.Tensor) -> None:
 # --------------------------------------------------------------------- GEMM
 def _gemm(a, b, c, a_mn, b_mn, out_mode):
     C.gemm(a, b, c, a_mn, b_mn, out_mode, status_word(a.device))
+    _count()
 
 
 def _f32_gemm(a, b, a_t, b_t):
@@ -102,6 +113,7 @@ def rmsnorm(x, weight, eps):
     y = torch.empty_like(x)
     rstd = torch.empty(x.shape[0], dtype=torch.float32, device=x.device)
     C.rmsnorm_fwd(x, weight.contiguous().float(), y, rstd, float(eps))
+    _count()
     return y, rstd
 
 
@@ -119,6 +131,7 @@ def rmsnorm_bwd(dy, x, weight, rstd, wgrad_out):
     nblk = C.rmsnorm_bwd_blocks(x.shape[0])
     part = _partial(x.device, nblk, x.shape[1])
     C.rmsnorm_bwd(dy.contiguous(), x, weight.contiguous().float(), rstd, dx, part)
+    _count(2)
     if wgrad_out is not None:
         C.reduce_rows_add(part, nblk, wgrad_out)
         return dx, None
@@ -128,11 +141,13 @@ def rmsnorm_bwd(dy, x, weight, rstd, wgrad_out):
 
 
 # ---------------------------------------------------------------- attention
-def attention(qkv, batch, heads, head_dim, cos, sin):
-    """RoPE (in place on a copy of q/k) + causal flash attention."""
-    qkv = qkv.contiguous()
+def attention(qkv, batch, heads, head_dim, cos, sin, inplace=False):
+    """RoPE + causal flash attention. With ``inplace`` the rotation is applied
+    to ``qkv`` itself (the model passes its private QKV GEMM output)."""
+    qkv = qkv.contiguous() if inplace else qkv.clone(memory_format=torch.contiguous_format)
     C.rope_inplace(qkv, cos, sin, batch, heads, head_dim, 1.0)
     o, lse = C.flash_attn_fwd(qkv, batch, heads, head_dim)
+    _count(2)
     return o, (qkv, o, lse)
 
 
@@ -140,6 +155,7 @@ def attention_bwd(do, saved, batch, heads, head_dim, cos, sin):
     qkv, o, lse = saved
     dqkv = C.flash_attn_bwd(do.contiguous(), qkv, o, lse, batch, heads, head_dim)
     C.rope_inplace(dqkv, cos, sin, batch, heads, head_dim, -1.0)
+    _count(4)
     return dqkv
 
 
@@ -147,12 +163,14 @@ def attention_bwd(do, saved, batch, heads, head_dim, cos, sin):
 def swiglu(gu):
     a = torch.empty((gu.shape[0], gu.shape[1] // 2), dtype=gu.dtype, device=gu.device)
     C.swiglu_fwd(gu.contiguous(), a)
+    _count()
     return a
 
 
 def swiglu_bwd(da, gu):
     dgu = torch.empty_like(gu)
     C.swiglu_bwd(da.contiguous(), gu.contiguous(), dgu)
+    _count()
     return dgu
 
 
@@ -162,11 +180,13 @@ def embedding(ids, weight, vocab_start, vocab_end, out_dtype=None, vocab_size=No
     out = torch.empty((ids.numel(), weight.shape[1]), dtype=out_dtype or weight.dtype, device=weight.device)
     vocab = vocab_size if vocab_size is not None else 1 << 62
     C.embedding_fwd(ids, weight.contiguous(), out, vocab_start, vocab_end, vocab, status_word(weight.device))
+    _count()
     return out
 
 
 def embedding_bwd(dy, ids, wgrad_out, vocab_start, vocab_end):
     C.embedding_bwd(dy.contiguous(), ids.contiguous(), wgrad_out, vocab_start, vocab_end)
+    _count()
 
 
 # ------------------------------------------------------------ cross entropy
@@ -176,8 +196,8 @@ def ce_local_stats(logits, target, vocab_start, vocab_end):
     se = torch.empty_like(mx)
     tl = torch.empty_like(mx)
     C.ce_stats(logits, target.contiguous(), mx, se, tl, vocab_start)
-    owned = (target >= vocab_start) & (target < vocab_end)
-    return mx, se, tl, owned
+    _count()
+    return mx, se, tl, None
 
 
 def ce_grad(logits, target, vocab_start, gmax, gsum, scale, out_dtype):
@@ -206,12 +226,14 @@ def lm_head_ce_grad(X, w, labels, vocab_start, state, g_over_n):
     logits, gm, gs = state
     d = torch.empty_like(logits)
     C.ce_grad(logits, labels.contiguous(), gm, gs, g_over_n.float().reshape(1), 1.0, d, vocab_start)
+    _count()
     return d
 
 
 # -------------------------------------------------------------- optimizer
 def adamw_flat(p, g, m, v, compute, scale, *, lr, beta1, beta2, eps, weight_decay, step):
     C.adamw_flat(p, g, m, v, compute, scale.reshape(1), lr, beta1, beta2, eps, weight_decay, step)
+    _count()
 
 
 _norm_tables: dict[tuple, tuple] = {}
@@ -240,4 +262,5 @@ def weighted_sq_norm(tensors, weights):
         _norm_tables[key] = table
     out = torch.zeros((), dtype=torch.float64, device=device)
     C.weighted_sq_norm(*table, out)
+    _count()
     return out

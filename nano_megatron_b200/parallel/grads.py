@@ -156,9 +156,19 @@ def grad_norm_squared(model, ctx: ParallelContext, *, tie_embeddings: bool = Fal
     params = list(model.parameters())
     device = params[0].device if params else torch.device("cpu")
     terms = _norm_terms(model, ctx, tie_embeddings)
-    if device.type == "cuda" and terms:
+    buffers = _flat_buffers(model)
+    if device.type == "cuda" and terms and buffers is not None:
+        # One pass over the flat gradient buffer, region by region (a fused
+        # q|k|v or gate|up region holds parameters with one common weight).
         from .. import ops
-        total = ops.cuda_ops().weighted_sq_norm([p.grad for p, _ in terms], [w for _, w in terms])
+        weight_of = {id(p): w for p, w in terms}
+        blocks, weights = [], []
+        for region in buffers.regions:
+            w = weight_of.get(id(region.params[0]))
+            if w is not None:
+                blocks.append(region.grad_block)
+                weights.append(w)
+        total = ops.cuda_ops().weighted_sq_norm(blocks, weights)
     else:
         total = torch.zeros((), dtype=torch.float64, device=device)
         for p, w in terms:

@@ -19,6 +19,7 @@ SOURCES = [
     "elementwise_bindings.cpp",
     "gemm.cu",
     "kernels.cu",
+    "attention.cu",
 ]
 
 NVCC_FLAGS = [

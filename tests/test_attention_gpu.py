@@ -1,0 +1,59 @@
+"""Flash attention kernels (forward and backward, with RoPE) against the
+plain-PyTorch fp32 computation of the same causal attention."""
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+if not torch.cuda.is_available():  # pragma: no cover
+    pytest.skip("needs a CUDA GPU", allow_module_level=True)
+
+from nano_megatron_b200.ops import cuda as KC  # noqa: E402
+from nano_megatron_b200.ops import reference as R  # noqa: E402
+
+DEV = torch.device("cuda", 0)
+
+
+def _rel(a, b):
+    return ((a.float() - b.float()).norm() / b.float().norm().clamp_min(1e-12)).item()
+
+
+@pytest.mark.parametrize("S,b,h", [(64, 1, 1), (128, 2, 2), (512, 1, 4), (1024, 2, 3)])
+def test_flash_attention_fwd_bwd(S, b, h):
+    torch.manual_seed(S + b + h)
+    d = 128
+    cos, sin = R.rope_cache(S, d, 10000.0, DEV)
+    qkv = torch.randn(S * b, 3 * h * d, device=DEV).bfloat16()
+    o, saved = KC.attention(qkv, b, h, d, cos, sin)
+    o_ref, saved_ref = R.attention(qkv.float(), b, h, d, cos, sin)
+    assert _rel(o, o_ref) < 1.5e-2, _rel(o, o_ref)
+    do = torch.randn(S * b, h * d, device=DEV).bfloat16()
+    dqkv = KC.attention_bwd(do, saved, b, h, d, cos, sin)
+    dqkv_ref = R.attention_bwd(do.float(), saved_ref, b, h, d, cos, sin)
+    q, k, v = R.split_qkv(dqkv, b, h, d)
+    qr, kr, vr = R.split_qkv(dqkv_ref, b, h, d)
+    assert _rel(v, vr) < 2e-2, _rel(v, vr)
+    assert _rel(k, kr) < 3e-2, _rel(k, kr)
+    assert _rel(q, qr) < 3e-2, _rel(q, qr)
+
+
+def test_attention_leaves_input_untouched():
+    S, b, h, d = 128, 1, 2, 128
+    cos, sin = R.rope_cache(S, d, 10000.0, DEV)
+    qkv = torch.randn(S * b, 3 * h * d, device=DEV).bfloat16()
+    before = qkv.clone()
+    KC.attention(qkv, b, h, d, cos, sin)
+    assert torch.equal(qkv, before)
+
+
+def test_lse_is_log_sum_exp_of_scaled_scores():
+    torch.manual_seed(0)
+    S, b, h, d = 128, 1, 1, 128
+    qkv = torch.randn(S * b, 3 * h * d, device=DEV).bfloat16()
+    from nano_megatron_b200 import _C
+    o, lse = _C.flash_attn_fwd(qkv.contiguous(), b, h, d)
+    q, k, _ = R.split_qkv(qkv.float(), b, h, d)
+    s = (q[:, 0, 0] @ k[:, 0, 0].t()) / d ** 0.5
+    s = s.masked_fill(torch.triu(torch.ones(S, S, device=DEV, dtype=torch.bool), 1), float("-inf"))
+    torch.testing.assert_close(lse[0], torch.logsumexp(s, -1), rtol=1e-3, atol=1e-3)
