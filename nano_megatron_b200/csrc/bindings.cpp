@@ -9,6 +9,7 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
 
+#include "fused_tp.cuh"
 #include "gemm.cuh"
 #include "kernels.cuh"
 
@@ -84,6 +85,51 @@ void gemm(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, bool a_mn, bo
   check_ok(nmb::gemm_bf16(g, at::cuda::getCurrentCUDAStream()), "gemm_bf16");
 }
 
+// One fused tensor-parallel GEMM + collective (see fused_tp.cu). `ws` holds every
+// rank's workspace pointer (mapped in this process); offsets are in bytes.
+void fused_tp_gemm(int64_t mode, const at::Tensor& a_local, const at::Tensor& B, bool b_mn, at::Tensor& out,
+                   const std::vector<int64_t>& ws, int64_t rank, int64_t M, int64_t gather_off, int64_t recv_off,
+                   int64_t flags_off, int64_t epoch, bool copy_own, const at::Tensor& err, double timeout_s) {
+  check_cuda(a_local, "a_local");
+  check_cuda(B, "B");
+  check_cuda(out, "out");
+  TORCH_CHECK(a_local.scalar_type() == at::kBFloat16 && B.scalar_type() == at::kBFloat16 &&
+                  out.scalar_type() == at::kBFloat16,
+              "fused TP GEMMs run in bf16");
+  TORCH_CHECK(a_local.is_contiguous() && B.stride(1) == 1 && out.stride(1) == 1, "layout");
+  const int world = (int)ws.size();
+  TORCH_CHECK(world >= 1 && world <= nmb::kMaxRanks && rank >= 0 && rank < world, "bad group");
+  nmb::FusedTpArgs a{};
+  a.M = (int)M;
+  a.K = (int)a_local.size(1);
+  a.N = (int)(b_mn ? B.size(1) : B.size(0));
+  TORCH_CHECK((b_mn ? B.size(0) : B.size(1)) == a.K, "inner dimensions differ");
+  a.rank = (int)rank;
+  a.world = world;
+  a.m_chunk = (int)(M / world);
+  TORCH_CHECK(M % world == 0 && a.m_chunk % 128 == 0, "rows per rank must be a multiple of 128");
+  TORCH_CHECK(mode == nmb::kAllGatherGemm ? a_local.size(0) == a.m_chunk : a_local.size(0) == M, "A rows");
+  TORCH_CHECK(out.size(0) == (mode == nmb::kAllGatherGemm ? M : a.m_chunk) && out.size(1) == a.N, "out shape");
+  a.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  a.ldo = out.stride(0);
+  for (int r = 0; r < world; ++r) a.ws[r] = reinterpret_cast<uint8_t*>(ws[r]);
+  a.gather_off = gather_off;
+  a.recv_off = recv_off;
+  a.flags_off = flags_off;
+  a.a_local = reinterpret_cast<const __nv_bfloat16*>(a_local.data_ptr());
+  a.lda_local = a_local.stride(0);
+  a.epoch = (uint32_t)epoch;
+  a.copy_own = copy_own ? 1 : 0;
+  a.err = err.data_ptr<int>();
+  a.timeout_ns = (uint64_t)(timeout_s * 1e9);
+  const at::cuda::CUDAGuard guard(a_local.device());
+  check_ok(nmb::fused_tp_gemm((int)mode, a, B.data_ptr(), row_stride(B), b_mn, num_sms(),
+                              at::cuda::getCurrentCUDAStream()),
+           "fused_tp_gemm");
+}
+
+int64_t fused_tp_flag_bytes() { return nmb::kFlagInts * 4; }
+
 }  // namespace
 
 void register_elementwise(pybind11::module& m);
@@ -92,5 +138,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "nano_megatron_b200 sm_100a kernels";
   m.def("gemm", &gemm, "tcgen05 bf16 GEMM", pybind11::arg("A"), pybind11::arg("B"), pybind11::arg("C"),
         pybind11::arg("a_mn"), pybind11::arg("b_mn"), pybind11::arg("out_mode"), pybind11::arg("err") = pybind11::none());
+  m.def("fused_tp_gemm", &fused_tp_gemm);
+  m.def("fused_tp_flag_bytes", &fused_tp_flag_bytes);
   register_elementwise(m);
 }

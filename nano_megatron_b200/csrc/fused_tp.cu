@@ -1,0 +1,430 @@
+// Tensor-parallel GEMMs fused with their sequence-parallel collectives over
+// NVLink peer memory (one kernel does the math and the communication):
+//
+//   all-gather -> GEMM   Y[M,N] = AG(x)[M,K] @ B     (QKV, gate|up forward;
+//                                                      row-parallel dgrad)
+//   GEMM -> reduce-scatter   out[M/t,N] = RS(A[M,K] @ B)   (proj, down forward;
+//                                                      column-parallel dgrad)
+//
+// Both are the persistent tcgen05 GEMM of gemm.cu (TMA producer warp, MMA
+// warp, four epilogue warps, double-buffered TMEM accumulator) plus one comm
+// warp, working in a symmetric workspace that every rank of the TP group has
+// mapped (peer pointers `ws[r]`):
+//
+//   workspace = gather [M][K] bf16 | recv [t][M/t][N] bf16 | flags (int32)
+//
+// all-gather -> GEMM (rank r):
+//   * comm warp: announces `ready[r] = epoch` on every peer, then pushes this
+//     CTA's slice of the local shard x into peer p's gather buffer, rows of
+//     chunk r, for p = r-1, r-2, ... (the peer that needs chunk r soonest
+//     first), each after p announced ready; then sets ag_done[r][cta] = epoch
+//     on p (release, system scope, after a system fence).
+//   * tiles run chunk by chunk starting with the own chunk, whose A tiles TMA
+//     reads straight from x. Before the first tile of chunk c the producer
+//     waits until all of c's CTAs have set ag_done[c][*] (acquire), fences the
+//     async proxy, and TMA-loads A from the local gather buffer. Only local
+//     memory is ever read by TMA; no TMA load uses cluster multicast.
+// GEMM -> reduce-scatter (rank r):
+//   * tiles run chunk r+1, r+2, ... and the own chunk last. The epilogue of a
+//     foreign tile converts the fp32 accumulator to bf16 and stores it into
+//     the owner's recv[r] slot (peer stores), then sets rs_done[tile][r].
+//     The epilogue of an own tile waits for rs_done[tile][*] of every peer and
+//     writes acc + sum of the peers' partials (fp32 sum) to the output.
+//   * no rank waits before it has pushed everything the others wait on, so
+//     the protocol cannot deadlock as long as every rank runs the kernel.
+//
+// Reuse of the workspace across calls: every call carries a new epoch; a rank
+// writes into a peer's buffers only after that peer announced the epoch,
+// i.e. after the peer's previous kernels (which read the buffers) finished.
+// Every wait is bounded (`timeout_ns`): on expiry the kernel records
+// kPeerTimeout in the error word, stops waiting and returns (results are then
+// garbage and the host raises).
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include "fused_tp.cuh"
+#include "gemm.cuh"
+#include "ptx.cuh"
+
+namespace nmb {
+
+namespace {
+
+constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4;
+constexpr int A_TILE_BYTES = BM * BK * 2;
+constexpr int B_TILE_BYTES = BN * BK * 2;
+constexpr int STAGE_BYTES = A_TILE_BYTES + B_TILE_BYTES;
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
+constexpr int THREADS = 224;  // 7 warps: producer, MMA, 4 epilogue, comm
+
+__device__ __forceinline__ void st_release_sys(int* p, int v) {
+  asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ int ld_acquire_sys(const int* p) {
+  int v;
+  asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
+__device__ __forceinline__ void epilogue_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+// Wait until *flag >= want. Returns false (and records kPeerTimeout) on expiry.
+__device__ bool wait_flag(const int* flag, int want, int* err, uint64_t timeout_ns, volatile int* abort_flag) {
+  if (ld_acquire_sys(flag) >= want) return true;
+  const uint64_t start = globaltimer_ns();
+  while (true) {
+    if (*abort_flag) return false;
+    for (int i = 0; i < 32; ++i) {
+      if (ld_acquire_sys(flag) >= want) return true;
+      __nanosleep(64);
+    }
+    if (globaltimer_ns() - start > timeout_ns) {
+      report_error(err, kPeerTimeout);
+      *abort_flag = 1;
+      return false;
+    }
+  }
+}
+
+// mbarrier wait that gives up at once when another role has aborted.
+__device__ bool mbar_wait_abortable(uint64_t* bar, uint32_t parity, int* err, volatile int* abort_flag,
+                                    uint64_t timeout_ns = 20000000000ull) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t start = globaltimer_ns();
+  while (true) {
+    if (*abort_flag) return false;
+    for (int i = 0; i < 64; ++i)
+      if (mbar_try_wait(bar, parity)) return true;
+    if (globaltimer_ns() - start > timeout_ns) {
+      report_error(err, kBarrierTimeout);
+      *abort_flag = 1;
+      return false;
+    }
+  }
+}
+
+__device__ __forceinline__ int* flags_of(const FusedTpArgs& a, int rank) {
+  return reinterpret_cast<int*>(a.ws[rank] + a.flags_off);
+}
+
+struct TileInfo {
+  int tm, tn, chunk, local;
+};
+
+template <int MODE>
+__device__ __forceinline__ TileInfo tile_of(int t, const FusedTpArgs& a, int mt_chunk, int num_n) {
+  const int per_chunk = mt_chunk * num_n;
+  const int slot = t / per_chunk;
+  TileInfo ti;
+  ti.local = t - slot * per_chunk;
+  ti.chunk = MODE == kAllGatherGemm ? (a.rank + slot) % a.world : (a.rank + 1 + slot) % a.world;
+  ti.tm = ti.chunk * mt_chunk + ti.local % mt_chunk;
+  ti.tn = ti.local / mt_chunk;
+  return ti;
+}
+
+template <int MODE, bool B_MN>
+__global__ void __launch_bounds__(THREADS, 1)
+fused_tp_kernel(const __grid_constant__ CUtensorMap tmA_local, const __grid_constant__ CUtensorMap tmA_gather,
+                const __grid_constant__ CUtensorMap tmB, const FusedTpArgs a) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* mma_done = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int mt_chunk = a.m_chunk / BM;
+  const int num_n = (a.N + BN - 1) / BN;
+  const int num_tiles = a.world * mt_chunk * num_n;
+  const int num_k = (a.K + BK - 1) / BK;
+  const int epoch = (int)a.epoch;
+  int* my_flags = flags_of(a, a.rank);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 128);
+    }
+    mbar_init(mma_done, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 6) {
+    // ---------------------------------------------------------------- comm
+    if (lane == 0 && blockIdx.x == 0) {
+      for (int p = 0; p < a.world; ++p)
+        if (p != a.rank) st_release_sys(flags_of(a, p) + kReadyOff + a.rank, epoch);
+    }
+    if (MODE == kAllGatherGemm) {
+      // This CTA's slice of the local shard, in 16-byte units.
+      const long total = (long)a.m_chunk * a.K / 8;
+      const long per = (total + gridDim.x - 1) / gridDim.x;
+      const long beg = per * blockIdx.x, end = min(total, beg + per);
+      const uint4* src = reinterpret_cast<const uint4*>(a.a_local);
+      const long chunk_off = a.gather_off + (long)a.rank * a.m_chunk * a.K * 2;
+      for (int j = 1; j <= a.world; ++j) {
+        const int p = (a.rank - j + a.world) % a.world;  // j == world -> own slot
+        if (p == a.rank && !a.copy_own) continue;
+        if (p != a.rank) {
+          bool ok = true;
+          if (lane == 0) ok = wait_flag(my_flags + kReadyOff + p, epoch, a.err, a.timeout_ns, abort_flag);
+          ok = __shfl_sync(0xffffffffu, ok, 0);
+          if (!ok) break;
+        }
+        uint4* dst = reinterpret_cast<uint4*>(a.ws[p] + chunk_off);
+        long i = beg + lane;
+        for (; i + 31 * 8 < end; i += 32 * 8) {
+          uint4 v[8];
+#pragma unroll
+          for (int u = 0; u < 8; ++u) v[u] = src[i + 32 * u];
+#pragma unroll
+          for (int u = 0; u < 8; ++u) dst[i + 32 * u] = v[u];
+        }
+        for (; i < end; i += 32) dst[i] = src[i];
+        if (p != a.rank) {
+          __threadfence_system();
+          __syncwarp();
+          if (lane == 0) st_release_sys(flags_of(a, p) + kAgDoneOff + a.rank * kMaxCtas + blockIdx.x, epoch);
+        }
+      }
+    }
+  } else if (warp == 0 && lane == 0) {
+    // ------------------------------------------------------------ producer
+    tma_prefetch_desc(&tmA_local);
+    tma_prefetch_desc(&tmB);
+    uint32_t ready_mask = 1u << a.rank;
+    int stage = 0;
+    uint32_t phase = 0;
+    int issued[STAGES];  // parity of the last load issued into each stage, -1 if none
+#pragma unroll
+    for (int s = 0; s < STAGES; ++s) issued[s] = -1;
+    for (int t = blockIdx.x; t < num_tiles && !*abort_flag; t += gridDim.x) {
+      const TileInfo ti = tile_of<MODE>(t, a, mt_chunk, num_n);
+      const bool from_gather = MODE == kAllGatherGemm && ti.chunk != a.rank;
+      if (from_gather && !((ready_mask >> ti.chunk) & 1u)) {
+        const int* done = my_flags + kAgDoneOff + ti.chunk * kMaxCtas;
+        for (int c = 0; c < (int)gridDim.x; ++c)
+          if (!wait_flag(done + c, epoch, a.err, a.timeout_ns, abort_flag)) break;
+        fence_proxy_async_global();
+        ready_mask |= 1u << ti.chunk;
+      }
+      const CUtensorMap* amap = from_gather ? &tmA_gather : &tmA_local;
+      const int arow = (MODE == kAllGatherGemm && !from_gather) ? (ti.tm * BM - a.rank * a.m_chunk) : ti.tm * BM;
+      for (int kb = 0; kb < num_k; ++kb) {
+        if (!mbar_wait_abortable(&empty[stage], phase ^ 1, a.err, abort_flag)) break;
+        uint8_t* a_dst = smem + stage * STAGE_BYTES;
+        uint8_t* b_dst = a_dst + A_TILE_BYTES;
+        mbar_arrive_expect_tx(&full[stage], STAGE_BYTES);
+        issued[stage] = (int)phase;
+        const int k0 = kb * BK;
+        tma_load_2d(a_dst, amap, &full[stage], k0, arow);
+        if (B_MN) {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) tma_load_2d(b_dst + j * 8192, &tmB, &full[stage], ti.tn * BN + 64 * j, k0);
+        } else {
+          tma_load_2d(b_dst, &tmB, &full[stage], k0, ti.tn * BN);
+        }
+        if (++stage == STAGES) { stage = 0; phase ^= 1; }
+      }
+    }
+    // Never leave a TMA copy in flight at exit (matters only after an abort).
+    for (int s = 0; s < STAGES; ++s)
+      if (issued[s] >= 0) mbar_wait(&full[s], (uint32_t)issued[s], nullptr, 1000000000ull);
+  } else if (warp == 1 && lane == 0) {
+    // ------------------------------------------------------------- MMA issue
+    constexpr uint32_t idesc = idesc_bf16_f32(BM, BN, false, B_MN);
+    int stage = 0;
+    uint32_t phase = 0;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int t = blockIdx.x; t < num_tiles && !*abort_flag; t += gridDim.x) {
+      if (!mbar_wait_abortable(&tempty[acc], acc_phase ^ 1, a.err, abort_flag)) break;
+      tc_fence_after();
+      const uint32_t d_tmem = tmem_base + acc * BN;
+      for (int kb = 0; kb < num_k; ++kb) {
+        if (!mbar_wait_abortable(&full[stage], phase, a.err, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t a_base = smem_u32(smem + stage * STAGE_BYTES);
+        const uint32_t b_base = a_base + A_TILE_BYTES;
+#pragma unroll
+        for (int kk = 0; kk < BK / 16; ++kk) {
+          const uint64_t a_desc = smem_desc_sw128(a_base + kk * 32, 0, 1024);
+          const uint64_t b_desc = B_MN ? smem_desc_sw128(b_base + kk * 2048, 8192, 1024)
+                                       : smem_desc_sw128(b_base + kk * 32, 0, 1024);
+          mma_bf16_ss(d_tmem, a_desc, b_desc, idesc, (kb | kk) != 0);
+        }
+        mma_commit(&empty[stage]);
+        if (++stage == STAGES) { stage = 0; phase ^= 1; }
+      }
+      mma_commit(&tfull[acc]);
+      if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+    }
+    // Let the last MMAs finish before TMEM is released (matters only after an abort).
+    mma_commit(mma_done);
+    mbar_wait(mma_done, 0, nullptr, 1000000000ull);
+  } else if (warp >= 2 && warp <= 5) {
+    // ------------------------------------------------------------- epilogue
+    const int quarter = warp & 3;
+    const bool leader = warp == 2 && lane == 0;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    uint32_t ready_mask = 1u << a.rank;
+    // Control flow here is uniform over the 128 epilogue threads (named
+    // barriers): after an abort the loop still runs to the end, skipping waits.
+    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
+      const TileInfo ti = tile_of<MODE>(t, a, mt_chunk, num_n);
+      mbar_wait_abortable(&tfull[acc], acc_phase, a.err, abort_flag);
+      tc_fence_after();
+      const int row = ti.tm * BM + quarter * 32 + lane;
+      const int row_local = row - ti.chunk * a.m_chunk;
+      const uint32_t t_row = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN;
+      if (MODE == kReduceScatterGemm) {
+        // foreign tile: wait once for the owner's ready; own tile: wait for all partials
+        if (ti.chunk != a.rank && !((ready_mask >> ti.chunk) & 1u)) {
+          if (leader) wait_flag(my_flags + kReadyOff + ti.chunk, epoch, a.err, a.timeout_ns, abort_flag);
+          ready_mask |= 1u << ti.chunk;
+          epilogue_bar();
+        } else if (ti.chunk == a.rank) {
+          if (leader) {
+            const int* done = my_flags + kRsDoneOff + ti.local * kMaxRanks;
+            for (int s = 0; s < a.world; ++s)
+              if (s != a.rank && !wait_flag(done + s, epoch, a.err, a.timeout_ns, abort_flag)) break;
+          }
+          epilogue_bar();
+        }
+      }
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 32) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(t_row + c, r);
+        tmem_wait_ld();
+        const int col = ti.tn * BN + c;
+        if (col >= a.N) continue;
+        float v[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+        __nv_bfloat16* dst;
+        if (MODE == kAllGatherGemm) {
+          dst = a.out + (long)row * a.ldo + col;
+        } else if (ti.chunk != a.rank) {
+          dst = reinterpret_cast<__nv_bfloat16*>(a.ws[ti.chunk] + a.recv_off) +
+                ((long)a.rank * a.m_chunk + row_local) * a.N + col;
+        } else {
+          for (int s = 0; s < a.world; ++s) {
+            if (s == a.rank) continue;
+            const __nv_bfloat16* src = reinterpret_cast<const __nv_bfloat16*>(a.ws[a.rank] + a.recv_off) +
+                                       ((long)s * a.m_chunk + row_local) * a.N + col;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              if (col + 8 * j < a.N) {
+                const uint4 u = *reinterpret_cast<const uint4*>(src + 8 * j);
+                float2 f;
+                f = unpack_bf16x2(u.x); v[8 * j + 0] += f.x; v[8 * j + 1] += f.y;
+                f = unpack_bf16x2(u.y); v[8 * j + 2] += f.x; v[8 * j + 3] += f.y;
+                f = unpack_bf16x2(u.z); v[8 * j + 4] += f.x; v[8 * j + 5] += f.y;
+                f = unpack_bf16x2(u.w); v[8 * j + 6] += f.x; v[8 * j + 7] += f.y;
+              }
+            }
+          }
+          dst = a.out + (long)row_local * a.ldo + col;
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          if (col + 8 * j < a.N) {
+            uint4 u;
+            u.x = pack_bf16x2(v[8 * j + 0], v[8 * j + 1]);
+            u.y = pack_bf16x2(v[8 * j + 2], v[8 * j + 3]);
+            u.z = pack_bf16x2(v[8 * j + 4], v[8 * j + 5]);
+            u.w = pack_bf16x2(v[8 * j + 6], v[8 * j + 7]);
+            *reinterpret_cast<uint4*>(dst + 8 * j) = u;
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&tempty[acc]);
+      if (MODE == kReduceScatterGemm && ti.chunk != a.rank) {
+        __threadfence_system();
+        epilogue_bar();
+        if (leader) st_release_sys(flags_of(a, ti.chunk) + kRsDoneOff + ti.local * kMaxRanks + a.rank, epoch);
+      }
+      if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, 512);
+  }
+}
+
+template <int MODE, bool B_MN>
+cudaError_t launch(const FusedTpArgs& a, const void* B, long ldb, int num_sms, cudaStream_t stream) {
+  auto kernel = fused_tp_kernel<MODE, B_MN>;
+  static bool configured = false;
+  if (!configured) {
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    if (e != cudaSuccess) return e;
+    configured = true;
+  }
+  CUtensorMap ta_local, ta_gather, tb;
+  if (MODE == kAllGatherGemm) {
+    if (!make_tmap_bf16_2d(&ta_local, a.a_local, a.K, a.m_chunk, a.lda_local, 64, BM)) return cudaErrorInvalidValue;
+    if (!make_tmap_bf16_2d(&ta_gather, a.ws[a.rank] + a.gather_off, a.K, a.M, a.K, 64, BM))
+      return cudaErrorInvalidValue;
+  } else {
+    if (!make_tmap_bf16_2d(&ta_local, a.a_local, a.K, a.M, a.lda_local, 64, BM)) return cudaErrorInvalidValue;
+    ta_gather = ta_local;
+  }
+  if (!make_tmap_bf16_2d(&tb, B, B_MN ? a.N : a.K, B_MN ? a.K : a.N, ldb, 64, B_MN ? 64 : BN))
+    return cudaErrorInvalidValue;
+  const int tiles = a.world * (a.m_chunk / BM) * ((a.N + BN - 1) / BN);
+  int grid = tiles < num_sms ? tiles : num_sms;
+  if (grid > kMaxCtas) grid = kMaxCtas;
+  kernel<<<grid, THREADS, SMEM_BYTES, stream>>>(ta_local, ta_gather, tb, a);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t fused_tp_gemm(int mode, const FusedTpArgs& a, const void* B, long ldb, bool b_mn, int num_sms,
+                          cudaStream_t stream) {
+  if (a.world < 1 || a.world > kMaxRanks || a.m_chunk % BM != 0 || a.M != a.m_chunk * a.world || a.N % 8 != 0 ||
+      a.K % 8 != 0)
+    return cudaErrorInvalidValue;
+  if (mode == kReduceScatterGemm && (a.m_chunk / BM) * ((a.N + BN - 1) / BN) > kMaxTiles) return cudaErrorInvalidValue;
+  if (mode == kAllGatherGemm) {
+    return b_mn ? launch<kAllGatherGemm, true>(a, B, ldb, num_sms, stream)
+                : launch<kAllGatherGemm, false>(a, B, ldb, num_sms, stream);
+  }
+  return b_mn ? launch<kReduceScatterGemm, true>(a, B, ldb, num_sms, stream)
+              : launch<kReduceScatterGemm, false>(a, B, ldb, num_sms, stream);
+}
+
+}  // namespace nmb

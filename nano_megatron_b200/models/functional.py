@@ -77,8 +77,13 @@ class WeightRef:
 
 
 # ---------------------------------------------------------------- comm glue
-def _use_fused(pctx: ParallelContext, x: torch.Tensor) -> bool:
-    return x.is_cuda and pctx.tp_size > 1 and pctx.resources.get("fused_tp", False)
+def _use_fused(pctx: ParallelContext, x: torch.Tensor, rows_local: int) -> bool:
+    """Fused all-gather/reduce-scatter GEMM kernels: CUDA, bf16, TP > 1, enabled."""
+    if not (x.is_cuda and x.dtype == torch.bfloat16 and pctx.tp_size > 1
+            and pctx.resources.get("fused_tp", False)):
+        return False
+    from ..ops import fused_tp
+    return fused_tp.supported(rows_local, pctx)
 
 
 def _ag(x, pctx):
@@ -99,7 +104,7 @@ class _ColumnLinear(torch.autograd.Function):
     def forward(ctx, x, wref, pctx, mode, dtype, *params):
         x = x if x.dtype == dtype else x.to(dtype)
         w = wref.for_compute(dtype)
-        if mode == "ag" and _use_fused(pctx, x):
+        if mode == "ag" and _use_fused(pctx, x, x.shape[0]):
             from ..ops import fused_tp
             y = fused_tp.all_gather_matmul(x, w, pctx)
         else:
@@ -114,7 +119,7 @@ class _ColumnLinear(torch.autograd.Function):
         x, w = ctx.saved_tensors
         pctx, mode, wref = ctx.pctx, ctx.mode, ctx.wref
         dy = dy.contiguous()
-        if mode == "ag" and _use_fused(pctx, dy):
+        if mode == "ag" and _use_fused(pctx, dy, x.shape[0]):
             from ..ops import fused_tp
             dx = fused_tp.matmul_reduce_scatter(dy, w, pctx, transpose_b=True)
             X = fused_tp.all_gather(x, pctx)
@@ -136,7 +141,7 @@ class _RowLinear(torch.autograd.Function):
     def forward(ctx, x, wref, pctx, mode, dtype, *params):
         x = x if x.dtype == dtype else x.to(dtype)
         w = wref.for_compute(dtype)
-        if mode == "rs" and _use_fused(pctx, x):
+        if mode == "rs" and _use_fused(pctx, x, x.shape[0] // pctx.tp_size):
             from ..ops import fused_tp
             y = fused_tp.matmul_reduce_scatter(x, w, pctx, transpose_b=False)
         else:
@@ -154,7 +159,7 @@ class _RowLinear(torch.autograd.Function):
         x, w = ctx.saved_tensors
         pctx, mode, wref = ctx.pctx, ctx.mode, ctx.wref
         dy = dy.contiguous()
-        if mode == "rs" and _use_fused(pctx, dy):
+        if mode == "rs" and _use_fused(pctx, dy, dy.shape[0]):
             from ..ops import fused_tp
             dY, dx = fused_tp.all_gather_matmul(dy, w, pctx, transpose_b=True, return_gathered=True)
         else:

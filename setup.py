@@ -20,6 +20,7 @@ SOURCES = [
     "gemm.cu",
     "kernels.cu",
     "attention.cu",
+    "fused_tp.cu",
 ]
 
 NVCC_FLAGS = [

@@ -1,0 +1,119 @@
+"""Fused all-gather->GEMM and GEMM->reduce-scatter kernels on 2 GPUs, against
+fp32 torch references and against the NCCL path; plus a TP=2 sequence-parallel
+GPT step with and without the fused kernels. Needs at least 2 GPUs (skipped
+otherwise). Every cross-GPU wait in the kernels is bounded; the test lowers the
+bound to 10 s so a protocol bug fails fast instead of waiting."""
+
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+if not torch.cuda.is_available() or torch.cuda.device_count() < 2:  # pragma: no cover
+    pytest.skip("needs 2 CUDA GPUs", allow_module_level=True)
+
+
+def _rel(a, b):
+    return ((a.float() - b.float()).norm() / b.float().norm().clamp_min(1e-12)).item()
+
+
+def _port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, q):
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    from datetime import timedelta
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            timeout=timedelta(seconds=60), device_id=dev)
+    failures = []
+    try:
+        from nano_megatron_b200.ops import cuda as KC
+        from nano_megatron_b200.ops import fused_tp
+        from nano_megatron_b200.parallel import init_parallel
+        fused_tp.TIMEOUT_S = 10.0
+        pctx = init_parallel(tp_size=world)
+
+        def full(seed, *shape):
+            g = torch.Generator(device=dev).manual_seed(seed)
+            return torch.randn(*shape, generator=g, device=dev).bfloat16()
+
+        for it in range(3):
+            for (mc, k, n) in [(256, 512, 768), (128, 256, 392)]:
+                rows = mc * world
+                x = full(1 + it, rows, k)
+                w = full(2 + it, k, n)
+                wt = w.t().contiguous()
+                # all-gather -> GEMM, both B layouts, with the gathered copy
+                y = fused_tp.all_gather_matmul(x[rank * mc:(rank + 1) * mc], w, pctx)
+                ref = x.float() @ w.float()
+                if _rel(y, ref) > 5e-3:
+                    failures.append(f"ag_gemm {mc},{k},{n}: {_rel(y, ref)}")
+                g, y2 = fused_tp.all_gather_matmul(x[rank * mc:(rank + 1) * mc], wt, pctx, transpose_b=True,
+                                                   return_gathered=True)
+                if not torch.equal(g, x):
+                    failures.append("gathered copy differs")
+                if _rel(y2, ref) > 5e-3:
+                    failures.append(f"ag_gemm^T {_rel(y2, ref)}")
+                # GEMM -> reduce-scatter: every rank has its own partial A
+                a_parts = [full(100 + r + it, rows, k) for r in range(world)]
+                out = fused_tp.matmul_reduce_scatter(a_parts[rank], w, pctx)
+                ref = sum(p.float() @ w.float() for p in a_parts)[rank * mc:(rank + 1) * mc]
+                if _rel(out, ref) > 1e-2:
+                    failures.append(f"gemm_rs {mc},{k},{n}: {_rel(out, ref)}")
+                out2 = fused_tp.matmul_reduce_scatter(a_parts[rank], wt, pctx, transpose_b=True)
+                if _rel(out2, ref) > 1e-2:
+                    failures.append(f"gemm_rs^T {_rel(out2, ref)}")
+        torch.cuda.synchronize()
+        KC.check_status(dev)
+
+        # a TP=2 SP model step: fused kernels vs NCCL collectives, same weights
+        from nano_megatron_b200 import GPT, GPTConfig
+        cfg = GPTConfig(vocab_size=1024, n_layer=2, n_head=4, n_embd=512, seq_len=512, ffn_hidden_size=1024,
+                        compute_dtype="bfloat16", sequence_parallel=True, tie_word_embeddings=False,
+                        init_std=0.05)
+        torch.manual_seed(rank)
+        model = GPT(cfg, pctx, device=dev)
+        x = torch.randint(0, 1024, (1, 512), generator=torch.Generator().manual_seed(5)).to(dev)
+        t = torch.randint(0, 1024, (1, 512), generator=torch.Generator().manual_seed(6)).to(dev)
+        grads = {}
+        losses = {}
+        for fused in (False, True):
+            pctx.resources["fused_tp"] = fused
+            model.zero_grad()
+            loss = model(x, t)
+            loss.backward()
+            losses[fused] = loss.item()
+            grads[fused] = [p.grad.clone() for p in model.parameters()]
+        if abs(losses[True] - losses[False]) > 1e-2 * abs(losses[False]):
+            failures.append(f"model loss fused {losses[True]} vs nccl {losses[False]}")
+        for (name, _), gf, gn in zip(model.named_parameters(), grads[True], grads[False]):
+            if _rel(gf, gn) > 3e-2:
+                failures.append(f"model grad {name}: {_rel(gf, gn)}")
+        KC.check_status(dev)
+    except Exception as exc:  # report instead of hanging the peer
+        failures.append(f"exception: {exc!r}")
+    q.put((rank, failures))
+    dist.destroy_process_group()
+
+
+def test_fused_tp_two_gpus():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = dict(q.get(timeout=300) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+    assert results[0] == [] and results[1] == [], results
