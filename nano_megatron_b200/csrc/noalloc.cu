@@ -1,0 +1,93 @@
+// RMSNorm backward without any memory allocation, for callers that cannot
+// allocate: code that runs where cudaMalloc is forbidden or unsafe, such as
+// inside a host callback, in a process whose device memory is owned by
+// another allocator that must not be bypassed, or in a real-time loop where
+// an allocation could block or fail at an arbitrary moment.
+//
+// The regular entry point (rmsnorm_bwd in kernels.cu, used by the framework)
+// takes a caller-provided fp32 buffer for the per-block weight-gradient
+// partials. This variant keeps those partials in a fixed array in device
+// global memory instead, defined below at file scope. Properties:
+//
+//  * Size limit: the array holds kScratchFloats fp32 values (4.6 MiB). A call
+//    needs rmsnorm_bwd_blocks(rows) * cols of them (at most 296 * cols), so
+//    every `rows` works for cols <= 4096; larger requests are rejected with
+//    NMB_NOALLOC_TOO_LARGE before anything is launched.
+//  * Every GPU on which the library is loaded holds this array until the
+//    process exits.
+//  * Set-up: the array's name in host code is only a host-side stand-in, not a
+//    device address. The first call on a device (with that device current)
+//    looks up the device address with cudaGetSymbolAddress and caches it; make
+//    that first call before any stream capture.
+//  * All calls share the array, and a call leaves its partials in it. The
+//    kernel writes every partial it later reads, so nothing needs clearing,
+//    but two calls whose kernels overlap on the GPU (different streams
+//    without ordering) race on the array and give wrong results.
+//  * No cudaMalloc, cudaFree or allocating library routine is called.
+
+#include <cuda_runtime.h>
+
+#include <mutex>
+
+#include "kernels.cuh"
+#include "noalloc.h"
+
+namespace {
+
+constexpr long kScratchFloats = 296L * 4096L;
+constexpr int kMaxDevices = 64;
+
+static __device__ __align__(256) float g_norm_partials[kScratchFloats];
+
+float* g_scratch_ptr[kMaxDevices] = {nullptr};
+std::mutex g_setup_mutex;
+
+float* scratch_for_current_device(int* code) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+    *code = NMB_NOALLOC_SETUP_FAILED;
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lock(g_setup_mutex);
+  if (g_scratch_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_norm_partials) != cudaSuccess || p == nullptr) {
+      *code = NMB_NOALLOC_SETUP_FAILED;
+      return nullptr;
+    }
+    g_scratch_ptr[dev] = static_cast<float*>(p);
+  }
+  return g_scratch_ptr[dev];
+}
+
+}  // namespace
+
+extern "C" long nmb_rmsnorm_bwd_noalloc_scratch_floats(void) { return kScratchFloats; }
+
+extern "C" int nmb_rmsnorm_bwd_noalloc(const void* dy, const void* x, const float* w, const float* rstd, void* dx,
+                                       float* dweight, int rows, int cols, int dtype, cudaStream_t stream) {
+  if (!dy || !x || !w || !rstd || !dx || !dweight || rows <= 0 || cols <= 0 || cols % 8 != 0 ||
+      (dtype != 0 && dtype != 1))
+    return NMB_NOALLOC_BAD_ARGUMENT;
+  const int blocks = nmb::rmsnorm_bwd_blocks(rows);
+  if ((long)blocks * cols > kScratchFloats) return NMB_NOALLOC_TOO_LARGE;
+  int code = NMB_NOALLOC_OK;
+  float* partials = scratch_for_current_device(&code);
+  if (partials == nullptr) return code;
+  if (nmb::rmsnorm_bwd(dy, x, w, rstd, dx, partials, rows, cols, dtype, stream) != cudaSuccess)
+    return NMB_NOALLOC_LAUNCH_FAILED;
+  if (nmb::reduce_rows_add(partials, dweight, blocks, cols, stream) != cudaSuccess)
+    return NMB_NOALLOC_LAUNCH_FAILED;
+  return NMB_NOALLOC_OK;
+}
+
+extern "C" const char* nmb_noalloc_error_string(int code) {
+  switch (code) {
+    case NMB_NOALLOC_OK: return "ok";
+    case NMB_NOALLOC_TOO_LARGE: return "rows/cols need more scratch than the fixed 296*4096-float array holds";
+    case NMB_NOALLOC_BAD_ARGUMENT: return "null pointer, non-positive size, cols not a multiple of 8, or bad dtype";
+    case NMB_NOALLOC_SETUP_FAILED: return "could not obtain the scratch array's device address on this device";
+    case NMB_NOALLOC_LAUNCH_FAILED: return "a kernel launch failed";
+    default: return "unknown code";
+  }
+}

@@ -21,6 +21,7 @@ SOURCES = [
     "kernels.cu",
     "attention.cu",
     "fused_tp.cu",
+    "noalloc.cu",
 ]
 
 NVCC_FLAGS = [
