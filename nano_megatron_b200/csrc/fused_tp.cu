@@ -23,7 +23,7 @@
 //     reads straight from x. Before the first tile of chunk c the producer
 //     waits until all of c's CTAs have set ag_done[c][*] (acquire), fences the
 //     async proxy, and TMA-loads A from the local gather buffer. Only local
-//     memory is ever read by TMA; no TMA load uses cluster multicast.
+//     memory is ever read by TMA (peer data arrives by plain stores).
 // GEMM -> reduce-scatter (rank r):
 //   * tiles run chunk r+1, r+2, ... and the own chunk last. The epilogue of a
 //     foreign tile converts the fp32 accumulator to bf16 and stores it into
