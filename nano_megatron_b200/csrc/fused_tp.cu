@@ -52,11 +52,21 @@ namespace nmb {
 
 namespace {
 
-constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4;
+constexpr int BM = 128, BN = 256, BK = 64;
 constexpr int A_TILE_BYTES = BM * BK * 2;
 constexpr int B_TILE_BYTES = BN * BK * 2;
 constexpr int STAGE_BYTES = A_TILE_BYTES + B_TILE_BYTES;
-constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
+// The reduce-scatter variant trades one pipeline stage for a 64 KB staging
+// area in which each epilogue warp assembles 32 full 512-byte output rows, so
+// partial tiles cross NVLink as whole rows (one warp instruction = 512
+// contiguous bytes) instead of 64-byte pieces of 32 different rows.
+constexpr int STAGING_BYTES = 4 * 32 * BN * 2;
+template <int MODE>
+struct Cfg {
+  static constexpr int STAGES = MODE == kReduceScatterGemm ? 3 : 4;
+  static constexpr int STAGING = MODE == kReduceScatterGemm ? STAGING_BYTES : 0;
+  static constexpr int SMEM = STAGES * STAGE_BYTES + STAGING + 1024 + 256;
+};
 constexpr int THREADS = 224;  // 7 warps: producer, MMA, 4 epilogue, comm
 
 __device__ __forceinline__ void st_release_sys(int* p, int v) {
@@ -134,9 +144,11 @@ template <int MODE, bool B_MN>
 __global__ void __launch_bounds__(THREADS, 1)
 fused_tp_kernel(const __grid_constant__ CUtensorMap tmA_local, const __grid_constant__ CUtensorMap tmA_gather,
                 const __grid_constant__ CUtensorMap tmB, const FusedTpArgs a) {
+  constexpr int STAGES = Cfg<MODE>::STAGES;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+  uint8_t* staging = smem + STAGES * STAGE_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(staging + Cfg<MODE>::STAGING);
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
@@ -332,8 +344,20 @@ fused_tp_kernel(const __grid_constant__ CUtensorMap tmA_local, const __grid_cons
         if (MODE == kAllGatherGemm) {
           dst = a.out + (long)row * a.ldo + col;
         } else if (ti.chunk != a.rank) {
-          dst = reinterpret_cast<__nv_bfloat16*>(a.ws[ti.chunk] + a.recv_off) +
-                ((long)a.rank * a.m_chunk + row_local) * a.N + col;
+          // stage this thread's 32 columns (row `lane` of the warp's 32 rows);
+          // 16-byte chunk j of a row sits at position j ^ (row % 8)
+          uint8_t* srow = staging + (quarter * 32 + lane) * (BN * 2);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            uint4 u;
+            u.x = pack_bf16x2(v[8 * j + 0], v[8 * j + 1]);
+            u.y = pack_bf16x2(v[8 * j + 2], v[8 * j + 3]);
+            u.z = pack_bf16x2(v[8 * j + 4], v[8 * j + 5]);
+            u.w = pack_bf16x2(v[8 * j + 6], v[8 * j + 7]);
+            const int chunk = c / 8 + j;
+            *reinterpret_cast<uint4*>(srow + ((chunk ^ (lane & 7)) << 4)) = u;
+          }
+          continue;
         } else {
           for (int s = 0; s < a.world; ++s) {
             if (s == a.rank) continue;
@@ -368,6 +392,19 @@ fused_tp_kernel(const __grid_constant__ CUtensorMap tmA_local, const __grid_cons
       tc_fence_before();
       mbar_arrive(&tempty[acc]);
       if (MODE == kReduceScatterGemm && ti.chunk != a.rank) {
+        // write the warp's 32 staged rows to the owner, one 512-byte row per instruction
+        __syncwarp();
+        const int col = ti.tn * BN + lane * 8;
+        const int row0 = ti.tm * BM + quarter * 32 - ti.chunk * a.m_chunk;
+        __nv_bfloat16* dst0 = reinterpret_cast<__nv_bfloat16*>(a.ws[ti.chunk] + a.recv_off) +
+                              ((long)a.rank * a.m_chunk + row0) * a.N + col;
+#pragma unroll 4
+        for (int r = 0; r < 32; ++r) {
+          const uint4 u = *reinterpret_cast<const uint4*>(staging + (quarter * 32 + r) * (BN * 2) +
+                                                           ((lane ^ (r & 7)) << 4));
+          if (col < a.N) *reinterpret_cast<uint4*>(dst0 + (long)r * a.N) = u;
+        }
+        __syncwarp();
         __threadfence_system();
         epilogue_bar();
         if (leader) st_release_sys(flags_of(a, ti.chunk) + kRsDoneOff + ti.local * kMaxRanks + a.rank, epoch);
@@ -389,7 +426,7 @@ cudaError_t launch(const FusedTpArgs& a, const void* B, long ldb, int num_sms, c
   auto kernel = fused_tp_kernel<MODE, B_MN>;
   static bool configured = false;
   if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<MODE>::SMEM);
     if (e != cudaSuccess) return e;
     configured = true;
   }
@@ -407,7 +444,7 @@ cudaError_t launch(const FusedTpArgs& a, const void* B, long ldb, int num_sms, c
   const int tiles = a.world * (a.m_chunk / BM) * ((a.N + BN - 1) / BN);
   int grid = tiles < num_sms ? tiles : num_sms;
   if (grid > kMaxCtas) grid = kMaxCtas;
-  kernel<<<grid, THREADS, SMEM_BYTES, stream>>>(ta_local, ta_gather, tb, a);
+  kernel<<<grid, THREADS, Cfg<MODE>::SMEM, stream>>>(ta_local, ta_gather, tb, a);
   return cudaGetLastError();
 }
 
