@@ -1,6 +1,6 @@
 """Fused-collective microbenchmark on 2/4/8 GPUs.
 
-    torchrun --nproc-per-node N bench_tp.py [--m 4096 16384 65536]
+    torchrun --nproc-per-node N bench_tp.py [--tokens 4096 16384 65536]
 
 For every token count M and (K, N) shape, times on each rank with CUDA events
 (max over ranks, L2 flushed between iterations by writing a 256 MB buffer):
@@ -36,7 +36,7 @@ LINK_GBS = 770.0
 
 def main():
     p = argparse.ArgumentParser()
-    p.add_argument("--m", type=int, nargs="+", default=[4096, 16384, 65536])
+    p.add_argument("--tokens", type=int, nargs="+", default=[4096, 16384, 65536])
     p.add_argument("--shapes", default="4096x12288,4096x14336,14336x4096")
     p.add_argument("--iters", type=int, default=10)
     p.add_argument("--warmup", type=int, default=3)
@@ -78,7 +78,7 @@ def main():
     gen = torch.Generator(device=dev).manual_seed(rank)
     for shape in args.shapes.split(","):
         K, N = (int(v) for v in shape.split("x"))
-        for M in args.m:
+        for M in args.tokens:
             # ---- all-gather -> GEMM (N sharded)
             x = torch.randn(M // t, K, device=dev, generator=gen).bfloat16()
             w = torch.randn(K, N // t, device=dev, generator=gen).bfloat16()

@@ -10,6 +10,10 @@ namespace nmb {
 cudaError_t flash_attn_fwd(const __nv_bfloat16* qkv, __nv_bfloat16* out, float* lse, int S, int batch, int heads,
                            int head_dim, cudaStream_t stream);
 
+// Same contract on tcgen05 tensor cores; S must be a multiple of 128.
+cudaError_t flash_attn_fwd_tc(const __nv_bfloat16* qkv, __nv_bfloat16* out, float* lse, int S, int batch, int heads,
+                              int head_dim, int* err, cudaStream_t stream);
+
 // dqkv [S*batch, 3*heads*hd] (every element written); dvec [batch*heads*S] and
 // dq_acc [batch*heads*S*hd] fp32 are scratch.
 cudaError_t flash_attn_bwd(const __nv_bfloat16* dout, const __nv_bfloat16* qkv, const __nv_bfloat16* out,

@@ -158,6 +158,23 @@ std::vector<at::Tensor> flash_attn_fwd(const at::Tensor& qkv, int64_t batch, int
   return {out, lse};
 }
 
+std::vector<at::Tensor> flash_attn_fwd_tc(const at::Tensor& qkv, int64_t batch, int64_t heads, int64_t hd,
+                                          const at::Tensor& err) {
+  need(qkv, "qkv");
+  TORCH_CHECK(qkv.scalar_type() == at::kBFloat16, "flash attention runs in bf16");
+  TORCH_CHECK(qkv.size(1) == 3 * heads * hd && qkv.size(0) % batch == 0, "qkv shape");
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(qkv.data_ptr()) % 16 == 0, "qkv must be 16-byte aligned");
+  const int S = qkv.size(0) / batch;
+  auto out = at::empty({qkv.size(0), heads * hd}, qkv.options());
+  auto lse = at::empty({batch * heads, S}, qkv.options().dtype(at::kFloat));
+  const at::cuda::CUDAGuard g(qkv.device());
+  ok(nmb::flash_attn_fwd_tc(reinterpret_cast<const __nv_bfloat16*>(qkv.data_ptr()),
+                            reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), lse.data_ptr<float>(), S, batch, heads,
+                            hd, err.data_ptr<int>(), stream()),
+     "flash_attn_fwd_tc");
+  return {out, lse};
+}
+
 at::Tensor flash_attn_bwd(const at::Tensor& dout, const at::Tensor& qkv, const at::Tensor& out, const at::Tensor& lse,
                           int64_t batch, int64_t heads, int64_t hd) {
   need(dout, "dout"); need(qkv, "qkv"); need(out, "out"); need(lse, "lse");
@@ -194,5 +211,6 @@ void register_elementwise(pybind11::module& m) {
   m.def("adamw_flat", &adamw_flat);
   m.def("weighted_sq_norm", &weighted_sq_norm);
   m.def("flash_attn_fwd", &flash_attn_fwd);
+  m.def("flash_attn_fwd_tc", &flash_attn_fwd_tc);
   m.def("flash_attn_bwd", &flash_attn_bwd);
 }

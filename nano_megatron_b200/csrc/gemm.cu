@@ -270,6 +270,20 @@ bool make_tmap_bf16_2d(CUtensorMap* map, const void* base, uint64_t inner, uint6
   return r == CUDA_SUCCESS;
 }
 
+bool make_tmap_bf16_3d(CUtensorMap* map, const void* base, const uint64_t dims[3], const uint64_t strides_bytes[2],
+                       const uint32_t box[3]) {
+  auto fn = encode_fn();
+  if (fn == nullptr) return false;
+  cuuint64_t d[3] = {dims[0], dims[1], dims[2]};
+  cuuint64_t st[2] = {strides_bytes[0], strides_bytes[1]};
+  cuuint32_t bx[3] = {box[0], box[1], box[2]};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), d, st, bx, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 cudaError_t gemm_bf16(const GemmArgs& g, cudaStream_t stream) {
   if (g.M <= 0 || g.N <= 0 || g.K <= 0) return cudaSuccess;
   if (!g.a_mn && g.b_mn && g.out == OutMode::kBf16) return launch<false, true, 0>(g, stream);

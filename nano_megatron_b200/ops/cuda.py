@@ -146,7 +146,10 @@ def attention(qkv, batch, heads, head_dim, cos, sin, inplace=False):
     to ``qkv`` itself (the model passes its private QKV GEMM output)."""
     qkv = qkv.contiguous() if inplace else qkv.clone(memory_format=torch.contiguous_format)
     C.rope_inplace(qkv, cos, sin, batch, heads, head_dim, 1.0)
-    o, lse = C.flash_attn_fwd(qkv, batch, heads, head_dim)
+    if (qkv.shape[0] // batch) % 128 == 0:
+        o, lse = C.flash_attn_fwd_tc(qkv, batch, heads, head_dim, status_word(qkv.device))
+    else:  # sequence lengths that are not a multiple of 128: mma.sync kernel
+        o, lse = C.flash_attn_fwd(qkv, batch, heads, head_dim)
     _count(2)
     return o, (qkv, o, lse)
 

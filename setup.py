@@ -20,6 +20,7 @@ SOURCES = [
     "gemm.cu",
     "kernels.cu",
     "attention.cu",
+    "attention_tc.cu",
     "fused_tp.cu",
     "noalloc.cu",
 ]

@@ -57,3 +57,16 @@ def test_lse_is_log_sum_exp_of_scaled_scores():
     s = (q[:, 0, 0] @ k[:, 0, 0].t()) / d ** 0.5
     s = s.masked_fill(torch.triu(torch.ones(S, S, device=DEV, dtype=torch.bool), 1), float("-inf"))
     torch.testing.assert_close(lse[0], torch.logsumexp(s, -1), rtol=1e-3, atol=1e-3)
+
+
+@pytest.mark.parametrize("S,b,h", [(128, 1, 1), (1024, 2, 2), (2048, 1, 3)])
+def test_tcgen05_forward_matches_mma_sync_forward(S, b, h):
+    """The tcgen05 forward and the mma.sync forward agree (output and lse)."""
+    from nano_megatron_b200 import _C
+    torch.manual_seed(S * h)
+    qkv = torch.randn(S * b, 3 * h * 128, device=DEV).bfloat16()
+    o1, l1 = _C.flash_attn_fwd(qkv, b, h, 128)
+    o2, l2 = _C.flash_attn_fwd_tc(qkv, b, h, 128, KC.status_word(DEV))
+    KC.check_status(DEV)
+    assert _rel(o2, o1) < 1e-2, _rel(o2, o1)
+    torch.testing.assert_close(l2, l1, rtol=1e-4, atol=1e-4)
