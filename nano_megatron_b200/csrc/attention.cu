@@ -506,6 +506,13 @@ cudaError_t flash_attn_fwd(const __nv_bfloat16* qkv, __nv_bfloat16* out, float* 
   return cudaGetLastError();
 }
 
+cudaError_t flash_attn_bwd_dot(const __nv_bfloat16* dout, const __nv_bfloat16* out, float* dvec, int S, int batch,
+                               int heads, cudaStream_t stream) {
+  const long rows = (long)batch * heads * S;
+  flash_bwd_dot_kernel<<<(rows + 7) / 8, 256, 0, stream>>>(dout, out, dvec, S, batch, heads);
+  return cudaGetLastError();
+}
+
 cudaError_t flash_attn_bwd(const __nv_bfloat16* dout, const __nv_bfloat16* qkv, const __nv_bfloat16* out,
                            const float* lse, float* dvec, float* dq_acc, __nv_bfloat16* dqkv, int S, int batch,
                            int heads, int head_dim, cudaStream_t stream) {

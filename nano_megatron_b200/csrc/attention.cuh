@@ -20,4 +20,14 @@ cudaError_t flash_attn_bwd(const __nv_bfloat16* dout, const __nv_bfloat16* qkv, 
                            const float* lse, float* dvec, float* dq_acc, __nv_bfloat16* dqkv, int S, int batch,
                            int heads, int head_dim, cudaStream_t stream);
 
+// D[bh, s] = sum_d dO * O  (dvec [batch*heads*S])
+cudaError_t flash_attn_bwd_dot(const __nv_bfloat16* dout, const __nv_bfloat16* out, float* dvec, int S, int batch,
+                               int heads, cudaStream_t stream);
+
+// tcgen05 backward (dK/dV kernel + dQ kernel, no atomics); needs dvec from
+// flash_attn_bwd_dot; S must be a multiple of 128.
+cudaError_t flash_attn_bwd_tc(const __nv_bfloat16* dout, const __nv_bfloat16* qkv, const float* lse,
+                              const float* dvec, __nv_bfloat16* dqkv, int S, int batch, int heads, int head_dim,
+                              int* err, cudaStream_t stream);
+
 }  // namespace nmb

@@ -1,0 +1,464 @@
+// Causal flash-attention backward on 5th-generation tensor cores (sm_100a),
+// head_dim 128, bf16 in / out, fp32 math. Two deterministic kernels, no atomics:
+//
+//   dK/dV kernel (one CTA = 128 keys of one (batch, head); loops over the
+//   64-query blocks at or after it):
+//     S^T = K Q^T and dP^T = V dO^T      (tcgen05, M=128 keys, N=64 queries)
+//     P^T = exp(S^T*scale - lse[q]), dS^T = P^T (dP^T - D[q])   (4 warps, one
+//          key row per thread, causal mask on the diagonal blocks)
+//     dV += P^T dO and dK += dS^T Q      (tcgen05, accumulators stay in TMEM)
+//   dQ kernel (one CTA = 128 queries; loops over the 64-key blocks up to it):
+//     S = Q K^T, dP = dO V^T, dS = P (dP - D[q]), dQ += dS K.
+//
+// The dQ kernel recomputes S and dP instead of having the dK/dV kernel add
+// dQ partials with atomics: two extra 128x64x128 products per block pair buy
+// a fixed summation order and no fp32 atomic traffic.
+//
+// Both kernels: warp 0 issues TMA loads (tiles straight out of qkv / dO via
+// 3-D tensor maps), warp 1 issues the MMAs, warps 2-5 do the elementwise work
+// and the epilogue. S/dP live in double-buffered TMEM so the next block's
+// products overlap the current block's elementwise work. Every wait is bounded.
+// D[q] = rowsum(dO * O) comes from flash_bwd_dot_kernel (attention.cu).
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include <cmath>
+
+#include "attention.cuh"
+#include "gemm.cuh"
+#include "ptx.cuh"
+
+namespace nmb {
+
+namespace {
+
+constexpr int HD = 128;
+constexpr int THREADS = 192;
+constexpr int BIG = 128, SMALL = 64;           // rows of the resident / streamed tiles
+constexpr int HALF_BIG = BIG * 128;            // 16 KB: one 64-column half of a 128-row tile
+constexpr int HALF_SMALL = SMALL * 128;        // 8 KB: one 64-column half of a 64-row tile
+constexpr int TILE_BIG = 2 * HALF_BIG, TILE_SMALL = 2 * HALF_SMALL;
+constexpr float LOG2E = 1.4426950408889634f;
+
+// Row `r` of a [rows][64] bf16 K-major SW128 operand (128-byte rows): 16-byte
+// chunk `ch` of the row is stored at chunk position ch ^ (r % 8).
+__device__ __forceinline__ void store_row64(uint8_t* tile, int r, const float (&v)[SMALL]) {
+  uint8_t* row = tile + r * 128;
+#pragma unroll
+  for (int ch = 0; ch < SMALL / 8; ++ch) {
+    uint4 u;
+    u.x = pack_bf16x2(v[8 * ch + 0], v[8 * ch + 1]);
+    u.y = pack_bf16x2(v[8 * ch + 2], v[8 * ch + 3]);
+    u.z = pack_bf16x2(v[8 * ch + 4], v[8 * ch + 5]);
+    u.w = pack_bf16x2(v[8 * ch + 6], v[8 * ch + 7]);
+    *reinterpret_cast<uint4*>(row + ((ch ^ (r & 7)) << 4)) = u;
+  }
+}
+
+__device__ __forceinline__ void ld_row64(uint32_t taddr, float (&v)[SMALL]) {
+#pragma unroll
+  for (int c = 0; c < SMALL; c += 32) {
+    uint32_t u[32];
+    tmem_ld_32x32b_x32(taddr + c, u);
+    tmem_wait_ld();
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[c + i] = __uint_as_float(u[i]);
+  }
+}
+
+// Write a 128-column fp32 TMEM row, times `scale`, as bf16 to global memory.
+__device__ __forceinline__ void store_tmem_row(uint32_t taddr, __nv_bfloat16* dst, float scale, bool write) {
+#pragma unroll
+  for (int c = 0; c < HD; c += 32) {
+    uint32_t v[32];
+    tmem_ld_32x32b_x32(taddr + c, v);
+    tmem_wait_ld();
+    if (write) {
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        uint4 u;
+        u.x = pack_bf16x2(__uint_as_float(v[8 * k + 0]) * scale, __uint_as_float(v[8 * k + 1]) * scale);
+        u.y = pack_bf16x2(__uint_as_float(v[8 * k + 2]) * scale, __uint_as_float(v[8 * k + 3]) * scale);
+        u.z = pack_bf16x2(__uint_as_float(v[8 * k + 4]) * scale, __uint_as_float(v[8 * k + 5]) * scale);
+        u.w = pack_bf16x2(__uint_as_float(v[8 * k + 6]) * scale, __uint_as_float(v[8 * k + 7]) * scale);
+        *reinterpret_cast<uint4*>(dst + c + 8 * k) = u;
+      }
+    }
+  }
+}
+
+struct BwdArgs {
+  const float* lse;   // [batch*heads, S]
+  const float* dvec;  // [batch*heads, S]
+  __nv_bfloat16* dqkv;
+  int S, batch, heads;
+  float scale;
+  int* err;
+};
+
+// ============================================================ dK / dV kernel
+// smem: K 32K | V 32K | Q[2] 2x16K | dO[2] 2x16K | P^T 16K | dS^T 16K
+constexpr int KV_OFF_K = 0, KV_OFF_V = TILE_BIG, KV_OFF_Q = 2 * TILE_BIG, KV_OFF_DO = KV_OFF_Q + 2 * TILE_SMALL,
+              KV_OFF_PT = KV_OFF_DO + 2 * TILE_SMALL, KV_OFF_DST = KV_OFF_PT + BIG * 128,
+              KV_OFF_BAR = KV_OFF_DST + BIG * 128;
+constexpr int KV_SMEM = KV_OFF_BAR + 256 + 1024;
+
+__global__ void __launch_bounds__(THREADS, 1)
+flash_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tm_qkv_big, const __grid_constant__ CUtensorMap tm_qkv_small,
+                      const __grid_constant__ CUtensorMap tm_do_small, const BwdArgs a) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + KV_OFF_BAR);
+  uint64_t* kv_full = bars;         // K and V
+  uint64_t* qdo_full = bars + 1;    // [2]
+  uint64_t* qdo_empty = bars + 3;   // [2]
+  uint64_t* st_full = bars + 5;     // [2] S^T and dP^T of a block
+  uint64_t* st_free = bars + 7;     // [2]
+  uint64_t* pds_full = bars + 9;    // P^T and dS^T in smem
+  uint64_t* pds_free = bars + 10;
+  uint64_t* acc_done = bars + 11;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int kb = blockIdx.x;  // key block of 128; low index = most query blocks
+  const int bh = blockIdx.y, b = bh / a.heads, h = bh % a.heads;
+  const int first_qb = 2 * kb, nqb = a.S / SMALL;
+  const int nblk = nqb - first_qb;
+  const int q_col = h * HD, k_col = a.heads * HD + h * HD, v_col = 2 * a.heads * HD + h * HD, do_col = h * HD;
+
+  if (threadIdx.x == 0) {
+    mbar_init(kv_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&qdo_full[i], 1);
+      mbar_init(&qdo_empty[i], 1);
+      mbar_init(&st_full[i], 1);
+      mbar_init(&st_free[i], 128);
+    }
+    mbar_init(pds_full, 128);
+    mbar_init(pds_free, 1);
+    mbar_init(acc_done, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;  // S^T [0,64)+[64,128), dP^T [128,192)+[192,256), dV 256, dK 384
+  const uint32_t sbase = smem_u32(smem);
+
+  if (warp == 0 && lane == 0) {
+    int issued[2] = {-1, -1};
+    mbar_arrive_expect_tx(kv_full, 2 * TILE_BIG);
+    tma_load_3d(smem + KV_OFF_K, &tm_qkv_big, kv_full, k_col, b, kb * BIG);
+    tma_load_3d(smem + KV_OFF_K + HALF_BIG, &tm_qkv_big, kv_full, k_col + 64, b, kb * BIG);
+    tma_load_3d(smem + KV_OFF_V, &tm_qkv_big, kv_full, v_col, b, kb * BIG);
+    tma_load_3d(smem + KV_OFF_V + HALF_BIG, &tm_qkv_big, kv_full, v_col + 64, b, kb * BIG);
+    for (int i = 0; i < nblk; ++i) {
+      const int st = i & 1;
+      if (!lane_wait(&qdo_empty[st], ((i >> 1) & 1) ^ 1, a.err, abort_flag)) break;
+      const int q0 = (first_qb + i) * SMALL;
+      uint8_t* qd = smem + KV_OFF_Q + st * TILE_SMALL;
+      uint8_t* dd = smem + KV_OFF_DO + st * TILE_SMALL;
+      mbar_arrive_expect_tx(&qdo_full[st], 2 * TILE_SMALL);
+      tma_load_3d(qd, &tm_qkv_small, &qdo_full[st], q_col, b, q0);
+      tma_load_3d(qd + HALF_SMALL, &tm_qkv_small, &qdo_full[st], q_col + 64, b, q0);
+      tma_load_3d(dd, &tm_do_small, &qdo_full[st], do_col, b, q0);
+      tma_load_3d(dd + HALF_SMALL, &tm_do_small, &qdo_full[st], do_col + 64, b, q0);
+      issued[st] = (i >> 1) & 1;
+    }
+    mbar_wait(kv_full, 0, nullptr, 1000000000ull);
+    for (int st = 0; st < 2; ++st)
+      if (issued[st] >= 0) mbar_wait(&qdo_full[st], issued[st], nullptr, 1000000000ull);
+  } else if (warp == 1 && lane == 0) {
+    constexpr uint32_t idesc_t = idesc_bf16_f32(BIG, SMALL, false, false);  // S^T, dP^T
+    constexpr uint32_t idesc_acc = idesc_bf16_f32(BIG, HD, false, true);    // dV, dK
+    bool ok = lane_wait(kv_full, 0, a.err, abort_flag);
+    for (int i = 0; ok && i <= nblk; ++i) {
+      if (i < nblk) {
+        const int st = i & 1;
+        if (!lane_wait(&qdo_full[st], (i >> 1) & 1, a.err, abort_flag)) break;
+        if (!lane_wait(&st_free[st], ((i >> 1) & 1) ^ 1, a.err, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t qs = sbase + KV_OFF_Q + st * TILE_SMALL, ds = sbase + KV_OFF_DO + st * TILE_SMALL;
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; ++kk) {
+          mma_bf16_ss(tmem + st * SMALL, kmajor_desc(sbase + KV_OFF_K, kk, HALF_BIG), kmajor_desc(qs, kk, HALF_SMALL),
+                      idesc_t, kk > 0);
+          mma_bf16_ss(tmem + 128 + st * SMALL, kmajor_desc(sbase + KV_OFF_V, kk, HALF_BIG),
+                      kmajor_desc(ds, kk, HALF_SMALL), idesc_t, kk > 0);
+        }
+        mma_commit(&st_full[st]);
+      }
+      if (i >= 1) {
+        const int p = i - 1, st = p & 1;
+        if (!lane_wait(pds_full, p & 1, a.err, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t qs = sbase + KV_OFF_Q + st * TILE_SMALL, ds = sbase + KV_OFF_DO + st * TILE_SMALL;
+#pragma unroll
+        for (int kk = 0; kk < SMALL / 16; ++kk) {
+          // B = dO / Q block viewed N-major: [2 d-halves][64 q rows][128 B]
+          mma_bf16_ss(tmem + 256, smem_desc_sw128(sbase + KV_OFF_PT + kk * 32, 0, 1024),
+                      smem_desc_sw128(ds + kk * 2048, HALF_SMALL, 1024), idesc_acc, (p > 0 || kk > 0));
+          mma_bf16_ss(tmem + 384, smem_desc_sw128(sbase + KV_OFF_DST + kk * 32, 0, 1024),
+                      smem_desc_sw128(qs + kk * 2048, HALF_SMALL, 1024), idesc_acc, (p > 0 || kk > 0));
+        }
+        mma_commit(pds_free);
+        mma_commit(&qdo_empty[st]);
+      }
+    }
+    mma_commit(acc_done);
+  } else if (warp >= 2) {
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;  // key row within the block
+    const int key = kb * BIG + r;
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    const float* lse = a.lse + (long)bh * a.S;
+    const float* dvec = a.dvec + (long)bh * a.S;
+    const float sl2 = a.scale * LOG2E;
+    bool ok = true;
+    for (int i = 0; i < nblk && ok; ++i) {
+      const int st = i & 1;
+      const int q0 = (first_qb + i) * SMALL;
+      ok = warp_wait(&st_full[st], (i >> 1) & 1, a.err, abort_flag);
+      if (!ok) break;
+      tc_fence_after();
+      float s[SMALL], dp[SMALL];
+      ld_row64(tmem + lane_off + st * SMALL, s);
+      ld_row64(tmem + lane_off + 128 + st * SMALL, dp);
+      tc_fence_before();
+      mbar_arrive(&st_free[st]);
+#pragma unroll
+      for (int c = 0; c < SMALL; ++c) {
+        const int q = q0 + c;
+        const float pr = (key > q) ? 0.f : exp2f(s[c] * sl2 - __ldg(lse + q) * LOG2E);
+        s[c] = pr;
+        dp[c] = pr * (dp[c] - __ldg(dvec + q));
+      }
+      if (i > 0) {
+        ok = warp_wait(pds_free, (i - 1) & 1, a.err, abort_flag);
+        if (!ok) break;
+      }
+      store_row64(smem + KV_OFF_PT, r, s);
+      store_row64(smem + KV_OFF_DST, r, dp);
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(pds_full);
+    }
+    if (ok) ok = warp_wait(acc_done, 0, a.err, abort_flag);
+    tc_fence_after();
+    const long ld = 3L * a.heads * HD;
+    __nv_bfloat16* row = a.dqkv + ((long)key * a.batch + b) * ld;
+    store_tmem_row(tmem + lane_off + 256, row + v_col, 1.f, ok);     // dV
+    store_tmem_row(tmem + lane_off + 384, row + k_col, a.scale, ok);  // dK
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// ================================================================= dQ kernel
+// smem: Q 32K | dO 32K | K[2] 2x16K | V[2] 2x16K | dS 16K
+constexpr int Q_OFF_Q = 0, Q_OFF_DO = TILE_BIG, Q_OFF_K = 2 * TILE_BIG, Q_OFF_V = Q_OFF_K + 2 * TILE_SMALL,
+              Q_OFF_DS = Q_OFF_V + 2 * TILE_SMALL, Q_OFF_BAR = Q_OFF_DS + BIG * 128;
+constexpr int Q_SMEM = Q_OFF_BAR + 256 + 1024;
+
+__global__ void __launch_bounds__(THREADS, 1)
+flash_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tm_qkv_big, const __grid_constant__ CUtensorMap tm_qkv_small,
+                       const __grid_constant__ CUtensorMap tm_do_big, const BwdArgs a) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Q_OFF_BAR);
+  uint64_t* qdo_full = bars;
+  uint64_t* kv_full = bars + 1;    // [2]
+  uint64_t* kv_empty = bars + 3;   // [2]
+  uint64_t* s_full = bars + 5;     // [2]
+  uint64_t* s_free = bars + 7;     // [2]
+  uint64_t* ds_full = bars + 9;
+  uint64_t* ds_free = bars + 10;
+  uint64_t* acc_done = bars + 11;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int nqb = a.S / BIG;
+  const int qb = nqb - 1 - blockIdx.x;  // longest rows first
+  const int bh = blockIdx.y, b = bh / a.heads, h = bh % a.heads;
+  const int nblk = 2 * qb + 2;          // 64-key blocks up to the diagonal
+  const int q_col = h * HD, k_col = a.heads * HD + h * HD, v_col = 2 * a.heads * HD + h * HD, do_col = h * HD;
+
+  if (threadIdx.x == 0) {
+    mbar_init(qdo_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_free[i], 128);
+    }
+    mbar_init(ds_full, 128);
+    mbar_init(ds_free, 1);
+    mbar_init(acc_done, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;  // S [0,64)+[64,128), dP [128,192)+[192,256), dQ [256,384)
+  const uint32_t sbase = smem_u32(smem);
+
+  if (warp == 0 && lane == 0) {
+    int issued[2] = {-1, -1};
+    mbar_arrive_expect_tx(qdo_full, 2 * TILE_BIG);
+    tma_load_3d(smem + Q_OFF_Q, &tm_qkv_big, qdo_full, q_col, b, qb * BIG);
+    tma_load_3d(smem + Q_OFF_Q + HALF_BIG, &tm_qkv_big, qdo_full, q_col + 64, b, qb * BIG);
+    tma_load_3d(smem + Q_OFF_DO, &tm_do_big, qdo_full, do_col, b, qb * BIG);
+    tma_load_3d(smem + Q_OFF_DO + HALF_BIG, &tm_do_big, qdo_full, do_col + 64, b, qb * BIG);
+    for (int j = 0; j < nblk; ++j) {
+      const int st = j & 1;
+      if (!lane_wait(&kv_empty[st], ((j >> 1) & 1) ^ 1, a.err, abort_flag)) break;
+      uint8_t* kd = smem + Q_OFF_K + st * TILE_SMALL;
+      uint8_t* vd = smem + Q_OFF_V + st * TILE_SMALL;
+      mbar_arrive_expect_tx(&kv_full[st], 2 * TILE_SMALL);
+      tma_load_3d(kd, &tm_qkv_small, &kv_full[st], k_col, b, j * SMALL);
+      tma_load_3d(kd + HALF_SMALL, &tm_qkv_small, &kv_full[st], k_col + 64, b, j * SMALL);
+      tma_load_3d(vd, &tm_qkv_small, &kv_full[st], v_col, b, j * SMALL);
+      tma_load_3d(vd + HALF_SMALL, &tm_qkv_small, &kv_full[st], v_col + 64, b, j * SMALL);
+      issued[st] = (j >> 1) & 1;
+    }
+    mbar_wait(qdo_full, 0, nullptr, 1000000000ull);
+    for (int st = 0; st < 2; ++st)
+      if (issued[st] >= 0) mbar_wait(&kv_full[st], issued[st], nullptr, 1000000000ull);
+  } else if (warp == 1 && lane == 0) {
+    constexpr uint32_t idesc_s = idesc_bf16_f32(BIG, SMALL, false, false);  // S, dP
+    constexpr uint32_t idesc_q = idesc_bf16_f32(BIG, HD, false, true);      // dQ
+    bool ok = lane_wait(qdo_full, 0, a.err, abort_flag);
+    for (int j = 0; ok && j <= nblk; ++j) {
+      if (j < nblk) {
+        const int st = j & 1;
+        if (!lane_wait(&kv_full[st], (j >> 1) & 1, a.err, abort_flag)) break;
+        if (!lane_wait(&s_free[st], ((j >> 1) & 1) ^ 1, a.err, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t ks = sbase + Q_OFF_K + st * TILE_SMALL, vs = sbase + Q_OFF_V + st * TILE_SMALL;
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; ++kk) {
+          mma_bf16_ss(tmem + st * SMALL, kmajor_desc(sbase + Q_OFF_Q, kk, HALF_BIG), kmajor_desc(ks, kk, HALF_SMALL),
+                      idesc_s, kk > 0);
+          mma_bf16_ss(tmem + 128 + st * SMALL, kmajor_desc(sbase + Q_OFF_DO, kk, HALF_BIG),
+                      kmajor_desc(vs, kk, HALF_SMALL), idesc_s, kk > 0);
+        }
+        mma_commit(&s_full[st]);
+      }
+      if (j >= 1) {
+        const int p = j - 1, st = p & 1;
+        if (!lane_wait(ds_full, p & 1, a.err, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t ks = sbase + Q_OFF_K + st * TILE_SMALL;
+#pragma unroll
+        for (int kk = 0; kk < SMALL / 16; ++kk)
+          mma_bf16_ss(tmem + 256, smem_desc_sw128(sbase + Q_OFF_DS + kk * 32, 0, 1024),
+                      smem_desc_sw128(ks + kk * 2048, HALF_SMALL, 1024), idesc_q, (p > 0 || kk > 0));
+        mma_commit(ds_free);
+        mma_commit(&kv_empty[st]);
+      }
+    }
+    mma_commit(acc_done);
+  } else if (warp >= 2) {
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;  // query row
+    const int q = qb * BIG + r;
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    const float sl2 = a.scale * LOG2E;
+    const float lse2 = a.lse[(long)bh * a.S + q] * LOG2E;
+    const float dq = a.dvec[(long)bh * a.S + q];
+    bool ok = true;
+    for (int j = 0; j < nblk && ok; ++j) {
+      const int st = j & 1;
+      ok = warp_wait(&s_full[st], (j >> 1) & 1, a.err, abort_flag);
+      if (!ok) break;
+      tc_fence_after();
+      float s[SMALL], dp[SMALL];
+      ld_row64(tmem + lane_off + st * SMALL, s);
+      ld_row64(tmem + lane_off + 128 + st * SMALL, dp);
+      tc_fence_before();
+      mbar_arrive(&s_free[st]);
+#pragma unroll
+      for (int c = 0; c < SMALL; ++c) {
+        const int key = j * SMALL + c;
+        const float pr = (key > q) ? 0.f : exp2f(s[c] * sl2 - lse2);
+        dp[c] = pr * (dp[c] - dq);
+      }
+      if (j > 0) {
+        ok = warp_wait(ds_free, (j - 1) & 1, a.err, abort_flag);
+        if (!ok) break;
+      }
+      store_row64(smem + Q_OFF_DS, r, dp);
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(ds_full);
+    }
+    if (ok) ok = warp_wait(acc_done, 0, a.err, abort_flag);
+    tc_fence_after();
+    store_tmem_row(tmem + lane_off + 256, a.dqkv + ((long)q * a.batch + b) * 3L * a.heads * HD + q_col, a.scale, ok);
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+bool qkv_map(CUtensorMap* m, const void* base, int S, int batch, long cols, uint32_t rows) {
+  const uint64_t dims[3] = {(uint64_t)cols, (uint64_t)batch, (uint64_t)S};
+  const uint64_t strides[2] = {(uint64_t)cols * 2, (uint64_t)cols * 2 * batch};
+  const uint32_t box[3] = {64, 1, rows};
+  return make_tmap_bf16_3d(m, base, dims, strides, box);
+}
+
+}  // namespace
+
+cudaError_t flash_attn_bwd_tc(const __nv_bfloat16* dout, const __nv_bfloat16* qkv, const float* lse,
+                              const float* dvec, __nv_bfloat16* dqkv, int S, int batch, int heads, int head_dim,
+                              int* err, cudaStream_t stream) {
+  if (head_dim != HD || S % BIG != 0) return cudaErrorInvalidValue;
+  static bool configured = false;
+  if (!configured) {
+    cudaError_t e = cudaFuncSetAttribute(flash_bwd_dkdv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, KV_SMEM);
+    if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(flash_bwd_dq_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Q_SMEM);
+    if (e != cudaSuccess) return e;
+    configured = true;
+  }
+  const long cols = 3L * heads * HD;
+  CUtensorMap qkv_big, qkv_small, do_big, do_small;
+  if (!qkv_map(&qkv_big, qkv, S, batch, cols, BIG) || !qkv_map(&qkv_small, qkv, S, batch, cols, SMALL) ||
+      !qkv_map(&do_big, dout, S, batch, (long)heads * HD, BIG) ||
+      !qkv_map(&do_small, dout, S, batch, (long)heads * HD, SMALL))
+    return cudaErrorInvalidValue;
+  BwdArgs a{lse, dvec, dqkv, S, batch, heads, 1.0f / sqrtf((float)HD), err};
+  dim3 grid_kv(S / BIG, batch * heads);
+  flash_bwd_dkdv_kernel<<<grid_kv, THREADS, KV_SMEM, stream>>>(qkv_big, qkv_small, do_small, a);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  dim3 grid_q(S / BIG, batch * heads);
+  flash_bwd_dq_tc_kernel<<<grid_q, THREADS, Q_SMEM, stream>>>(qkv_big, qkv_small, do_big, a);
+  return cudaGetLastError();
+}
+
+}  // namespace nmb

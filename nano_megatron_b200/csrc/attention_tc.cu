@@ -45,28 +45,7 @@ constexpr int OFF_Q = 0, OFF_K = TILE, OFF_V = 3 * TILE, OFF_P = 5 * TILE, OFF_B
 constexpr int SMEM = 6 * TILE + 256 + 1024;
 constexpr int THREADS = 192;
 
-__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, int* err, volatile int* abort_flag) {
-  bool ok = true;
-  if ((threadIdx.x & 31) == 0) {
-    ok = !*abort_flag && mbar_wait(bar, parity, err);
-    if (!ok) *abort_flag = 1;
-  }
-  return __shfl_sync(0xffffffffu, ok, 0);
-}
-
-__device__ __forceinline__ bool lane_wait(uint64_t* bar, uint32_t parity, int* err, volatile int* abort_flag) {
-  if (*abort_flag) return false;
-  if (!mbar_wait(bar, parity, err)) {
-    *abort_flag = 1;
-    return false;
-  }
-  return true;
-}
-
-// K-major operand descriptor for k-step kk (16 elements) of a [2][128][64] tile.
-__device__ __forceinline__ uint64_t kmajor_desc(uint32_t base, int kk) {
-  return smem_desc_sw128(base + (kk >> 2) * HALF + (kk & 3) * 32, 0, 1024);
-}
+__device__ __forceinline__ uint64_t kmajor_desc(uint32_t base, int kk) { return nmb::kmajor_desc(base, kk, HALF); }
 
 __global__ void __launch_bounds__(THREADS, 1)
 flash_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_qkv, __nv_bfloat16* __restrict__ out,

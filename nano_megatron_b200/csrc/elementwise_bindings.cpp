@@ -193,6 +193,24 @@ at::Tensor flash_attn_bwd(const at::Tensor& dout, const at::Tensor& qkv, const a
   return dqkv;
 }
 
+at::Tensor flash_attn_bwd_tc(const at::Tensor& dout, const at::Tensor& qkv, const at::Tensor& out,
+                             const at::Tensor& lse, int64_t batch, int64_t heads, int64_t hd, const at::Tensor& err) {
+  need(dout, "dout"); need(qkv, "qkv"); need(out, "out"); need(lse, "lse");
+  TORCH_CHECK(dout.scalar_type() == at::kBFloat16 && qkv.scalar_type() == at::kBFloat16, "bf16 only");
+  const int S = qkv.size(0) / batch;
+  auto dqkv = at::empty_like(qkv);
+  auto dvec = at::empty({batch * heads * S}, qkv.options().dtype(at::kFloat));
+  const at::cuda::CUDAGuard g(qkv.device());
+  auto bf = [](const at::Tensor& t) { return reinterpret_cast<const __nv_bfloat16*>(t.data_ptr()); };
+  ok(nmb::flash_attn_bwd_dot(bf(dout), bf(out), dvec.data_ptr<float>(), S, batch, heads, stream()),
+     "flash_attn_bwd_dot");
+  ok(nmb::flash_attn_bwd_tc(bf(dout), bf(qkv), lse.data_ptr<float>(), dvec.data_ptr<float>(),
+                            reinterpret_cast<__nv_bfloat16*>(dqkv.data_ptr()), S, batch, heads, hd,
+                            err.data_ptr<int>(), stream()),
+     "flash_attn_bwd_tc");
+  return dqkv;
+}
+
 }  // namespace
 
 void register_elementwise(pybind11::module& m) {
@@ -213,4 +231,5 @@ void register_elementwise(pybind11::module& m) {
   m.def("flash_attn_fwd", &flash_attn_fwd);
   m.def("flash_attn_fwd_tc", &flash_attn_fwd_tc);
   m.def("flash_attn_bwd", &flash_attn_bwd);
+  m.def("flash_attn_bwd_tc", &flash_attn_bwd_tc);
 }

@@ -223,6 +223,33 @@ __host__ __device__ constexpr uint32_t idesc_bf16_f32(int m, int n, bool a_mn_ma
          ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
 }
 
+// Warp-uniform bounded wait: lane 0 polls, the result is broadcast so every
+// lane takes the same branch before warp-collective tcgen05 instructions.
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, int* err, volatile int* abort_flag) {
+  bool ok = true;
+  if ((threadIdx.x & 31) == 0) {
+    ok = !*abort_flag && mbar_wait(bar, parity, err);
+    if (!ok) *abort_flag = 1;
+  }
+  return __shfl_sync(0xffffffffu, ok, 0);
+}
+
+// Single-thread bounded wait that also gives up when another role aborted.
+__device__ __forceinline__ bool lane_wait(uint64_t* bar, uint32_t parity, int* err, volatile int* abort_flag) {
+  if (*abort_flag) return false;
+  if (!mbar_wait(bar, parity, err)) {
+    *abort_flag = 1;
+    return false;
+  }
+  return true;
+}
+
+// K-major 128B-swizzled operand stored as [2][rows][64] bf16 halves of `half`
+// bytes: descriptor of k-step kk (16 elements).
+__device__ __forceinline__ uint64_t kmajor_desc(uint32_t base, int kk, uint32_t half) {
+  return smem_desc_sw128(base + (kk >> 2) * half + (kk & 3) * 32, 0, 1024);
+}
+
 // ------------------------------------------------------------- conversions
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);

@@ -156,9 +156,12 @@ def attention(qkv, batch, heads, head_dim, cos, sin, inplace=False):
 
 def attention_bwd(do, saved, batch, heads, head_dim, cos, sin):
     qkv, o, lse = saved
-    dqkv = C.flash_attn_bwd(do.contiguous(), qkv, o, lse, batch, heads, head_dim)
+    if (qkv.shape[0] // batch) % 128 == 0:
+        dqkv = C.flash_attn_bwd_tc(do.contiguous(), qkv, o, lse, batch, heads, head_dim, status_word(qkv.device))
+    else:
+        dqkv = C.flash_attn_bwd(do.contiguous(), qkv, o, lse, batch, heads, head_dim)
     C.rope_inplace(dqkv, cos, sin, batch, heads, head_dim, -1.0)
-    _count(4)
+    _count(4 if (qkv.shape[0] // batch) % 128 == 0 else 4)
     return dqkv
 
 

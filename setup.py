@@ -21,6 +21,7 @@ SOURCES = [
     "kernels.cu",
     "attention.cu",
     "attention_tc.cu",
+    "attention_bwd_tc.cu",
     "fused_tp.cu",
     "noalloc.cu",
 ]

@@ -70,3 +70,20 @@ def test_tcgen05_forward_matches_mma_sync_forward(S, b, h):
     KC.check_status(DEV)
     assert _rel(o2, o1) < 1e-2, _rel(o2, o1)
     torch.testing.assert_close(l2, l1, rtol=1e-4, atol=1e-4)
+
+
+@pytest.mark.parametrize("S,b,h", [(128, 1, 1), (512, 2, 2), (2048, 1, 3)])
+def test_tcgen05_backward_matches_mma_sync_backward(S, b, h):
+    """The tcgen05 backward (dK/dV + dQ kernels) and the mma.sync backward agree."""
+    from nano_megatron_b200 import _C
+    torch.manual_seed(S + h)
+    qkv = torch.randn(S * b, 3 * h * 128, device=DEV).bfloat16()
+    o, lse = _C.flash_attn_fwd(qkv, b, h, 128)
+    do = torch.randn(S * b, h * 128, device=DEV).bfloat16()
+    d1 = _C.flash_attn_bwd(do, qkv, o, lse, b, h, 128)
+    d2 = _C.flash_attn_bwd_tc(do, qkv, o, lse, b, h, 128, KC.status_word(DEV))
+    KC.check_status(DEV)
+    for i, name in enumerate("qkv"):
+        a_ = d1.view(S * b, 3, -1)[:, i]
+        b_ = d2.view(S * b, 3, -1)[:, i]
+        assert _rel(b_, a_) < 2e-2, (name, _rel(b_, a_))
