@@ -89,6 +89,9 @@ __device__ __forceinline__ void store_tmem_row(uint32_t taddr, __nv_bfloat16* ds
   }
 }
 
+// Named barrier over the 128 threads of warps 2-5.
+__device__ __forceinline__ void epilogue_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
 struct BwdArgs {
   const float* lse;   // [batch*heads, S]
   const float* dvec;  // [batch*heads, S]
@@ -102,7 +105,7 @@ struct BwdArgs {
 // smem: K 32K | V 32K | Q[2] 2x16K | dO[2] 2x16K | P^T 16K | dS^T 16K
 constexpr int KV_OFF_K = 0, KV_OFF_V = TILE_BIG, KV_OFF_Q = 2 * TILE_BIG, KV_OFF_DO = KV_OFF_Q + 2 * TILE_SMALL,
               KV_OFF_PT = KV_OFF_DO + 2 * TILE_SMALL, KV_OFF_DST = KV_OFF_PT + BIG * 128,
-              KV_OFF_BAR = KV_OFF_DST + BIG * 128;
+              KV_OFF_LD = KV_OFF_DST + BIG * 128, KV_OFF_BAR = KV_OFF_LD + 2 * 2 * SMALL * 4;
 constexpr int KV_SMEM = KV_OFF_BAR + 256 + 1024;
 
 __global__ void __launch_bounds__(THREADS, 1)
@@ -223,28 +226,41 @@ flash_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tm_qkv_big, const __gr
     const float* dvec = a.dvec + (long)bh * a.S;
     const float sl2 = a.scale * LOG2E;
     bool ok = true;
-    for (int i = 0; i < nblk && ok; ++i) {
+    // No early exit from this loop: the named barrier needs all 128 threads
+    // every iteration, so after an abort the remaining iterations only sync.
+    for (int i = 0; i < nblk; ++i) {
       const int st = i & 1;
       const int q0 = (first_qb + i) * SMALL;
-      ok = warp_wait(&st_full[st], (i >> 1) & 1, a.err, abort_flag);
-      if (!ok) break;
+      // this block's lse*log2(e) and D, staged once in shared memory (double buffered)
+      float* lse_s = reinterpret_cast<float*>(smem + KV_OFF_LD) + st * 2 * SMALL;
+      float* d_s = lse_s + SMALL;
+      if (r < SMALL) lse_s[r] = lse[q0 + r] * LOG2E;
+      else d_s[r - SMALL] = dvec[q0 + r - SMALL];
+      epilogue_sync();
+      if (ok) ok = warp_wait(&st_full[st], (i >> 1) & 1, a.err, abort_flag);
+      if (!ok) continue;
       tc_fence_after();
       float s[SMALL], dp[SMALL];
       ld_row64(tmem + lane_off + st * SMALL, s);
       ld_row64(tmem + lane_off + 128 + st * SMALL, dp);
       tc_fence_before();
       mbar_arrive(&st_free[st]);
+      const bool diagonal = q0 < kb * BIG + BIG;  // some key of this block is after some query
 #pragma unroll
-      for (int c = 0; c < SMALL; ++c) {
-        const int q = q0 + c;
-        const float pr = (key > q) ? 0.f : exp2f(s[c] * sl2 - __ldg(lse + q) * LOG2E);
-        s[c] = pr;
-        dp[c] = pr * (dp[c] - __ldg(dvec + q));
+      for (int c = 0; c < SMALL; c += 4) {
+        const float4 l4 = *reinterpret_cast<const float4*>(lse_s + c);
+        const float4 d4 = *reinterpret_cast<const float4*>(d_s + c);
+        const float lv[4] = {l4.x, l4.y, l4.z, l4.w}, dv[4] = {d4.x, d4.y, d4.z, d4.w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          float pr = fast_exp2(fmaf(s[c + k], sl2, -lv[k]));
+          if (diagonal && key > q0 + c + k) pr = 0.f;
+          s[c + k] = pr;
+          dp[c + k] = pr * (dp[c + k] - dv[k]);
+        }
       }
-      if (i > 0) {
-        ok = warp_wait(pds_free, (i - 1) & 1, a.err, abort_flag);
-        if (!ok) break;
-      }
+      if (i > 0) ok = warp_wait(pds_free, (i - 1) & 1, a.err, abort_flag);
+      if (!ok) continue;
       store_row64(smem + KV_OFF_PT, r, s);
       store_row64(smem + KV_OFF_DST, r, dp);
       fence_proxy_async_smem();
@@ -396,10 +412,11 @@ flash_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tm_qkv_big, const __g
       ld_row64(tmem + lane_off + 128 + st * SMALL, dp);
       tc_fence_before();
       mbar_arrive(&s_free[st]);
+      const bool diagonal = j * SMALL + SMALL > qb * BIG;
 #pragma unroll
       for (int c = 0; c < SMALL; ++c) {
-        const int key = j * SMALL + c;
-        const float pr = (key > q) ? 0.f : exp2f(s[c] * sl2 - lse2);
+        float pr = fast_exp2(fmaf(s[c], sl2, -lse2));
+        if (diagonal && j * SMALL + c > q) pr = 0.f;
         dp[c] = pr * (dp[c] - dq);
       }
       if (j > 0) {

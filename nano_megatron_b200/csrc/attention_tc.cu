@@ -183,18 +183,24 @@ flash_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_qkv, __nv_bfloat16* _
         for (int c = 0; c < TK; ++c)
           if (c > r) s[c] = -INFINITY;
       }
-      float mx = s[0];
+      float mx0 = s[0], mx1 = s[1];
 #pragma unroll
-      for (int c = 1; c < TK; ++c) mx = fmaxf(mx, s[c]);
-      const float m_new = fmaxf(m, mx);
-      const float alpha = exp2f((m - m_new) * scale_log2);
-      const float ms = m_new * scale_log2;
-      float sum = 0.f;
-#pragma unroll
-      for (int c = 0; c < TK; ++c) {
-        s[c] = exp2f(s[c] * scale_log2 - ms);
-        sum += s[c];
+      for (int c = 2; c < TK; c += 2) {
+        mx0 = fmaxf(mx0, s[c]);
+        mx1 = fmaxf(mx1, s[c + 1]);
       }
+      const float m_new = fmaxf(m, fmaxf(mx0, mx1));
+      const float alpha = fast_exp2((m - m_new) * scale_log2);
+      const float ms = m_new * scale_log2;
+      float sum0 = 0.f, sum1 = 0.f;
+#pragma unroll
+      for (int c = 0; c < TK; c += 2) {
+        s[c] = fast_exp2(fmaf(s[c], scale_log2, -ms));
+        s[c + 1] = fast_exp2(fmaf(s[c + 1], scale_log2, -ms));
+        sum0 += s[c];
+        sum1 += s[c + 1];
+      }
+      const float sum = sum0 + sum1;
       l = l * alpha + sum;
       m = m_new;
       if (j > 0) {

@@ -250,6 +250,14 @@ __device__ __forceinline__ uint64_t kmajor_desc(uint32_t base, int kk, uint32_t 
   return smem_desc_sw128(base + (kk >> 2) * half + (kk & 3) * 32, 0, 1024);
 }
 
+// 2^x with the SFU's approximate exp2 (flushes denormal results to zero); the
+// attention kernels feed it pre-scaled scores, where that precision suffices.
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 // ------------------------------------------------------------- conversions
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
