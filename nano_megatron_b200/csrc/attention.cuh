@@ -24,8 +24,9 @@ cudaError_t flash_attn_bwd(const __nv_bfloat16* dout, const __nv_bfloat16* qkv, 
 cudaError_t flash_attn_bwd_dot(const __nv_bfloat16* dout, const __nv_bfloat16* out, float* dvec, int S, int batch,
                                int heads, cudaStream_t stream);
 
-// tcgen05 backward (dK/dV kernel + dQ kernel, no atomics); needs dvec from
-// flash_attn_bwd_dot; S must be a multiple of 128.
+// tcgen05 backward (dK/dV kernel + dQ kernel, no atomics); dvec holds
+// [2][batch*heads*S] floats: D from flash_attn_bwd_dot, then scratch for
+// lse*log2(e); S must be a multiple of 128.
 cudaError_t flash_attn_bwd_tc(const __nv_bfloat16* dout, const __nv_bfloat16* qkv, const float* lse,
                               const float* dvec, __nv_bfloat16* dqkv, int S, int batch, int heads, int head_dim,
                               int* err, cudaStream_t stream);

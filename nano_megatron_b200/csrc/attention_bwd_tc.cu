@@ -94,6 +94,7 @@ __device__ __forceinline__ void epilogue_sync() { asm volatile("bar.sync 1, 128;
 
 struct BwdArgs {
   const float* lse;   // [batch*heads, S]
+  const float* lse2;  // lse * log2(e), [batch*heads, S]
   const float* dvec;  // [batch*heads, S]
   __nv_bfloat16* dqkv;
   int S, batch, heads;
@@ -102,27 +103,34 @@ struct BwdArgs {
 };
 
 // ============================================================ dK / dV kernel
-// smem: K 32K | V 32K | Q[2] 2x16K | dO[2] 2x16K | P^T 16K | dS^T 16K
-constexpr int KV_OFF_K = 0, KV_OFF_V = TILE_BIG, KV_OFF_Q = 2 * TILE_BIG, KV_OFF_DO = KV_OFF_Q + 2 * TILE_SMALL,
-              KV_OFF_PT = KV_OFF_DO + 2 * TILE_SMALL, KV_OFF_DST = KV_OFF_PT + BIG * 128,
-              KV_OFF_LD = KV_OFF_DST + BIG * 128, KV_OFF_BAR = KV_OFF_LD + 2 * 2 * SMALL * 4;
+// Two elementwise warpgroups (warps 2-5 and 6-9) take alternate 64-query
+// blocks, each with its own S^T/dP^T TMEM columns and P^T/dS^T smem tiles, so
+// one group's exp/convert work overlaps the tensor core's work for the other.
+// smem: K 32K | V 32K | Q[3] 3x16K | dO[3] 3x16K | P^T[2] 2x16K | dS^T[2] 2x16K | lse2,D[3]
+// (lse2 = lse * log2(e) and D of a query block travel with its Q/dO stage)
+constexpr int KV_THREADS = 320;
+constexpr int KV_STAGES = 3;
+constexpr int KV_OFF_K = 0, KV_OFF_V = TILE_BIG, KV_OFF_Q = 2 * TILE_BIG,
+              KV_OFF_DO = KV_OFF_Q + KV_STAGES * TILE_SMALL, KV_OFF_PT = KV_OFF_DO + KV_STAGES * TILE_SMALL,
+              KV_OFF_DST = KV_OFF_PT + 2 * BIG * 128,
+              KV_OFF_LD = KV_OFF_DST + 2 * BIG * 128, KV_OFF_BAR = KV_OFF_LD + KV_STAGES * 2 * SMALL * 4;
 constexpr int KV_SMEM = KV_OFF_BAR + 256 + 1024;
 
-__global__ void __launch_bounds__(THREADS, 1)
+__global__ void __launch_bounds__(KV_THREADS, 1)
 flash_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tm_qkv_big, const __grid_constant__ CUtensorMap tm_qkv_small,
                       const __grid_constant__ CUtensorMap tm_do_small, const BwdArgs a) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + KV_OFF_BAR);
   uint64_t* kv_full = bars;         // K and V
-  uint64_t* qdo_full = bars + 1;    // [2]
-  uint64_t* qdo_empty = bars + 3;   // [2]
-  uint64_t* st_full = bars + 5;     // [2] S^T and dP^T of a block
-  uint64_t* st_free = bars + 7;     // [2]
-  uint64_t* pds_full = bars + 9;    // P^T and dS^T in smem
-  uint64_t* pds_free = bars + 10;
-  uint64_t* acc_done = bars + 11;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+  uint64_t* qdo_full = bars + 1;    // [3] Q/dO stage i % 3
+  uint64_t* qdo_empty = bars + 4;   // [3]
+  uint64_t* st_full = bars + 7;     // [2] per group: S^T and dP^T ready
+  uint64_t* st_free = bars + 9;     // [2] per group: S^T and dP^T read
+  uint64_t* pds_full = bars + 11;   // [2] per group: P^T and dS^T in smem
+  uint64_t* pds_free = bars + 13;   // [2] per group: dV/dK products done with them
+  uint64_t* acc_done = bars + 15;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
@@ -134,14 +142,16 @@ flash_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tm_qkv_big, const __gr
 
   if (threadIdx.x == 0) {
     mbar_init(kv_full, 1);
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < KV_STAGES; ++i) {
       mbar_init(&qdo_full[i], 1);
       mbar_init(&qdo_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
       mbar_init(&st_full[i], 1);
       mbar_init(&st_free[i], 128);
+      mbar_init(&pds_full[i], 128);
+      mbar_init(&pds_free[i], 1);
     }
-    mbar_init(pds_full, 128);
-    mbar_init(pds_free, 1);
     mbar_init(acc_done, 1);
     *abort_flag = 0;
     fence_barrier_init();
@@ -153,98 +163,119 @@ flash_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tm_qkv_big, const __gr
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const uint32_t tmem = *tmem_slot;  // S^T [0,64)+[64,128), dP^T [128,192)+[192,256), dV 256, dK 384
+  // TMEM columns: S^T of group g at 64g, dP^T of group g at 128 + 64g, dV 256, dK 384
+  const uint32_t tmem = *tmem_slot;
   const uint32_t sbase = smem_u32(smem);
 
   if (warp == 0 && lane == 0) {
-    int issued[2] = {-1, -1};
+    int issued[KV_STAGES] = {-1, -1, -1};
     mbar_arrive_expect_tx(kv_full, 2 * TILE_BIG);
     tma_load_3d(smem + KV_OFF_K, &tm_qkv_big, kv_full, k_col, b, kb * BIG);
     tma_load_3d(smem + KV_OFF_K + HALF_BIG, &tm_qkv_big, kv_full, k_col + 64, b, kb * BIG);
     tma_load_3d(smem + KV_OFF_V, &tm_qkv_big, kv_full, v_col, b, kb * BIG);
     tma_load_3d(smem + KV_OFF_V + HALF_BIG, &tm_qkv_big, kv_full, v_col + 64, b, kb * BIG);
     for (int i = 0; i < nblk; ++i) {
-      const int st = i & 1;
-      if (!lane_wait(&qdo_empty[st], ((i >> 1) & 1) ^ 1, a.err, abort_flag)) break;
+      const int st = i % KV_STAGES;
+      if (!lane_wait(&qdo_empty[st], ((i / KV_STAGES) & 1) ^ 1, a.err, abort_flag)) break;
       const int q0 = (first_qb + i) * SMALL;
       uint8_t* qd = smem + KV_OFF_Q + st * TILE_SMALL;
       uint8_t* dd = smem + KV_OFF_DO + st * TILE_SMALL;
-      mbar_arrive_expect_tx(&qdo_full[st], 2 * TILE_SMALL);
+      mbar_arrive_expect_tx(&qdo_full[st], 2 * TILE_SMALL + 2 * SMALL * 4);
+      float* ld_dst = reinterpret_cast<float*>(smem + KV_OFF_LD) + st * 2 * SMALL;
+      bulk_load(ld_dst, a.lse2 + (long)bh * a.S + q0, SMALL * 4, &qdo_full[st]);
+      bulk_load(ld_dst + SMALL, a.dvec + (long)bh * a.S + q0, SMALL * 4, &qdo_full[st]);
       tma_load_3d(qd, &tm_qkv_small, &qdo_full[st], q_col, b, q0);
       tma_load_3d(qd + HALF_SMALL, &tm_qkv_small, &qdo_full[st], q_col + 64, b, q0);
       tma_load_3d(dd, &tm_do_small, &qdo_full[st], do_col, b, q0);
       tma_load_3d(dd + HALF_SMALL, &tm_do_small, &qdo_full[st], do_col + 64, b, q0);
-      issued[st] = (i >> 1) & 1;
+      issued[st] = (i / KV_STAGES) & 1;
     }
     mbar_wait(kv_full, 0, nullptr, 1000000000ull);
-    for (int st = 0; st < 2; ++st)
+    for (int st = 0; st < KV_STAGES; ++st)
       if (issued[st] >= 0) mbar_wait(&qdo_full[st], issued[st], nullptr, 1000000000ull);
   } else if (warp == 1 && lane == 0) {
+    // Event loop: issue the S^T/dP^T products of block `ns` as soon as its
+    // group's TMEM columns are free and its Q/dO stage has landed, and the
+    // dV/dK products of block `na` as soon as its group has published P^T/dS^T,
+    // whichever is ready first; never more than one block ahead per group.
     constexpr uint32_t idesc_t = idesc_bf16_f32(BIG, SMALL, false, false);  // S^T, dP^T
     constexpr uint32_t idesc_acc = idesc_bf16_f32(BIG, HD, false, true);    // dV, dK
     bool ok = lane_wait(kv_full, 0, a.err, abort_flag);
-    for (int i = 0; ok && i <= nblk; ++i) {
-      if (i < nblk) {
-        const int st = i & 1;
-        if (!lane_wait(&qdo_full[st], (i >> 1) & 1, a.err, abort_flag)) break;
-        if (!lane_wait(&st_free[st], ((i >> 1) & 1) ^ 1, a.err, abort_flag)) break;
-        tc_fence_after();
-        const uint32_t qs = sbase + KV_OFF_Q + st * TILE_SMALL, ds = sbase + KV_OFF_DO + st * TILE_SMALL;
+    int ns = 0, na = 0;
+    uint64_t idle_since = 0;
+    while (ok && na < nblk) {
+      bool progressed = false;
+      if (ns < nblk && ns < na + 2) {
+        const int g = ns & 1, st = ns % KV_STAGES;
+        if (mbar_try_wait(&qdo_full[st], (ns / KV_STAGES) & 1) && mbar_try_wait(&st_free[g], ((ns >> 1) & 1) ^ 1)) {
+          tc_fence_after();
+          const uint32_t qs = sbase + KV_OFF_Q + st * TILE_SMALL, ds = sbase + KV_OFF_DO + st * TILE_SMALL;
 #pragma unroll
-        for (int kk = 0; kk < HD / 16; ++kk) {
-          mma_bf16_ss(tmem + st * SMALL, kmajor_desc(sbase + KV_OFF_K, kk, HALF_BIG), kmajor_desc(qs, kk, HALF_SMALL),
-                      idesc_t, kk > 0);
-          mma_bf16_ss(tmem + 128 + st * SMALL, kmajor_desc(sbase + KV_OFF_V, kk, HALF_BIG),
-                      kmajor_desc(ds, kk, HALF_SMALL), idesc_t, kk > 0);
+          for (int kk = 0; kk < HD / 16; ++kk) {
+            mma_bf16_ss(tmem + g * SMALL, kmajor_desc(sbase + KV_OFF_K, kk, HALF_BIG),
+                        kmajor_desc(qs, kk, HALF_SMALL), idesc_t, kk > 0);
+            mma_bf16_ss(tmem + 128 + g * SMALL, kmajor_desc(sbase + KV_OFF_V, kk, HALF_BIG),
+                        kmajor_desc(ds, kk, HALF_SMALL), idesc_t, kk > 0);
+          }
+          mma_commit(&st_full[g]);
+          ++ns;
+          progressed = true;
         }
-        mma_commit(&st_full[st]);
       }
-      if (i >= 1) {
-        const int p = i - 1, st = p & 1;
-        if (!lane_wait(pds_full, p & 1, a.err, abort_flag)) break;
-        tc_fence_after();
-        const uint32_t qs = sbase + KV_OFF_Q + st * TILE_SMALL, ds = sbase + KV_OFF_DO + st * TILE_SMALL;
+      if (na < ns) {
+        const int g = na & 1, st = na % KV_STAGES;
+        if (mbar_try_wait(&pds_full[g], (na >> 1) & 1)) {
+          tc_fence_after();
+          const uint32_t qs = sbase + KV_OFF_Q + st * TILE_SMALL, ds = sbase + KV_OFF_DO + st * TILE_SMALL;
+          const uint32_t pt = sbase + KV_OFF_PT + g * BIG * 128, dst = sbase + KV_OFF_DST + g * BIG * 128;
 #pragma unroll
-        for (int kk = 0; kk < SMALL / 16; ++kk) {
-          // B = dO / Q block viewed N-major: [2 d-halves][64 q rows][128 B]
-          mma_bf16_ss(tmem + 256, smem_desc_sw128(sbase + KV_OFF_PT + kk * 32, 0, 1024),
-                      smem_desc_sw128(ds + kk * 2048, HALF_SMALL, 1024), idesc_acc, (p > 0 || kk > 0));
-          mma_bf16_ss(tmem + 384, smem_desc_sw128(sbase + KV_OFF_DST + kk * 32, 0, 1024),
-                      smem_desc_sw128(qs + kk * 2048, HALF_SMALL, 1024), idesc_acc, (p > 0 || kk > 0));
+          for (int kk = 0; kk < SMALL / 16; ++kk) {
+            // B = dO / Q block viewed N-major: [2 d-halves][64 q rows][128 B]
+            mma_bf16_ss(tmem + 256, smem_desc_sw128(pt + kk * 32, 0, 1024),
+                        smem_desc_sw128(ds + kk * 2048, HALF_SMALL, 1024), idesc_acc, (na > 0 || kk > 0));
+            mma_bf16_ss(tmem + 384, smem_desc_sw128(dst + kk * 32, 0, 1024),
+                        smem_desc_sw128(qs + kk * 2048, HALF_SMALL, 1024), idesc_acc, (na > 0 || kk > 0));
+          }
+          mma_commit(&pds_free[g]);
+          mma_commit(&qdo_empty[st]);
+          ++na;
+          progressed = true;
         }
-        mma_commit(pds_free);
-        mma_commit(&qdo_empty[st]);
+      }
+      if (progressed) {
+        idle_since = 0;
+      } else if (idle_since == 0) {
+        idle_since = globaltimer_ns();
+      } else if (*abort_flag || globaltimer_ns() - idle_since > 2000000000ull) {
+        report_error(a.err, kBarrierTimeout);
+        *abort_flag = 1;
+        ok = false;
       }
     }
     mma_commit(acc_done);
   } else if (warp >= 2) {
-    const int quarter = warp & 3;
+    const int g = (warp - 2) / 4;   // elementwise group
+    const int quarter = warp & 3;   // TMEM lane quarter this warp may access
     const int r = quarter * 32 + lane;  // key row within the block
     const int key = kb * BIG + r;
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
-    const float* lse = a.lse + (long)bh * a.S;
-    const float* dvec = a.dvec + (long)bh * a.S;
     const float sl2 = a.scale * LOG2E;
+    uint8_t* pt_tile = smem + KV_OFF_PT + g * BIG * 128;
+    uint8_t* dst_tile = smem + KV_OFF_DST + g * BIG * 128;
     bool ok = true;
-    // No early exit from this loop: the named barrier needs all 128 threads
-    // every iteration, so after an abort the remaining iterations only sync.
-    for (int i = 0; i < nblk; ++i) {
-      const int st = i & 1;
+    for (int i = g, n = 0; i < nblk && ok; i += 2, ++n) {
       const int q0 = (first_qb + i) * SMALL;
-      // this block's lse*log2(e) and D, staged once in shared memory (double buffered)
-      float* lse_s = reinterpret_cast<float*>(smem + KV_OFF_LD) + st * 2 * SMALL;
-      float* d_s = lse_s + SMALL;
-      if (r < SMALL) lse_s[r] = lse[q0 + r] * LOG2E;
-      else d_s[r - SMALL] = dvec[q0 + r - SMALL];
-      epilogue_sync();
-      if (ok) ok = warp_wait(&st_full[st], (i >> 1) & 1, a.err, abort_flag);
-      if (!ok) continue;
+      // the block's lse2 and D arrived with its Q/dO stage (complete before S^T was issued)
+      const float* lse_s = reinterpret_cast<const float*>(smem + KV_OFF_LD) + (i % KV_STAGES) * 2 * SMALL;
+      const float* d_s = lse_s + SMALL;
+      ok = warp_wait(&st_full[g], n & 1, a.err, abort_flag);
+      if (!ok) break;
       tc_fence_after();
       float s[SMALL], dp[SMALL];
-      ld_row64(tmem + lane_off + st * SMALL, s);
-      ld_row64(tmem + lane_off + 128 + st * SMALL, dp);
+      ld_row64(tmem + lane_off + g * SMALL, s);
+      ld_row64(tmem + lane_off + 128 + g * SMALL, dp);
       tc_fence_before();
-      mbar_arrive(&st_free[st]);
+      mbar_arrive(&st_free[g]);
       const bool diagonal = q0 < kb * BIG + BIG;  // some key of this block is after some query
 #pragma unroll
       for (int c = 0; c < SMALL; c += 4) {
@@ -259,20 +290,20 @@ flash_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tm_qkv_big, const __gr
           dp[c + k] = pr * (dp[c + k] - dv[k]);
         }
       }
-      if (i > 0) ok = warp_wait(pds_free, (i - 1) & 1, a.err, abort_flag);
-      if (!ok) continue;
-      store_row64(smem + KV_OFF_PT, r, s);
-      store_row64(smem + KV_OFF_DST, r, dp);
+      if (n > 0) ok = warp_wait(&pds_free[g], (n - 1) & 1, a.err, abort_flag);
+      if (!ok) break;
+      store_row64(pt_tile, r, s);
+      store_row64(dst_tile, r, dp);
       fence_proxy_async_smem();
       tc_fence_before();
-      mbar_arrive(pds_full);
+      mbar_arrive(&pds_full[g]);
     }
     if (ok) ok = warp_wait(acc_done, 0, a.err, abort_flag);
     tc_fence_after();
     const long ld = 3L * a.heads * HD;
     __nv_bfloat16* row = a.dqkv + ((long)key * a.batch + b) * ld;
-    store_tmem_row(tmem + lane_off + 256, row + v_col, 1.f, ok);     // dV
-    store_tmem_row(tmem + lane_off + 384, row + k_col, a.scale, ok);  // dK
+    if (g == 0) store_tmem_row(tmem + lane_off + 256, row + v_col, 1.f, ok);      // dV
+    else store_tmem_row(tmem + lane_off + 384, row + k_col, a.scale, ok);         // dK
   }
 
   tc_fence_before();
@@ -441,6 +472,11 @@ flash_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tm_qkv_big, const __g
   }
 }
 
+__global__ void scale_kernel(const float* __restrict__ x, float* __restrict__ y, long n, float s) {
+  const long i = blockIdx.x * (long)blockDim.x + threadIdx.x;
+  if (i < n) y[i] = x[i] * s;
+}
+
 bool qkv_map(CUtensorMap* m, const void* base, int S, int batch, long cols, uint32_t rows) {
   const uint64_t dims[3] = {(uint64_t)cols, (uint64_t)batch, (uint64_t)S};
   const uint64_t strides[2] = {(uint64_t)cols * 2, (uint64_t)cols * 2 * batch};
@@ -468,9 +504,14 @@ cudaError_t flash_attn_bwd_tc(const __nv_bfloat16* dout, const __nv_bfloat16* qk
       !qkv_map(&do_big, dout, S, batch, (long)heads * HD, BIG) ||
       !qkv_map(&do_small, dout, S, batch, (long)heads * HD, SMALL))
     return cudaErrorInvalidValue;
-  BwdArgs a{lse, dvec, dqkv, S, batch, heads, 1.0f / sqrtf((float)HD), err};
+  // lse2 = lse * log2(e) is written into the second half of the dvec scratch
+  // ([2][batch*heads*S] floats, allocated by the caller).
+  const long rows = (long)batch * heads * S;
+  float* lse2 = const_cast<float*>(dvec) + rows;
+  scale_kernel<<<(int)((rows + 255) / 256), 256, 0, stream>>>(lse, lse2, rows, LOG2E);
+  BwdArgs a{lse, lse2, dvec, dqkv, S, batch, heads, 1.0f / sqrtf((float)HD), err};
   dim3 grid_kv(S / BIG, batch * heads);
-  flash_bwd_dkdv_kernel<<<grid_kv, THREADS, KV_SMEM, stream>>>(qkv_big, qkv_small, do_small, a);
+  flash_bwd_dkdv_kernel<<<grid_kv, KV_THREADS, KV_SMEM, stream>>>(qkv_big, qkv_small, do_small, a);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   dim3 grid_q(S / BIG, batch * heads);

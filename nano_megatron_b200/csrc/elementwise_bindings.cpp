@@ -5,6 +5,7 @@
 #include <torch/extension.h>
 
 #include "attention.cuh"
+#include "fp32.cuh"
 #include "kernels.cuh"
 
 namespace {
@@ -199,7 +200,7 @@ at::Tensor flash_attn_bwd_tc(const at::Tensor& dout, const at::Tensor& qkv, cons
   TORCH_CHECK(dout.scalar_type() == at::kBFloat16 && qkv.scalar_type() == at::kBFloat16, "bf16 only");
   const int S = qkv.size(0) / batch;
   auto dqkv = at::empty_like(qkv);
-  auto dvec = at::empty({batch * heads * S}, qkv.options().dtype(at::kFloat));
+  auto dvec = at::empty({2 * batch * heads * S}, qkv.options().dtype(at::kFloat));  // D | lse*log2(e)
   const at::cuda::CUDAGuard g(qkv.device());
   auto bf = [](const at::Tensor& t) { return reinterpret_cast<const __nv_bfloat16*>(t.data_ptr()); };
   ok(nmb::flash_attn_bwd_dot(bf(dout), bf(out), dvec.data_ptr<float>(), S, batch, heads, stream()),
@@ -209,6 +210,35 @@ at::Tensor flash_attn_bwd_tc(const at::Tensor& dout, const at::Tensor& qkv, cons
                             err.data_ptr<int>(), stream()),
      "flash_attn_bwd_tc");
   return dqkv;
+}
+
+// fp32 GEMM on strided views: C (+)= op(A) op(B); A is [M,K] (or [K,M] with
+// a_t), B is [K,N] (or [N,K] with b_t). Any element strides.
+void gemm_f32(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, bool a_t, bool b_t, double beta) {
+  TORCH_CHECK(A.is_cuda() && B.is_cuda() && C.is_cuda(), "CUDA tensors");
+  TORCH_CHECK(A.scalar_type() == at::kFloat && B.scalar_type() == at::kFloat && C.scalar_type() == at::kFloat,
+              "fp32 only");
+  const int M = a_t ? A.size(1) : A.size(0), K = a_t ? A.size(0) : A.size(1);
+  const int N = b_t ? B.size(0) : B.size(1);
+  TORCH_CHECK((b_t ? B.size(1) : B.size(0)) == K && C.size(0) == M && C.size(1) == N && C.stride(1) == 1, "shapes");
+  const long sam = a_t ? A.stride(1) : A.stride(0), sak = a_t ? A.stride(0) : A.stride(1);
+  const long sbk = b_t ? B.stride(1) : B.stride(0), sbn = b_t ? B.stride(0) : B.stride(1);
+  ok(nmb::gemm_f32(M, N, K, A.data_ptr<float>(), sam, sak, B.data_ptr<float>(), sbk, sbn, C.data_ptr<float>(),
+                   C.stride(0), (float)beta, stream()),
+     "gemm_f32");
+}
+
+void causal_softmax_f32(const at::Tensor& S, at::Tensor& P, double scale) {
+  need(S, "S"); need(P, "P");
+  ok(nmb::causal_softmax_f32(S.data_ptr<float>(), P.data_ptr<float>(), S.size(0), (float)scale, stream()),
+     "causal_softmax_f32");
+}
+
+void softmax_bwd_f32(const at::Tensor& P, const at::Tensor& dP, at::Tensor& dS, double scale) {
+  need(P, "P"); need(dP, "dP"); need(dS, "dS");
+  ok(nmb::softmax_bwd_f32(P.data_ptr<float>(), dP.data_ptr<float>(), dS.data_ptr<float>(), P.size(0), (float)scale,
+                          stream()),
+     "softmax_bwd_f32");
 }
 
 }  // namespace
@@ -228,6 +258,9 @@ void register_elementwise(pybind11::module& m) {
   m.def("ce_grad", &ce_grad);
   m.def("adamw_flat", &adamw_flat);
   m.def("weighted_sq_norm", &weighted_sq_norm);
+  m.def("gemm_f32", &gemm_f32);
+  m.def("causal_softmax_f32", &causal_softmax_f32);
+  m.def("softmax_bwd_f32", &softmax_bwd_f32);
   m.def("flash_attn_fwd", &flash_attn_fwd);
   m.def("flash_attn_fwd_tc", &flash_attn_fwd_tc);
   m.def("flash_attn_bwd", &flash_attn_bwd);

@@ -4,10 +4,10 @@ Importing this module loads ``nano_megatron_b200/_C*.so`` and raises if it is
 missing or was not built for this GPU: there is no silent fallback to
 PyTorch kernels on the CUDA path.
 
-GEMMs run the tcgen05 kernel of ``csrc/gemm.cu`` in bf16. fp32 GEMMs (the
-reference's ``--dtype float32`` path) run the exact-fp32 SIMT kernel of
-``csrc/attention.cu``'s companion (``gemm_f32``) when built; bf16 is the
-performance path.
+GEMMs run the tcgen05 kernel of ``csrc/gemm.cu`` in bf16. The reference's
+``--dtype float32`` mode runs the exact-fp32 SIMT kernels of ``csrc/fp32.cu``
+(strided GEMM, materialized causal softmax attention): correct to fp32
+tolerances, not fast; bf16 is the performance path.
 """
 
 from __future__ import annotations
@@ -73,9 +73,15 @@ def _gemm(a, b, c, a_mn, b_mn, out_mode):
     _count()
 
 
-def _f32_gemm(a, b, a_t, b_t):
-    """Exact fp32 product via the SIMT fp32 GEMM kernel."""
-    return C.gemm_f32(a, b, a_t, b_t)
+def _f32_gemm(a, b, a_t, b_t, out=None, beta=0.0):
+    """Exact fp32 ``op(a) @ op(b)`` (SIMT FMA kernel, no TF32), optionally ``+= out``."""
+    m = a.shape[1] if a_t else a.shape[0]
+    n = b.shape[0] if b_t else b.shape[1]
+    if out is None:
+        out = torch.empty((m, n), dtype=torch.float32, device=a.device)
+    C.gemm_f32(a, b, out, a_t, b_t, beta)
+    _count()
+    return out
 
 
 def mm_nn(a, b):
@@ -99,7 +105,7 @@ def mm_nt(a, b):
 def mm_tn_acc(a, b, out):
     """``out[K,N] += a[M,K]^T @ b[M,N]`` (fp32 ``out``)."""
     if a.dtype == torch.float32:
-        out.add_(_f32_gemm(a, b, True, False))
+        _f32_gemm(a, b, True, False, out=out, beta=1.0)
         return
     if out.stride(-1) != 1:
         raise ValueError("accumulator must have unit inner stride")
@@ -141,9 +147,59 @@ def rmsnorm_bwd(dy, x, weight, rstd, wgrad_out):
 
 
 # ---------------------------------------------------------------- attention
+def _attention_f32(qkv, batch, heads, head_dim, cos, sin):
+    """fp32 causal attention, materialized per (batch, head) with the fp32 kernels."""
+    qkv = qkv.clone(memory_format=torch.contiguous_format)
+    C.rope_inplace(qkv, cos, sin, batch, heads, head_dim, 1.0)
+    s = qkv.shape[0] // batch
+    t = qkv.view(s, batch, 3, heads, head_dim)
+    o = torch.empty((qkv.shape[0], heads * head_dim), dtype=qkv.dtype, device=qkv.device)
+    ov = o.view(s, batch, heads, head_dim)
+    probs = torch.empty((batch, heads, s, s), dtype=torch.float32, device=qkv.device)
+    scores = torch.empty((s, s), dtype=torch.float32, device=qkv.device)
+    scale = head_dim ** -0.5
+    for bi in range(batch):
+        for h in range(heads):
+            q, k, v = t[:, bi, 0, h], t[:, bi, 1, h], t[:, bi, 2, h]
+            _f32_gemm(q, k, False, True, out=scores)
+            C.causal_softmax_f32(scores, probs[bi, h], scale)
+            C.gemm_f32(probs[bi, h], v, ov[:, bi, h], False, False, 0.0)
+            _count(2)
+    _count()
+    return o, (qkv, probs)
+
+
+def _attention_bwd_f32(do, saved, batch, heads, head_dim, cos, sin):
+    qkv, probs = saved
+    s = qkv.shape[0] // batch
+    t = qkv.view(s, batch, 3, heads, head_dim)
+    dqkv = torch.empty_like(qkv)
+    dt = dqkv.view(s, batch, 3, heads, head_dim)
+    dov = do.view(s, batch, heads, head_dim)
+    dp = torch.empty((s, s), dtype=torch.float32, device=qkv.device)
+    ds = torch.empty_like(dp)
+    scale = head_dim ** -0.5
+    for bi in range(batch):
+        for h in range(heads):
+            q, k, v = t[:, bi, 0, h], t[:, bi, 1, h], t[:, bi, 2, h]
+            p, g = probs[bi, h], dov[:, bi, h]
+            C.gemm_f32(p, g, dt[:, bi, 2, h], True, False, 0.0)      # dV = P^T dO
+            C.gemm_f32(g, v, dp, False, True, 0.0)                   # dP = dO V^T
+            C.softmax_bwd_f32(p, dp, ds, scale)                      # dS (scaled)
+            C.gemm_f32(ds, k, dt[:, bi, 0, h], False, False, 0.0)    # dQ = dS K
+            C.gemm_f32(ds, q, dt[:, bi, 1, h], True, False, 0.0)     # dK = dS^T Q
+            _count(5)
+    C.rope_inplace(dqkv, cos, sin, batch, heads, head_dim, -1.0)
+    _count()
+    return dqkv
+
+
 def attention(qkv, batch, heads, head_dim, cos, sin, inplace=False):
     """RoPE + causal flash attention. With ``inplace`` the rotation is applied
-    to ``qkv`` itself (the model passes its private QKV GEMM output)."""
+    to ``qkv`` itself (the model passes its private QKV GEMM output). fp32
+    inputs take the exact-fp32 materialized path."""
+    if qkv.dtype == torch.float32:
+        return _attention_f32(qkv, batch, heads, head_dim, cos, sin)
     qkv = qkv.contiguous() if inplace else qkv.clone(memory_format=torch.contiguous_format)
     C.rope_inplace(qkv, cos, sin, batch, heads, head_dim, 1.0)
     if (qkv.shape[0] // batch) % 128 == 0:
@@ -155,6 +211,8 @@ def attention(qkv, batch, heads, head_dim, cos, sin, inplace=False):
 
 
 def attention_bwd(do, saved, batch, heads, head_dim, cos, sin):
+    if len(saved) == 2:
+        return _attention_bwd_f32(do.contiguous(), saved, batch, heads, head_dim, cos, sin)
     qkv, o, lse = saved
     if (qkv.shape[0] // batch) % 128 == 0:
         dqkv = C.flash_attn_bwd_tc(do.contiguous(), qkv, o, lse, batch, heads, head_dim, status_word(qkv.device))

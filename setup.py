@@ -24,6 +24,7 @@ SOURCES = [
     "attention_bwd_tc.cu",
     "fused_tp.cu",
     "noalloc.cu",
+    "fp32.cu",
 ]
 
 NVCC_FLAGS = [

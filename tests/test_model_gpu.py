@@ -58,3 +58,23 @@ def test_training_step_on_gpu_decreases_loss():
         losses.append(sum(forward_backward_1f1b(model, batches, cfg, DEV, ParallelContext.single())).item())
         opt.step()
     assert losses[-1] < losses[0] - 0.5, losses
+
+
+def test_gpt_cuda_fp32_matches_cpu_tightly():
+    """fp32 mode on CUDA (exact-fp32 kernels) reproduces the CPU model to the
+    distributed tests' tolerance."""
+    cfg = GPTConfig(vocab_size=128, n_layer=2, n_head=4, n_embd=64, seq_len=32, init_std=0.05)
+    torch.manual_seed(0)
+    cpu = GPT(cfg)
+    gpu = GPT(cfg)
+    gpu.load_state_dict(cpu.state_dict())
+    gpu = gpu.to(DEV)
+    x = torch.randint(0, 128, (2, 32))
+    y = torch.randint(0, 128, (2, 32))
+    lc = cpu(x, y)
+    lc.backward()
+    lg = gpu(x.to(DEV), y.to(DEV))
+    lg.backward()
+    torch.testing.assert_close(lg.cpu(), lc, rtol=1e-5, atol=1e-5)
+    for (n, pc), (_, pg) in zip(cpu.named_parameters(), gpu.named_parameters()):
+        torch.testing.assert_close(pg.grad.cpu(), pc.grad, rtol=1e-4, atol=1e-5, msg=n)
