@@ -5,12 +5,14 @@ Every rank runs the same single-threaded loop. Stage ``r`` of ``p`` first runs
 backward, then drains the warm-up activations in cool-down backwards. With one
 stage the loop is plain gradient accumulation.
 
-Exchanges go through ``torch.distributed.batch_isend_irecv`` in the same
-per-pair order on both sides (receive-from-previous, send-to-next,
-receive-from-next, send-to-previous), so the schedule cannot deadlock. On NCCL
-the receives are waited on by the compute stream only (no host blocking) and
-sends are not waited on at all until the end of the step: the compute stream
-runs on while the NCCL stream carries the activation to the next stage.
+Exchanges go through ``torch.distributed.batch_isend_irecv``. In the steady
+state a stage pairs its forward send with the receive of the matching output
+gradient, and its backward send with the receive of the next activation, so
+the two directions of a stage boundary travel in one batched exchange and both
+sides always post matching pairs (deadlock-free by construction). On NCCL the
+receives are waited on by the compute stream only (no host blocking) and sends
+are not waited on at all until the end of the step: the compute stream runs on
+while the NCCL stream carries the activation to the next stage.
 Activations cross stages sequence-first as ``[s, b, H]``.
 
 Parity: ``nano_megatron/pipeline.py:22-224`` (schedule, warm-up depth, P2P
@@ -148,15 +150,24 @@ def forward_backward_1f1b(model: nn.Module, batches: Sequence[Batch], config, de
         inputs.append(hidden)
         outputs.append(output)
 
-    for _ in range(num_steady):
-        hidden = recv_forward()
+    # Steady state: each forward is followed by one backward. The activation
+    # for the next forward is received in the same batched exchange that sends
+    # this backward's input gradient (and the output gradient arrives with the
+    # forward's send), so adjacent stages always post matching pairs.
+    hidden = recv_forward() if num_steady > 0 else None
+    for k in range(num_steady):
         output = _forward_step(model, next(batch_iter), hidden, losses, num_microbatches, ctx)
         grad = None if ctx.is_last_stage else p2p.exchange(send_next=output, recv_next=True)[1]
         inputs.append(hidden)
         outputs.append(output)
         input_grad = run_backward(inputs.pop(0), outputs.pop(0), grad)
-        if not ctx.is_first_stage:
+        last = k == num_steady - 1
+        if ctx.is_first_stage:
+            hidden = None
+        elif last:
             p2p.exchange(send_prev=input_grad)
+        else:
+            hidden = p2p.exchange(send_prev=input_grad, recv_prev=True)[0]
 
     for _ in range(num_warmup):
         input_tensor, output_tensor = inputs.pop(0), outputs.pop(0)
