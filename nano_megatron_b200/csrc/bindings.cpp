@@ -89,7 +89,10 @@ void gemm(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, bool a_mn, bo
 // rank's workspace pointer (mapped in this process); offsets are in bytes.
 void fused_tp_gemm(int64_t mode, const at::Tensor& a_local, const at::Tensor& B, bool b_mn, at::Tensor& out,
                    const std::vector<int64_t>& ws, int64_t rank, int64_t M, int64_t gather_off, int64_t recv_off,
-                   int64_t flags_off, int64_t epoch, bool copy_own, const at::Tensor& err, double timeout_s) {
+                   int64_t flags_off, int64_t epoch, bool copy_own, const at::Tensor& err, double timeout_s,
+                   const c10::optional<at::Tensor>& save_out, const c10::optional<at::Tensor>& labels,
+                   int64_t vocab_start, const c10::optional<at::Tensor>& ce_part,
+                   const c10::optional<at::Tensor>& ce_target) {
   check_cuda(a_local, "a_local");
   check_cuda(B, "B");
   check_cuda(out, "out");
@@ -108,8 +111,9 @@ void fused_tp_gemm(int64_t mode, const at::Tensor& a_local, const at::Tensor& B,
   a.world = world;
   a.m_chunk = (int)(M / world);
   TORCH_CHECK(M % world == 0 && a.m_chunk % 128 == 0, "rows per rank must be a multiple of 128");
-  TORCH_CHECK(mode == nmb::kAllGatherGemm ? a_local.size(0) == a.m_chunk : a_local.size(0) == M, "A rows");
-  TORCH_CHECK(out.size(0) == (mode == nmb::kAllGatherGemm ? M : a.m_chunk) && out.size(1) == a.N, "out shape");
+  const bool ag = mode != nmb::kReduceScatterGemm;
+  TORCH_CHECK(ag ? a_local.size(0) == a.m_chunk : a_local.size(0) == M, "A rows");
+  TORCH_CHECK(out.size(0) == (ag ? M : a.m_chunk) && out.size(1) == a.N, "out shape");
   a.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
   a.ldo = out.stride(0);
   for (int r = 0; r < world; ++r) a.ws[r] = reinterpret_cast<uint8_t*>(ws[r]);
@@ -122,6 +126,26 @@ void fused_tp_gemm(int64_t mode, const at::Tensor& a_local, const at::Tensor& B,
   a.copy_own = copy_own ? 1 : 0;
   a.err = err.data_ptr<int>();
   a.timeout_ns = (uint64_t)(timeout_s * 1e9);
+  if (save_out.has_value()) {
+    TORCH_CHECK(ag && save_out->is_cuda() && save_out->scalar_type() == at::kBFloat16 && save_out->is_contiguous() &&
+                    save_out->size(0) == M && save_out->size(1) == a.K,
+                "save_out must be a contiguous bf16 [M, K] tensor of an all-gather call");
+    a.save_out = reinterpret_cast<__nv_bfloat16*>(save_out->data_ptr());
+  }
+  if (mode == nmb::kAllGatherGemmCE) {
+    TORCH_CHECK(labels.has_value() && ce_part.has_value() && ce_target.has_value(), "CE mode needs its buffers");
+    const int num_n = (a.N + 255) / 256;
+    TORCH_CHECK(labels->scalar_type() == at::kLong && labels->is_contiguous() && labels->numel() == M, "labels");
+    TORCH_CHECK(ce_part->scalar_type() == at::kFloat && ce_part->is_contiguous() &&
+                    ce_part->numel() == 2L * num_n * M,
+                "ce_part must be fp32 [num_n, M, 2]");
+    TORCH_CHECK(ce_target->scalar_type() == at::kFloat && ce_target->numel() == M, "ce_target");
+    TORCH_CHECK(!b_mn, "the LM-head weight is [V/t, H] (K-major)");
+    a.labels = labels->data_ptr<int64_t>();
+    a.vocab_start = vocab_start;
+    a.ce_part = reinterpret_cast<float2*>(ce_part->data_ptr<float>());
+    a.ce_target = ce_target->data_ptr<float>();
+  }
   const at::cuda::CUDAGuard guard(a_local.device());
   check_ok(nmb::fused_tp_gemm((int)mode, a, B.data_ptr(), row_stride(B), b_mn, num_sms(),
                               at::cuda::getCurrentCUDAStream()),
@@ -129,6 +153,44 @@ void fused_tp_gemm(int64_t mode, const at::Tensor& a_local, const at::Tensor& B,
 }
 
 int64_t fused_tp_flag_bytes() { return nmb::kFlagInts * 4; }
+
+// Cross-entropy merge over tiles and TP ranks (see fused_tp.cuh). `ws` is empty
+// for a group of one.
+void ce_merge(const at::Tensor& part, const at::Tensor& target_logit, const at::Tensor& labels, int64_t vocab_start,
+              int64_t vocab_end, const std::vector<int64_t>& ws, int64_t rank, int64_t data_off, int64_t flags_off,
+              int64_t epoch, const at::Tensor& err, double timeout_s, at::Tensor& loss, at::Tensor& gmax,
+              at::Tensor& gsum) {
+  check_cuda(part, "part");
+  TORCH_CHECK(part.scalar_type() == at::kFloat && part.is_contiguous() && part.dim() == 3 && part.size(2) == 2,
+              "part must be fp32 [num_n, T, 2]");
+  const int64_t T = part.size(1);
+  TORCH_CHECK(labels.scalar_type() == at::kLong && labels.is_contiguous() && labels.numel() == T, "labels");
+  TORCH_CHECK(target_logit.scalar_type() == at::kFloat && target_logit.numel() == T, "target_logit");
+  for (const at::Tensor* t : {&loss, &gmax, &gsum})
+    TORCH_CHECK(t->scalar_type() == at::kFloat && t->is_contiguous() && t->numel() == T, "outputs: fp32 [T]");
+  nmb::CeMergeArgs a{};
+  a.part = reinterpret_cast<const float2*>(part.data_ptr<float>());
+  a.target_logit = target_logit.data_ptr<float>();
+  a.labels = labels.data_ptr<int64_t>();
+  a.vocab_start = vocab_start;
+  a.vocab_end = vocab_end;
+  a.T = (int)T;
+  a.num_n = (int)part.size(0);
+  a.world = ws.empty() ? 1 : (int)ws.size();
+  TORCH_CHECK(a.world <= nmb::kMaxRanks && rank >= 0 && rank < a.world, "bad group");
+  a.rank = (int)rank;
+  for (size_t r = 0; r < ws.size(); ++r) a.ws[r] = reinterpret_cast<uint8_t*>(ws[r]);
+  a.data_off = data_off;
+  a.flags_off = flags_off;
+  a.epoch = (uint32_t)epoch;
+  a.err = err.data_ptr<int>();
+  a.timeout_ns = (uint64_t)(timeout_s * 1e9);
+  a.loss = loss.data_ptr<float>();
+  a.gmax = gmax.data_ptr<float>();
+  a.gsum = gsum.data_ptr<float>();
+  const at::cuda::CUDAGuard guard(part.device());
+  check_ok(nmb::ce_merge(a, at::cuda::getCurrentCUDAStream()), "ce_merge");
+}
 
 }  // namespace
 
@@ -138,7 +200,14 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "nano_megatron_b200 sm_100a kernels";
   m.def("gemm", &gemm, "tcgen05 bf16 GEMM", pybind11::arg("A"), pybind11::arg("B"), pybind11::arg("C"),
         pybind11::arg("a_mn"), pybind11::arg("b_mn"), pybind11::arg("out_mode"), pybind11::arg("err") = pybind11::none());
-  m.def("fused_tp_gemm", &fused_tp_gemm);
+  m.def("fused_tp_gemm", &fused_tp_gemm, pybind11::arg("mode"), pybind11::arg("a_local"), pybind11::arg("B"),
+        pybind11::arg("b_mn"), pybind11::arg("out"), pybind11::arg("ws"), pybind11::arg("rank"), pybind11::arg("M"),
+        pybind11::arg("gather_off"), pybind11::arg("recv_off"), pybind11::arg("flags_off"), pybind11::arg("epoch"),
+        pybind11::arg("copy_own"), pybind11::arg("err"), pybind11::arg("timeout_s"),
+        pybind11::arg("save_out") = pybind11::none(), pybind11::arg("labels") = pybind11::none(),
+        pybind11::arg("vocab_start") = 0, pybind11::arg("ce_part") = pybind11::none(),
+        pybind11::arg("ce_target") = pybind11::none());
+  m.def("ce_merge", &ce_merge);
   m.def("fused_tp_flag_bytes", &fused_tp_flag_bytes);
   register_elementwise(m);
 }

@@ -33,6 +33,18 @@
 //   * no rank waits before it has pushed everything the others wait on, so
 //     the protocol cannot deadlock as long as every rank runs the kernel.
 //
+// all-gather -> LM-head GEMM -> cross-entropy statistics (kAllGatherGemmCE):
+//   * the all-gather -> GEMM above with logits = AG(x) @ W^T; the epilogue
+//     rounds each logit to bf16 (the stored value), and per row and 256-column
+//     tile keeps the running max and sum of exp(v - max) (one query row per
+//     epilogue thread, so no cross-thread reduction) plus the target logit.
+//     ce_merge (below) then combines tiles and ranks; fp32 logits are never
+//     materialized.
+// Optional copy of the gathered input (all-gather modes, `save_out`): after
+// its pushes the comm warp of CTA b copies slice b of every chunk (its own
+// from x, chunk c once peer c's CTA b flagged it) into save_out, overlapping
+// the GEMM; the weight gradient then needs no second all-gather.
+//
 // Reuse of the workspace across calls: every call carries a new epoch; a rank
 // writes into a peer's buffers only after that peer announced the epoch,
 // i.e. after the peer's previous kernels (which read the buffers) finished.
@@ -68,6 +80,12 @@ struct Cfg {
   static constexpr int SMEM = STAGES * STAGE_BYTES + STAGING + 1024 + 256;
 };
 constexpr int THREADS = 224;  // 7 warps: producer, MMA, 4 epilogue, comm
+constexpr float kLog2e = 1.4426950408889634f;
+
+template <int MODE>
+constexpr bool is_ag() {
+  return MODE != kReduceScatterGemm;
+}
 
 __device__ __forceinline__ void st_release_sys(int* p, int v) {
   asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
@@ -134,7 +152,7 @@ __device__ __forceinline__ TileInfo tile_of(int t, const FusedTpArgs& a, int mt_
   const int slot = t / per_chunk;
   TileInfo ti;
   ti.local = t - slot * per_chunk;
-  ti.chunk = MODE == kAllGatherGemm ? (a.rank + slot) % a.world : (a.rank + 1 + slot) % a.world;
+  ti.chunk = is_ag<MODE>() ? (a.rank + slot) % a.world : (a.rank + 1 + slot) % a.world;
   ti.tm = ti.chunk * mt_chunk + ti.local % mt_chunk;
   ti.tn = ti.local / mt_chunk;
   return ti;
@@ -192,7 +210,7 @@ fused_tp_kernel(const __grid_constant__ CUtensorMap tmA_local, const __grid_cons
       for (int p = 0; p < a.world; ++p)
         if (p != a.rank) st_release_sys(flags_of(a, p) + kReadyOff + a.rank, epoch);
     }
-    if (MODE == kAllGatherGemm) {
+    if (is_ag<MODE>()) {
       // This CTA's slice of the local shard, in 16-byte units.
       const long total = (long)a.m_chunk * a.K / 8;
       const long per = (total + gridDim.x - 1) / gridDim.x;
@@ -224,6 +242,32 @@ fused_tp_kernel(const __grid_constant__ CUtensorMap tmA_local, const __grid_cons
           if (lane == 0) st_release_sys(flags_of(a, p) + kAgDoneOff + a.rank * kMaxCtas + blockIdx.x, epoch);
         }
       }
+      if (a.save_out != nullptr) {
+        const long chunk_units = (long)a.m_chunk * a.K / 8;
+        for (int j = 0; j < a.world && !*abort_flag; ++j) {
+          const int c = (a.rank + j) % a.world;  // own chunk first, then in arrival order
+          const uint4* from = src;
+          if (c != a.rank) {
+            bool ok = true;
+            if (lane == 0) ok = wait_flag(my_flags + kAgDoneOff + c * kMaxCtas + blockIdx.x, epoch, a.err,
+                                          a.timeout_ns, abort_flag);
+            ok = __shfl_sync(0xffffffffu, ok, 0);
+            __syncwarp();
+            if (!ok) break;
+            from = reinterpret_cast<const uint4*>(a.ws[a.rank] + a.gather_off) + c * chunk_units;
+          }
+          uint4* to = reinterpret_cast<uint4*>(a.save_out) + c * chunk_units;
+          long i = beg + lane;
+          for (; i + 31 * 8 < end; i += 32 * 8) {
+            uint4 v[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) v[u] = __ldcg(from + i + 32 * u);
+#pragma unroll
+            for (int u = 0; u < 8; ++u) to[i + 32 * u] = v[u];
+          }
+          for (; i < end; i += 32) to[i] = __ldcg(from + i);
+        }
+      }
     }
   } else if (warp == 0 && lane == 0) {
     // ------------------------------------------------------------ producer
@@ -237,7 +281,7 @@ fused_tp_kernel(const __grid_constant__ CUtensorMap tmA_local, const __grid_cons
     for (int s = 0; s < STAGES; ++s) issued[s] = -1;
     for (int t = blockIdx.x; t < num_tiles && !*abort_flag; t += gridDim.x) {
       const TileInfo ti = tile_of<MODE>(t, a, mt_chunk, num_n);
-      const bool from_gather = MODE == kAllGatherGemm && ti.chunk != a.rank;
+      const bool from_gather = is_ag<MODE>() && ti.chunk != a.rank;
       if (from_gather && !((ready_mask >> ti.chunk) & 1u)) {
         const int* done = my_flags + kAgDoneOff + ti.chunk * kMaxCtas;
         for (int c = 0; c < (int)gridDim.x; ++c)
@@ -246,7 +290,7 @@ fused_tp_kernel(const __grid_constant__ CUtensorMap tmA_local, const __grid_cons
         ready_mask |= 1u << ti.chunk;
       }
       const CUtensorMap* amap = from_gather ? &tmA_gather : &tmA_local;
-      const int arow = (MODE == kAllGatherGemm && !from_gather) ? (ti.tm * BM - a.rank * a.m_chunk) : ti.tm * BM;
+      const int arow = (is_ag<MODE>() && !from_gather) ? (ti.tm * BM - a.rank * a.m_chunk) : ti.tm * BM;
       for (int kb = 0; kb < num_k; ++kb) {
         if (!mbar_wait_abortable(&empty[stage], phase ^ 1, a.err, abort_flag)) break;
         uint8_t* a_dst = smem + stage * STAGE_BYTES;
@@ -315,6 +359,10 @@ fused_tp_kernel(const __grid_constant__ CUtensorMap tmA_local, const __grid_cons
       const int row = ti.tm * BM + quarter * 32 + lane;
       const int row_local = row - ti.chunk * a.m_chunk;
       const uint32_t t_row = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN;
+      // cross-entropy statistics of this row over the tile's columns
+      float ce_m = -INFINITY, ce_s = 0.f;
+      long ce_col = -1;  // target column relative to the tile, if inside
+      if (MODE == kAllGatherGemmCE) ce_col = a.labels[row] - a.vocab_start - (long)ti.tn * BN;
       if (MODE == kReduceScatterGemm) {
         // foreign tile: wait once for the owner's ready; own tile: wait for all partials
         if (ti.chunk != a.rank && !((ready_mask >> ti.chunk) & 1u)) {
@@ -341,7 +389,34 @@ fused_tp_kernel(const __grid_constant__ CUtensorMap tmA_local, const __grid_cons
 #pragma unroll
         for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
         __nv_bfloat16* dst;
-        if (MODE == kAllGatherGemm) {
+        if (MODE == kAllGatherGemmCE) {
+          const int nv = min(32, a.N - col);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = __bfloat162float(__float2bfloat16_rn(v[j]));
+          float mx = -INFINITY;
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (j < nv) mx = fmaxf(mx, v[j]);
+          const float nm = fmaxf(ce_m, mx);
+          const float nml = nm * kLog2e;
+          float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+          for (int j = 0; j < 32; j += 2) {
+            if (j < nv) s0 += fast_exp2(fmaf(v[j], kLog2e, -nml));
+            if (j + 1 < nv) s1 += fast_exp2(fmaf(v[j + 1], kLog2e, -nml));
+          }
+          ce_s = ce_s * fast_exp2((ce_m - nm) * kLog2e) + (s0 + s1);
+          ce_m = nm;
+          const long tc = ce_col - c;
+          if (tc >= 0 && tc < nv) {
+            float tv = 0.f;
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (j == tc) tv = v[j];
+            a.ce_target[row] = tv;
+          }
+        }
+        if (is_ag<MODE>()) {
           dst = a.out + (long)row * a.ldo + col;
         } else if (ti.chunk != a.rank) {
           // stage this thread's 32 columns (row `lane` of the warp's 32 rows);
@@ -391,6 +466,7 @@ fused_tp_kernel(const __grid_constant__ CUtensorMap tmA_local, const __grid_cons
       }
       tc_fence_before();
       mbar_arrive(&tempty[acc]);
+      if (MODE == kAllGatherGemmCE) a.ce_part[(long)ti.tn * a.M + row] = make_float2(ce_m, ce_s);
       if (MODE == kReduceScatterGemm && ti.chunk != a.rank) {
         // write the warp's 32 staged rows to the owner, one 512-byte row per instruction
         __syncwarp();
@@ -431,10 +507,13 @@ cudaError_t launch(const FusedTpArgs& a, const void* B, long ldb, int num_sms, c
     configured = true;
   }
   CUtensorMap ta_local, ta_gather, tb;
-  if (MODE == kAllGatherGemm) {
+  if (is_ag<MODE>()) {
     if (!make_tmap_bf16_2d(&ta_local, a.a_local, a.K, a.m_chunk, a.lda_local, 64, BM)) return cudaErrorInvalidValue;
-    if (!make_tmap_bf16_2d(&ta_gather, a.ws[a.rank] + a.gather_off, a.K, a.M, a.K, 64, BM))
+    if (a.world == 1) {
+      ta_gather = ta_local;  // nothing to gather: no workspace is needed
+    } else if (!make_tmap_bf16_2d(&ta_gather, a.ws[a.rank] + a.gather_off, a.K, a.M, a.K, 64, BM)) {
       return cudaErrorInvalidValue;
+    }
   } else {
     if (!make_tmap_bf16_2d(&ta_local, a.a_local, a.K, a.M, a.lda_local, 64, BM)) return cudaErrorInvalidValue;
     ta_gather = ta_local;
@@ -448,7 +527,82 @@ cudaError_t launch(const FusedTpArgs& a, const void* B, long ldb, int num_sms, c
   return cudaGetLastError();
 }
 
+__device__ __forceinline__ void merge_lse(float& m, float& s, float m2, float s2) {
+  const float nm = fmaxf(m, m2);
+  if (nm == -INFINITY) return;
+  s = s * __expf(m - nm) + s2 * __expf(m2 - nm);
+  m = nm;
+}
+
+constexpr int CE_THREADS = 256;
+
+__global__ void __launch_bounds__(CE_THREADS) ce_merge_kernel(const CeMergeArgs a) {
+  const int row = blockIdx.x * CE_THREADS + threadIdx.x;
+  const bool live = row < a.T;
+  float m = -INFINITY, s = 0.f, t = 0.f;
+  if (live) {
+    for (int n = 0; n < a.num_n; ++n) {
+      const float2 p = a.part[(long)n * a.T + row];
+      merge_lse(m, s, p.x, p.y);
+    }
+    const long lbl = a.labels[row];
+    if (lbl >= a.vocab_start && lbl < a.vocab_end) t = a.target_logit[row];
+  }
+  if (a.world > 1) {
+    __shared__ int ok;
+    __shared__ int abort_flag;
+    const long slot = (long)(a.epoch & 1u) * kMaxRanks * a.T;
+    if (live) {
+      const float4 mine = make_float4(m, s, t, 0.f);
+      for (int p = 0; p < a.world; ++p) {
+        float4* dst = reinterpret_cast<float4*>(a.ws[p] + a.data_off) + slot + (long)a.rank * a.T;
+        dst[row] = mine;
+      }
+      __threadfence_system();
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      __threadfence_system();
+      for (int p = 0; p < a.world; ++p)
+        if (p != a.rank)
+          st_release_sys(reinterpret_cast<int*>(a.ws[p] + a.flags_off) + kCeFlagOff + a.rank * kMaxCeBlocks +
+                             blockIdx.x,
+                         (int)a.epoch);
+      abort_flag = 0;
+      ok = 1;
+      const int* mine = reinterpret_cast<const int*>(a.ws[a.rank] + a.flags_off) + kCeFlagOff;
+      for (int p = 0; p < a.world && ok; ++p)
+        if (p != a.rank &&
+            !wait_flag(mine + p * kMaxCeBlocks + blockIdx.x, (int)a.epoch, a.err, a.timeout_ns, &abort_flag))
+          ok = 0;
+    }
+    __syncthreads();
+    if (!ok || !live) return;
+    const float4* src = reinterpret_cast<const float4*>(a.ws[a.rank] + a.data_off) + slot;
+    m = -INFINITY;
+    s = 0.f;
+    t = 0.f;
+    for (int p = 0; p < a.world; ++p) {
+      const float4 q = __ldcv(src + (long)p * a.T + row);
+      merge_lse(m, s, q.x, q.y);
+      t += q.z;
+    }
+  }
+  if (!live) return;
+  a.loss[row] = logf(s) + m - t;
+  a.gmax[row] = m;
+  a.gsum[row] = s;
+}
+
 }  // namespace
+
+cudaError_t ce_merge(const CeMergeArgs& a, cudaStream_t stream) {
+  if (a.T <= 0) return cudaSuccess;
+  const int blocks = (a.T + CE_THREADS - 1) / CE_THREADS;
+  if (a.world < 1 || a.world > kMaxRanks || blocks > kMaxCeBlocks || a.epoch == 0) return cudaErrorInvalidValue;
+  ce_merge_kernel<<<blocks, CE_THREADS, 0, stream>>>(a);
+  return cudaGetLastError();
+}
 
 cudaError_t fused_tp_gemm(int mode, const FusedTpArgs& a, const void* B, long ldb, bool b_mn, int num_sms,
                           cudaStream_t stream) {
@@ -459,6 +613,10 @@ cudaError_t fused_tp_gemm(int mode, const FusedTpArgs& a, const void* B, long ld
   if (mode == kAllGatherGemm) {
     return b_mn ? launch<kAllGatherGemm, true>(a, B, ldb, num_sms, stream)
                 : launch<kAllGatherGemm, false>(a, B, ldb, num_sms, stream);
+  }
+  if (mode == kAllGatherGemmCE) {
+    if (a.labels == nullptr || a.ce_part == nullptr || a.ce_target == nullptr || b_mn) return cudaErrorInvalidValue;
+    return launch<kAllGatherGemmCE, false>(a, B, ldb, num_sms, stream);
   }
   return b_mn ? launch<kReduceScatterGemm, true>(a, B, ldb, num_sms, stream)
               : launch<kReduceScatterGemm, false>(a, B, ldb, num_sms, stream);

@@ -349,9 +349,11 @@ __global__ void ce_stats_kernel(const T* __restrict__ logits, const int64_t* __r
 }
 
 template <typename T>
-__global__ void ce_grad_kernel(const T* __restrict__ logits, const int64_t* __restrict__ target,
+// `logits` and `dlogits` may be the same buffer (each element is read, then
+// written, by the same thread).
+__global__ void ce_grad_kernel(const T* logits, const int64_t* __restrict__ target,
                                const float* __restrict__ gmax, const float* __restrict__ gsum,
-                               const float* __restrict__ gscale, float inv_n, T* __restrict__ dlogits, long rows,
+                               const float* __restrict__ gscale, float inv_n, T* dlogits, long rows,
                                int vl, long ld, long vstart) {
   const long row = blockIdx.y;
   const float m = gmax[row];

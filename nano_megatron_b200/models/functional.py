@@ -86,6 +86,16 @@ def _use_fused(pctx: ParallelContext, x: torch.Tensor, rows_local: int) -> bool:
     return fused_tp.supported(rows_local, pctx)
 
 
+def _use_fused_ce(pctx: ParallelContext, x: torch.Tensor, w: torch.Tensor, mode: str) -> bool:
+    """Fused LM-head + cross-entropy kernels: CUDA, bf16; across GPUs only when enabled."""
+    if not (x.is_cuda and x.dtype == torch.bfloat16):
+        return False
+    from ..ops import fused_tp
+    if not fused_tp.ce_supported(x.shape[0], w.shape[0]):
+        return False
+    return pctx.tp_size == 1 or (pctx.tp_size <= 8 and pctx.resources.get("fused_tp", False))
+
+
 def _ag(x, pctx):
     return M.all_gather_sequence(x, pctx.tp_group, pctx.tp_size)
 
@@ -104,13 +114,17 @@ class _ColumnLinear(torch.autograd.Function):
     def forward(ctx, x, wref, pctx, mode, dtype, *params):
         x = x if x.dtype == dtype else x.to(dtype)
         w = wref.for_compute(dtype)
-        if mode == "ag" and _use_fused(pctx, x, x.shape[0]):
+        ctx.gathered = mode == "ag" and _use_fused(pctx, x, x.shape[0])
+        if ctx.gathered:
+            # The kernel also leaves a private copy of AG(x) for the weight
+            # gradient, so the backward needs no second all-gather.
             from ..ops import fused_tp
-            y = fused_tp.all_gather_matmul(x, w, pctx)
+            X, y = fused_tp.all_gather_matmul(x, w, pctx, save_gathered=True)
+            ctx.save_for_backward(X, w)
         else:
             X = _ag(x, pctx) if mode == "ag" else x
             y = ops.mm_nn(X, w)
-        ctx.save_for_backward(x, w)
+            ctx.save_for_backward(x, w)
         ctx.wref, ctx.pctx, ctx.mode = wref, pctx, mode
         return y
 
@@ -119,10 +133,13 @@ class _ColumnLinear(torch.autograd.Function):
         x, w = ctx.saved_tensors
         pctx, mode, wref = ctx.pctx, ctx.mode, ctx.wref
         dy = dy.contiguous()
-        if mode == "ag" and _use_fused(pctx, dy, x.shape[0]):
+        if ctx.gathered and _use_fused(pctx, dy, x.shape[0] // pctx.tp_size):
             from ..ops import fused_tp
             dx = fused_tp.matmul_reduce_scatter(dy, w, pctx, transpose_b=True)
-            X = fused_tp.all_gather(x, pctx)
+            X = x
+        elif ctx.gathered:
+            dx = _rs(ops.mm_nt(dy, w), pctx)
+            X = x
         else:
             dX = ops.mm_nt(dy, w)
             dx = _rs(dX, pctx) if mode == "ag" else (_ar(dX, pctx) if mode == "f" else dX)
@@ -288,22 +305,37 @@ def merge_ce_stats(mx, se, tl, pctx: ParallelContext):
 
 
 class _LMHeadCE(torch.autograd.Function):
-    """Vocab-parallel LM head + cross entropy; returns the mean token loss."""
+    """Vocab-parallel LM head + cross entropy; returns the mean token loss.
+
+    On CUDA in bf16 the forward is the fused kernel pair of
+    :func:`nano_megatron_b200.ops.fused_tp.lm_head_cross_entropy` (all-gather,
+    GEMM with the per-token statistics in its epilogue, one cross-rank merge);
+    the backward turns the saved bf16 logits into ``(softmax - onehot) * g/n``
+    in place and runs dgrad (fused with the reduce-scatter under sequence
+    parallelism) and wgrad on them.
+    """
 
     @staticmethod
     def forward(ctx, x, labels, wref, pctx, mode, dtype, vocab_start, vocab_end, *params):
         x = x if x.dtype == dtype else x.to(dtype)
         w = wref.for_compute(dtype)  # [V/t, H]
-        X = _ag(x, pctx) if mode == "ag" else x
-        if X.is_cuda:
-            loss_tok, state = ops.cuda_ops().lm_head_ce_fwd(X, w, labels, vocab_start, vocab_end, pctx)
+        ctx.fused = _use_fused_ce(pctx, x, w, mode)
+        if ctx.fused:
+            from ..ops import fused_tp
+            loss_tok, logits, gm, gs, X = fused_tp.lm_head_cross_entropy(
+                x, w, labels, vocab_start, vocab_end, pctx, gather=mode == "ag")
+            ctx.save_for_backward(X, labels, w, logits, gm, gs)
         else:
-            logits = ops.mm_nt(X, w)
-            mx, se, tl, _ = ops.ce_local_stats(logits, labels, vocab_start, vocab_end)
-            gm, gs, gt = merge_ce_stats(mx, se, tl, pctx)
-            loss_tok = gs.log() + gm - gt
-            state = (logits, gm, gs)
-        ctx.save_for_backward(x, labels, w, *state)
+            X = _ag(x, pctx) if mode == "ag" else x
+            if X.is_cuda:
+                loss_tok, state = ops.cuda_ops().lm_head_ce_fwd(X, w, labels, vocab_start, vocab_end, pctx)
+            else:
+                logits = ops.mm_nt(X, w)
+                mx, se, tl, _ = ops.ce_local_stats(logits, labels, vocab_start, vocab_end)
+                gm, gs, gt = merge_ce_stats(mx, se, tl, pctx)
+                loss_tok = gs.log() + gm - gt
+                state = (logits, gm, gs)
+            ctx.save_for_backward(x, labels, w, *state)
         ctx.wref, ctx.pctx, ctx.mode, ctx.vrange, ctx.dtype = wref, pctx, mode, (vocab_start, vocab_end), dtype
         return loss_tok.mean()
 
@@ -312,6 +344,18 @@ class _LMHeadCE(torch.autograd.Function):
         x, labels, w, *state = ctx.saved_tensors
         pctx, mode, wref = ctx.pctx, ctx.mode, ctx.wref
         n = labels.numel()
+        if ctx.fused:
+            X = x  # the gathered input saved by the forward kernel
+            dlogits = ops.cuda_ops().lm_head_ce_grad(X, w, labels, ctx.vrange[0], state, g / n, inplace=True)
+            rows_local = X.shape[0] // pctx.tp_size
+            if mode == "ag" and _use_fused(pctx, dlogits, rows_local):
+                from ..ops import fused_tp
+                dx = fused_tp.matmul_reduce_scatter(dlogits, w, pctx, transpose_b=False)
+            else:
+                dX = ops.mm_nn(dlogits, w)
+                dx = _rs(dX, pctx) if mode == "ag" else (_ar(dX, pctx) if mode == "f" else dX)
+            grads = wref.accumulate(ops.mm_tn_acc, dlogits, X)
+            return (dx, None, None, None, None, None, None, None, *grads)
         X = _ag(x, pctx) if mode == "ag" else x
         if X.is_cuda:
             dlogits = ops.cuda_ops().lm_head_ce_grad(X, w, labels, ctx.vrange[0], state, g / n)

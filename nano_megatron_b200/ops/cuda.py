@@ -286,9 +286,12 @@ def lm_head_ce_fwd(X, w, labels, vocab_start, vocab_end, pctx):
     return loss, (logits, gm, gs)
 
 
-def lm_head_ce_grad(X, w, labels, vocab_start, state, g_over_n):
+def lm_head_ce_grad(X, w, labels, vocab_start, state, g_over_n, inplace=False):
+    """``(softmax - onehot) * g/n`` from the saved logits; ``inplace`` overwrites them."""
     logits, gm, gs = state
-    d = torch.empty_like(logits)
+    d = logits if inplace else torch.empty_like(logits)
+    if inplace:
+        torch.autograd.graph.increment_version(logits)
     C.ce_grad(logits, labels.contiguous(), gm, gs, g_over_n.float().reshape(1), 1.0, d, vocab_start)
     _count()
     return d

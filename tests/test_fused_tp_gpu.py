@@ -1,4 +1,4 @@
-"""Fused all-gather->GEMM and GEMM->reduce-scatter kernels on 2 GPUs, against
+"""Fused all-gather->GEMM, GEMM->reduce-scatter and LM-head cross-entropy kernels on 2 GPUs, against
 fp32 torch references and against the NCCL path; plus a TP=2 sequence-parallel
 GPT step with and without the fused kernels. Needs at least 2 GPUs (skipped
 otherwise). Every cross-GPU wait in the kernels is bounded; the test lowers the
@@ -73,6 +73,38 @@ def _worker(rank, world, port, q):
                 out2 = fused_tp.matmul_reduce_scatter(a_parts[rank], wt, pctx, transpose_b=True)
                 if _rel(out2, ref) > 1e-2:
                     failures.append(f"gemm_rs^T {_rel(out2, ref)}")
+                # all-gather -> GEMM with the private gathered copy
+                xs, y3 = fused_tp.all_gather_matmul(x[rank * mc:(rank + 1) * mc], w, pctx, save_gathered=True)
+                if not torch.equal(xs, x):
+                    failures.append("saved gathered copy differs")
+                if _rel(y3, x.float() @ w.float()) > 5e-3:
+                    failures.append("ag_gemm with save")
+        torch.cuda.synchronize()
+        KC.check_status(dev)
+
+        # fused vocab-parallel LM head + cross entropy (sequence-sharded input,
+        # and full input with the merge only), against torch on the full vocab
+        for it in range(3):
+            rows, hidden, vocab = 512, 256, 2 * 1040
+            vl = vocab // world
+            xf = full(300 + it, rows, hidden)
+            wf = (full(400 + it, vocab, hidden).float() * 0.1).bfloat16()
+            gen = torch.Generator(device=dev).manual_seed(500 + it)
+            labels = torch.randint(0, vocab, (rows,), generator=gen, device=dev)
+            lf = xf.float() @ wf.float().t()
+            ref = torch.logsumexp(lf, dim=1) - lf.gather(1, labels[:, None])[:, 0]
+            wl = wf[rank * vl:(rank + 1) * vl]
+            for gather in (True, False):
+                xin = xf[rank * (rows // world):(rank + 1) * (rows // world)] if gather else xf
+                loss, logits, gm, gs, X = fused_tp.lm_head_cross_entropy(
+                    xin, wl, labels, rank * vl, (rank + 1) * vl, pctx, gather=gather)
+                if (loss - ref).abs().max().item() > 3e-2:
+                    failures.append(f"fused ce gather={gather}: {(loss - ref).abs().max().item()}")
+                if not torch.equal(X, xf):
+                    failures.append(f"fused ce gathered input gather={gather}")
+                lse = torch.logsumexp(lf, dim=1)
+                if (gm + gs.log() - lse).abs().max().item() > 3e-2:
+                    failures.append("fused ce global lse")
         torch.cuda.synchronize()
         KC.check_status(dev)
 

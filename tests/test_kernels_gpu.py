@@ -156,6 +156,42 @@ def test_cross_entropy_stats_and_grad():
     assert _rel(d, dr) < 1e-2
 
 
+@pytest.mark.parametrize("rows,hidden,vocab,start", [(256, 512, 1000, 0), (384, 256, 4096, 0), (128, 128, 520, 480)])
+def test_fused_lm_head_cross_entropy(rows, hidden, vocab, start):
+    """GEMM + CE-statistics epilogue + merge (one GPU) against torch on the same bf16 logits."""
+    import torch.nn.functional as F
+    from nano_megatron_b200.ops import fused_tp
+    from nano_megatron_b200.parallel.context import ParallelContext
+    torch.manual_seed(rows + vocab)
+    x = torch.randn(rows, hidden, device=DEV).bfloat16()
+    w = (torch.randn(vocab, hidden, device=DEV) * 0.1).bfloat16()
+    labels = torch.randint(0, start + vocab + 40, (rows,), device=DEV)  # some outside the shard
+    loss, logits, gm, gs, X = fused_tp.lm_head_cross_entropy(x, w, labels, start, start + vocab,
+                                                             ParallelContext.single(), gather=False)
+    KC.check_status(DEV)
+    ref_logits = x.float() @ w.float().t()
+    assert _rel(logits, ref_logits) < 5e-3
+    lf = logits.float()
+    rm = lf.max(dim=1).values
+    rs = torch.exp(lf - rm[:, None]).sum(dim=1)
+    local = labels - start
+    owned = (local >= 0) & (local < vocab)
+    rt = torch.where(owned, lf.gather(1, local.clamp(0, vocab - 1)[:, None])[:, 0], torch.zeros_like(rm))
+    assert torch.equal(gm, rm)
+    assert _rel(gs, rs) < 1e-5
+    assert (loss - (rs.log() + rm - rt)).abs().max().item() < 1e-4
+    if start == 0 and bool(owned.all()):
+        assert (loss - F.cross_entropy(lf, labels, reduction="none")).abs().max().item() < 1e-4
+    # backward: (softmax - onehot) * g/n, in place in the logits buffer
+    g = torch.tensor(0.7, device=DEV)
+    saved = logits.clone()
+    d = KC.lm_head_ce_grad(X, w, labels, start, (logits, gm, gs), g / rows, inplace=True)
+    assert d.data_ptr() == logits.data_ptr()
+    p = torch.exp(saved.float() - gm[:, None]) / gs[:, None]
+    p[owned, local[owned]] -= 1.0
+    assert _rel(d, p * (0.7 / rows)) < 1e-2
+
+
 def test_adamw_flat_matches_reference():
     torch.manual_seed(9)
     n = 4096 + 64
