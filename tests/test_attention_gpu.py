@@ -59,12 +59,17 @@ def test_lse_is_log_sum_exp_of_scaled_scores():
     torch.testing.assert_close(lse[0], torch.logsumexp(s, -1), rtol=1e-3, atol=1e-3)
 
 
-@pytest.mark.parametrize("S,b,h", [(128, 1, 1), (1024, 2, 2), (2048, 1, 3)])
-def test_tcgen05_forward_matches_mma_sync_forward(S, b, h):
-    """The tcgen05 forward and the mma.sync forward agree (output and lse)."""
+@pytest.mark.parametrize("S,b,h,amp", [(128, 1, 1, 1.0), (384, 1, 2, 1.0), (1024, 2, 2, 1.0), (2048, 1, 3, 1.0),
+                                       (640, 2, 1, 6.0), (1024, 1, 2, 12.0)])
+def test_tcgen05_forward_matches_mma_sync_forward(S, b, h, amp):
+    """The tcgen05 forward and the mma.sync forward agree (output and lse).
+
+    Odd tile counts (384, 640) leave the second query tile of a CTA empty;
+    large amplitudes make row maxima jump across key blocks, which exercises
+    the rescaling of the output accumulator."""
     from nano_megatron_b200 import _C
     torch.manual_seed(S * h)
-    qkv = torch.randn(S * b, 3 * h * 128, device=DEV).bfloat16()
+    qkv = (torch.randn(S * b, 3 * h * 128, device=DEV) * amp).bfloat16()
     o1, l1 = _C.flash_attn_fwd(qkv, b, h, 128)
     o2, l2 = _C.flash_attn_fwd_tc(qkv, b, h, 128, KC.status_word(DEV))
     KC.check_status(DEV)
