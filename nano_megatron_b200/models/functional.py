@@ -35,6 +35,24 @@ from ..parallel import mappings as M
 from ..parallel.context import ParallelContext
 
 
+# Observer of gradient writes: called with each ``main_grad`` tensor right
+# after a backward enqueued the kernel that accumulates into it (the
+# data-parallel bucketer of :mod:`nano_megatron_b200.parallel.grads` listens).
+_grad_observer = None
+
+
+def set_grad_observer(fn):
+    """Install ``fn(main_grad)`` as the gradient-write observer; returns the previous one."""
+    global _grad_observer
+    previous, _grad_observer = _grad_observer, fn
+    return previous
+
+
+def _grad_written(tensor) -> None:
+    if _grad_observer is not None:
+        _grad_observer(tensor)
+
+
 class WeightRef:
     """A weight as the kernels see it: master data, compute copy, grad buffer.
 
@@ -68,6 +86,7 @@ class WeightRef:
         """Accumulate via ``grad_fn(*args, out)``; returns autograd grads for ``params``."""
         if self.main_grad is not None:
             grad_fn(*args, self.main_grad)
+            _grad_written(self.main_grad)
             return (None,) * len(self.params)
         if len(self.params) != 1:
             raise RuntimeError("a fused weight needs a main_grad buffer")
@@ -204,6 +223,8 @@ class _RMSNorm(torch.autograd.Function):
         x, weight, rstd = ctx.saved_tensors
         main_grad = ctx.main_grad
         dx, dw = ops.rmsnorm_bwd(dy.contiguous(), x, weight.detach(), rstd, main_grad)
+        if main_grad is not None:
+            _grad_written(main_grad)
         return dx, (None if main_grad is not None else dw.to(weight.dtype)), None
 
 

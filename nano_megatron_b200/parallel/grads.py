@@ -84,6 +84,137 @@ def _dp_average(flat: torch.Tensor, ctx: ParallelContext) -> None:
         flat /= ctx.dp_size
 
 
+class GradBucketer:
+    """Data-parallel gradient averaging in buckets, started during the last backward.
+
+    The stage's flat gradient buffer is cut into buckets of whole regions,
+    about ``bucket_bytes`` each, formed from the end of the buffer (the last
+    layers, whose gradients backward produces first). Every kernel that
+    accumulates into a region reports it (``functional.set_grad_observer``);
+    the backwards before the last one teach the bucketer how many writes a
+    region receives per microbatch (two for an embedding tied to the LM head
+    on one stage), and during the final microbatch's backward a region is
+    complete once it received that many. When every region of a bucket is
+    complete, the bucket's all-reduce starts: on CUDA on a communication
+    stream that first waits for an event recorded after the last write, with
+    ``ReduceOp.AVG`` so NCCL folds the ``1/dp`` scale into the reduction.
+    :meth:`finish` starts whatever is left (a step with one microbatch learns
+    nothing the first time and reduces everything there) and makes the compute
+    stream wait for all of it.
+
+    ``overlap=False`` issues each bucket on the compute stream instead (still
+    bucket by bucket, still started during backward). That is the mode for
+    models whose fused tensor-parallel kernels run during backward: those
+    kernels keep one CTA per SM resident and wait for their TP peers, and an
+    NCCL kernel running beside them on another stream could leave one of
+    their CTAs without an SM on one rank while its peers wait for it.
+
+    Parity: replaces ``nano_megatron/grads.py:35-54`` (one flat all-reduce
+    after the whole backward, then a division by ``dp``).
+    """
+
+    def __init__(self, model, ctx: ParallelContext, bucket_bytes: int = 128 << 20, overlap: bool = True):
+        buffers = _flat_buffers(model)
+        if buffers is None:
+            raise ValueError("the bucketer needs a model with flat gradient buffers")
+        self.ctx = ctx
+        self.grad = buffers.grad
+        regions = buffers.regions
+        self.region_of_ptr: dict[int, int] = {}
+        for i, region in enumerate(regions):
+            self.region_of_ptr[region.grad_block.data_ptr()] = i
+            for p in region.params:
+                self.region_of_ptr[p.main_grad.data_ptr()] = i
+        # buckets of consecutive regions, from the end of the buffer
+        limit = max(1, bucket_bytes // self.grad.element_size())
+        self.buckets: list[tuple[int, int]] = []       # [start, end) element spans
+        self.bucket_regions: list[list[int]] = []
+        self.bucket_of = [0] * len(regions)
+        end = buffers.numel
+        current: list[int] = []
+        for i in range(len(regions) - 1, -1, -1):
+            current.append(i)
+            start = regions[i].offset
+            if end - start >= limit or i == 0:
+                b = len(self.buckets)
+                self.buckets.append((0 if i == 0 else start, end))
+                self.bucket_regions.append(current)
+                for r in current:
+                    self.bucket_of[r] = b
+                end, current = start, []
+        self.overlap = overlap and self.grad.is_cuda
+        self.stream = torch.cuda.Stream(device=self.grad.device) if self.overlap else None
+        self.per_microbatch: list[int] | None = None
+        self._reset()
+
+    def _reset(self) -> None:
+        self.writes = [0] * len(self.bucket_of)
+        self.armed = False
+        self.left: list[int] = []
+        self.bucket_left: list[int] = []
+        self.started = [False] * len(self.buckets)
+        self.works: list = []
+
+    # ------------------------------------------------------------ observers
+    def observe(self, tensor) -> None:
+        i = self.region_of_ptr.get(tensor.data_ptr())
+        if i is None:
+            return
+        self.writes[i] += 1
+        if self.armed and self.left[i] > 0:
+            self.left[i] -= 1
+            if self.left[i] == 0:
+                b = self.bucket_of[i]
+                self.bucket_left[b] -= 1
+                if self.bucket_left[b] == 0:
+                    self._start(b)
+
+    def before_last_backward(self, prior_backwards: int) -> None:
+        if prior_backwards > 0:
+            self.per_microbatch = [w // prior_backwards for w in self.writes]
+        if self.per_microbatch is None:
+            return
+        self.left = list(self.per_microbatch)
+        self.bucket_left = [sum(1 for r in regions if self.left[r] > 0) for regions in self.bucket_regions]
+        self.armed = True
+        for b, n in enumerate(self.bucket_left):
+            if n == 0:
+                self._start(b)
+
+    # ----------------------------------------------------------- reduction
+    def _start(self, b: int) -> None:
+        if self.started[b]:
+            return
+        self.started[b] = True
+        start, end = self.buckets[b]
+        view = self.grad[start:end]
+        if self.stream is not None:
+            ready = torch.cuda.Event()
+            ready.record(torch.cuda.current_stream(self.grad.device))
+            self.stream.wait_event(ready)
+            with torch.cuda.stream(self.stream):
+                self.works.append(dist.all_reduce(view, op=dist.ReduceOp.AVG, group=self.ctx.dp_group,
+                                                  async_op=True))
+        elif view.is_cuda:
+            dist.all_reduce(view, op=dist.ReduceOp.AVG, group=self.ctx.dp_group)
+        else:
+            self.works.append((dist.all_reduce(view, group=self.ctx.dp_group, async_op=True), view))
+
+    def finish(self) -> None:
+        """Start the remaining buckets (in bucket order) and wait for every bucket."""
+        for b in range(len(self.buckets)):
+            self._start(b)
+        for work in self.works:
+            if isinstance(work, tuple):
+                work[0].wait()
+                work[1].div_(self.ctx.dp_size)
+            else:
+                work.wait()
+        if self.stream is not None:
+            torch.cuda.current_stream(self.grad.device).wait_stream(self.stream)
+        self._reset()
+
+
 def all_reduce_embedding_gradients(model, ctx: ParallelContext) -> None:
     """SUM the tied embedding / LM-head gradient copies over the tied group."""
     if ctx.pp_size == 1 or ctx.tied_group is None:

@@ -103,13 +103,14 @@ def _backward_step(input_tensor, output_tensor, output_gradient, ctx):
 
 
 def forward_backward_1f1b(model: nn.Module, batches: Sequence[Batch], config, device,
-                          ctx: ParallelContext) -> list[torch.Tensor]:
+                          ctx: ParallelContext, before_last_backward=None) -> list[torch.Tensor]:
     """Run one 1F1B step over ``batches``; return the detached scaled losses (last stage).
 
     ``batches`` are ``(input_ids, labels)`` pairs, each ``[micro_batch, seq_len]``.
-    If ``model`` has a ``before_last_backward()`` method it is called right
-    before the final microbatch's backward (where overlapped gradient
-    reduction can start).
+    ``before_last_backward`` (or else a ``before_last_backward()`` method of
+    ``model``) is called right before the final microbatch's backward, where
+    overlapped gradient reduction can start; the argument form receives the
+    number of backwards already run in this step.
     """
     num_microbatches = len(batches)
     if num_microbatches == 0:
@@ -122,7 +123,10 @@ def forward_backward_1f1b(model: nn.Module, batches: Sequence[Batch], config, de
     sp = config.sequence_parallel and ctx.tp_size > 1
     seq = config.seq_len // (ctx.tp_size if sp else 1)
     p2p = _P2P(ctx, (seq, micro_batch_size, config.n_embd), config.activation_dtype, device)
-    hook = getattr(model, "before_last_backward", None)
+    hook = before_last_backward
+    if hook is None:
+        method = getattr(model, "before_last_backward", None)
+        hook = (lambda _prior: method()) if method is not None else None
 
     num_warmup = min(ctx.pp_size - ctx.pp_rank - 1, num_microbatches)
     num_steady = num_microbatches - num_warmup
@@ -136,7 +140,7 @@ def forward_backward_1f1b(model: nn.Module, batches: Sequence[Batch], config, de
         nonlocal backward_count
         backward_count += 1
         if hook is not None and backward_count == num_microbatches:
-            hook()
+            hook(num_microbatches - 1)
         return _backward_step(input_tensor, output_tensor, grad, ctx)
 
     def recv_forward():

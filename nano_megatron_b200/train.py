@@ -24,7 +24,8 @@ import torch.distributed as dist
 from .models import GPT, GPTConfig
 from .optim import FusedAdamW
 from .parallel import ParallelContext, init_parallel
-from .parallel.grads import (clip_coefficient, clip_grad_norm, finalize_gradients,
+from .models.functional import set_grad_observer
+from .parallel.grads import (GradBucketer, clip_coefficient, clip_grad_norm, finalize_gradients,
                              grad_norm_squared, synchronize_model_parameters)
 from .parallel.pipeline import forward_backward_1f1b
 from .utils.checkpoint import load_checkpoint, save_checkpoint
@@ -35,7 +36,8 @@ class Trainer:
     """One model stage, its optimizer and the per-step training procedure."""
 
     def __init__(self, config: GPTConfig, ctx: ParallelContext, device, *, lr: float = 3e-4,
-                 clip: float = 1.0, seed: int = 0, init_device=None, fused_tp: bool = True):
+                 clip: float = 1.0, seed: int = 0, init_device=None, fused_tp: bool = True,
+                 dp_bucket_mb: float = 128.0):
         self.config, self.ctx, self.clip = config, ctx, clip
         self.device = torch.device(device)
         if self.device.type == "cuda":
@@ -52,6 +54,16 @@ class Trainer:
             self.model = GPT(config, ctx).to(self.device)
         synchronize_model_parameters(self.model, ctx, tie_embeddings=config.tie_word_embeddings)
         self.optimizer = FusedAdamW(self.model, lr=lr)
+        # Data-parallel averaging bucket by bucket during the last backward.
+        # NCCL runs beside the compute stream only when no fused TP kernel
+        # (one resident CTA per SM, waiting for TP peers) runs in backward.
+        self.bucketer = None
+        if ctx.dp_size > 1 and dp_bucket_mb > 0 and getattr(self.model, "flat_buffers", None) is not None:
+            fused_in_backward = (self.device.type == "cuda" and fused_tp and ctx.tp_size > 1
+                                 and config.activation_dtype == torch.bfloat16)
+            self.bucketer = GradBucketer(self.model, ctx, bucket_bytes=int(dp_bucket_mb * (1 << 20)),
+                                         overlap=not fused_in_backward)
+            set_grad_observer(self.bucketer.observe)
 
     def to_device(self, batches):
         return [(x.to(self.device, non_blocking=True), y.to(self.device, non_blocking=True))
@@ -67,9 +79,13 @@ class Trainer:
         cfg, ctx, model = self.config, self.ctx, self.model
         self.optimizer.zero_grad()
         batches = self.to_device(batches)
-        losses = forward_backward_1f1b(model, batches, cfg, self.device, ctx)
+        bucketer = self.bucketer
+        losses = forward_backward_1f1b(model, batches, cfg, self.device, ctx,
+                                       before_last_backward=bucketer.before_last_backward if bucketer else None)
+        if bucketer is not None:
+            bucketer.finish()
         finalize_gradients(model, ctx, tie_embeddings=cfg.tie_word_embeddings,
-                           sequence_parallel=cfg.sequence_parallel)
+                           sequence_parallel=cfg.sequence_parallel, skip_data_parallel=bucketer is not None)
         if self.device.type == "cuda":
             # Norm on the device, coefficient applied inside the fused AdamW.
             if self.clip < 0:
@@ -112,7 +128,8 @@ def train(args):
               else torch.device(args.device))
     config = config_from_args(args)
     trainer = Trainer(config, ctx, device, lr=args.lr, clip=args.clip, seed=args.seed,
-                      init_device=args.init_device, fused_tp=not args.no_fused_tp)
+                      init_device=args.init_device, fused_tp=not args.no_fused_tp,
+                      dp_bucket_mb=args.dp_bucket_mb)
     stream = (TokenStream(args.data, dtype=args.data_dtype, seq_len=config.seq_len,
                           dp_rank=ctx.dp_rank, dp_size=ctx.dp_size) if args.data else None)
     training_state = {"lr": args.lr, "clip": args.clip, "micro_batch_size": args.micro_batch_size,
@@ -195,6 +212,9 @@ def build_parser():
     p.add_argument("--init-device", default=None,
                    help="initialize weights directly on this device (e.g. cuda) instead of CPU")
     p.add_argument("--timing", action="store_true", help="CUDA-event step time, max over ranks")
+    p.add_argument("--dp-bucket-mb", type=float, default=128.0,
+                   help="data-parallel gradient bucket size in MiB, reduced during the last backward "
+                        "(0: one all-reduce of the whole gradient buffer after backward)")
     p.add_argument("--no-fused-tp", action="store_true",
                    help="use NCCL collectives instead of the fused TP kernels")
     return p

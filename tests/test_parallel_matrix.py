@@ -33,7 +33,8 @@ import torch.multiprocessing as mp
 
 from nano_megatron_b200.models import GPT, GPTConfig
 from nano_megatron_b200.parallel import init_parallel
-from nano_megatron_b200.parallel.grads import (clip_grad_norm, finalize_gradients,
+from nano_megatron_b200.models.functional import set_grad_observer
+from nano_megatron_b200.parallel.grads import (GradBucketer, clip_grad_norm, finalize_gradients,
                                                synchronize_model_parameters)
 from nano_megatron_b200.parallel.pipeline import forward_backward_1f1b
 from tests.oracle import full_model, gather_tensor, parallel_model
@@ -113,13 +114,28 @@ def worker(rank, world, init_file, args, results):
         shapes = []
         hooks = [layer.register_forward_hook(lambda _m, _i, out: shapes.append(tuple(out.shape)))
                  for layer in model.layers]
-        losses = forward_backward_1f1b(model, batches, config, "cpu", ctx)
+        bucketer = None
+        if args.dp_bucket_bytes and ctx.dp_size > 1:
+            bucketer = GradBucketer(model, ctx, bucket_bytes=args.dp_bucket_bytes)
+            set_grad_observer(bucketer.observe)
+        losses = forward_backward_1f1b(model, batches, config, "cpu", ctx,
+                                       before_last_backward=bucketer.before_last_backward if bucketer else None)
         for h in hooks:
             h.remove()
+        if bucketer is not None:
+            started_in_backward = sum(bucketer.started)
+            bucketer.finish()
+            set_grad_observer(None)
+            if args.num_microbatches > 1 and started_in_backward == 0:
+                failures_pre = ["bucketer: no bucket started during the last backward"]
+            else:
+                failures_pre = []
+        else:
+            failures_pre = []
         finalize_gradients(model, ctx, tie_embeddings=True,
-                           sequence_parallel=config.sequence_parallel)
+                           sequence_parallel=config.sequence_parallel, skip_data_parallel=bucketer is not None)
 
-        failures = []
+        failures = list(failures_pre)
         seq = config.seq_len // (args.tp if config.sequence_parallel else 1)
         if any(s[0] != seq * args.micro_batch_size for s in shapes):
             failures.append(f"activation rows {[s[0] for s in shapes]} != {seq * args.micro_batch_size}")
@@ -193,7 +209,8 @@ def run_config(args, verbose=True) -> bool:
                 print(f"      FAIL {f}")
     ok = mismatches == 0 and not crashed and not timed_out and len(got) == world
     label = (f"tp={args.tp} pp={args.pp} dp={args.dp} M={args.num_microbatches} "
-             f"sp={int(args.sequence_parallel)} rc={int(args.recompute)}")
+             f"sp={int(args.sequence_parallel)} rc={int(args.recompute)}"
+             f"{' dp-buckets' if args.dp_bucket_bytes else ''}")
     detail = "" if ok else (f"  ({mismatches} mismatches, {len(crashed)} crashes, "
                             f"{len(timed_out)} timeouts, {world - len(got)} missing)")
     print(f"{'PASS' if ok else 'FAIL'}  {label}{detail}", flush=True)
@@ -208,6 +225,8 @@ MATRIX = [  # (tp, pp, dp, microbatches, sequence_parallel, recompute)
     (4, 1, 1, 4, True, False), (2, 2, 1, 4, True, False), (2, 2, 2, 2, True, False),
     (2, 2, 1, 2, True, True),
 ]
+# DP configs again with the gradient bucketer (small buckets: several per stage)
+MATRIX_BUCKETS = [(1, 1, 2, 4, False, False), (2, 2, 2, 2, True, False), (1, 2, 2, 1, False, False)]
 
 
 def build_parser():
@@ -228,6 +247,8 @@ def build_parser():
     p.add_argument("--sequence-parallel", action="store_true")
     p.add_argument("--recompute", action="store_true")
     p.add_argument("--timeout", type=float, default=180.0)
+    p.add_argument("--dp-bucket-bytes", type=int, default=0,
+                   help="reduce DP gradients with the bucketer, buckets of this many bytes")
     return p
 
 
@@ -236,26 +257,28 @@ def main():
     if not args.matrix:
         raise SystemExit(0 if run_config(args) else 1)
     results = []
-    for tp, pp, dp, m, sp, rc in MATRIX:
-        args.tp, args.pp, args.dp, args.num_microbatches = tp, pp, dp, m
-        args.sequence_parallel, args.recompute = sp, rc
-        results.append(run_config(args, verbose=False))
+    for buckets, configs in ((0, MATRIX), (4096, MATRIX_BUCKETS)):
+        for tp, pp, dp, m, sp, rc in configs:
+            args.tp, args.pp, args.dp, args.num_microbatches = tp, pp, dp, m
+            args.sequence_parallel, args.recompute, args.dp_bucket_bytes = sp, rc, buckets
+            results.append(run_config(args, verbose=False))
     print(f"\n{sum(results)}/{len(results)} configurations passed")
     raise SystemExit(0 if all(results) else 1)
 
 
 @pytest.mark.distributed
-@pytest.mark.parametrize("tp,pp,dp,sp,rc,ffn", [
-    (2, 1, 1, False, False, None),
-    (2, 2, 1, True, False, 48),
-    (2, 2, 2, True, True, None),
-    (1, 2, 2, False, False, None),
+@pytest.mark.parametrize("tp,pp,dp,sp,rc,ffn,buckets", [
+    (2, 1, 1, False, False, None, 0),
+    (2, 2, 1, True, False, 48, 0),
+    (2, 2, 2, True, True, None, 0),
+    (1, 2, 2, False, False, None, 0),
+    (2, 2, 2, True, False, None, 2048),
 ])
-def test_distributed_matrix(tp, pp, dp, sp, rc, ffn):
+def test_distributed_matrix(tp, pp, dp, sp, rc, ffn, buckets):
     args = build_parser().parse_args(["--n-embd=32", "--vocab-size=64", "--seq-len=8",
                                       "--micro-batch-size=1", "--num-microbatches=2"])
     args.tp, args.pp, args.dp, args.sequence_parallel, args.recompute = tp, pp, dp, sp, rc
-    args.ffn_hidden_size = ffn
+    args.ffn_hidden_size, args.dp_bucket_bytes = ffn, buckets
     assert run_config(args, verbose=True)
 
 
