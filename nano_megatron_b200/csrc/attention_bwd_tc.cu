@@ -15,9 +15,11 @@
 // a fixed summation order and no fp32 atomic traffic.
 //
 // Both kernels: warp 0 issues TMA loads (tiles straight out of qkv / dO via
-// 3-D tensor maps), warp 1 issues the MMAs, warps 2-5 do the elementwise work
-// and the epilogue. S/dP live in double-buffered TMEM so the next block's
-// products overlap the current block's elementwise work. Every wait is bounded.
+// 3-D tensor maps) through a 3-stage ring, warp 1 issues the MMAs from an event
+// loop, and two elementwise warpgroups (warps 2-5, 6-9) take alternate blocks,
+// each with its own TMEM columns and smem operand tiles, so one group's
+// exp/convert work overlaps the tensor core's products for the other. Every
+// wait is bounded.
 // D[q] = rowsum(dO * O) comes from flash_bwd_dot_kernel (attention.cu).
 
 #include <cuda.h>
@@ -35,7 +37,6 @@ namespace nmb {
 namespace {
 
 constexpr int HD = 128;
-constexpr int THREADS = 192;
 constexpr int BIG = 128, SMALL = 64;           // rows of the resident / streamed tiles
 constexpr int HALF_BIG = BIG * 128;            // 16 KB: one 64-column half of a 128-row tile
 constexpr int HALF_SMALL = SMALL * 128;        // 8 KB: one 64-column half of a 64-row tile
@@ -89,8 +90,6 @@ __device__ __forceinline__ void store_tmem_row(uint32_t taddr, __nv_bfloat16* ds
   }
 }
 
-// Named barrier over the 128 threads of warps 2-5.
-__device__ __forceinline__ void epilogue_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
 
 struct BwdArgs {
   const float* lse;   // [batch*heads, S]
@@ -315,26 +314,36 @@ flash_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tm_qkv_big, const __gr
 }
 
 // ================================================================= dQ kernel
-// smem: Q 32K | dO 32K | K[2] 2x16K | V[2] 2x16K | dS 16K
-constexpr int Q_OFF_Q = 0, Q_OFF_DO = TILE_BIG, Q_OFF_K = 2 * TILE_BIG, Q_OFF_V = Q_OFF_K + 2 * TILE_SMALL,
-              Q_OFF_DS = Q_OFF_V + 2 * TILE_SMALL, Q_OFF_BAR = Q_OFF_DS + BIG * 128;
+// One CTA = 128 queries of one (batch, head), looping over the 64-key blocks
+// up to the diagonal. Two elementwise warpgroups (warps 2-5 and 6-9) take
+// alternate key blocks, each with its own S/dP TMEM columns and dS smem tile,
+// so one group's exp/convert work overlaps the tensor core's work for the
+// other; warp 1 issues the MMAs from an event loop (S/dP of block ns as soon as
+// its group's columns are free and its K/V stage has landed, dQ += dS K of
+// block na as soon as its group published dS), and warp 0 streams K/V through
+// a 3-stage ring. dQ accumulates in TMEM in key-block order (deterministic).
+// smem: Q 32K | dO 32K | K[3] 3x16K | V[3] 3x16K | dS[2] 2x16K
+constexpr int Q_THREADS = 320;
+constexpr int Q_STAGES = 3;
+constexpr int Q_OFF_Q = 0, Q_OFF_DO = TILE_BIG, Q_OFF_K = 2 * TILE_BIG, Q_OFF_V = Q_OFF_K + Q_STAGES * TILE_SMALL,
+              Q_OFF_DS = Q_OFF_V + Q_STAGES * TILE_SMALL, Q_OFF_BAR = Q_OFF_DS + 2 * BIG * 128;
 constexpr int Q_SMEM = Q_OFF_BAR + 256 + 1024;
 
-__global__ void __launch_bounds__(THREADS, 1)
+__global__ void __launch_bounds__(Q_THREADS, 1)
 flash_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tm_qkv_big, const __grid_constant__ CUtensorMap tm_qkv_small,
                        const __grid_constant__ CUtensorMap tm_do_big, const BwdArgs a) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Q_OFF_BAR);
   uint64_t* qdo_full = bars;
-  uint64_t* kv_full = bars + 1;    // [2]
-  uint64_t* kv_empty = bars + 3;   // [2]
-  uint64_t* s_full = bars + 5;     // [2]
-  uint64_t* s_free = bars + 7;     // [2]
-  uint64_t* ds_full = bars + 9;
-  uint64_t* ds_free = bars + 10;
-  uint64_t* acc_done = bars + 11;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+  uint64_t* kv_full = bars + 1;    // [3]
+  uint64_t* kv_empty = bars + 4;   // [3]
+  uint64_t* st_full = bars + 7;    // [2] per group: S and dP ready
+  uint64_t* st_free = bars + 9;    // [2] per group: S and dP read
+  uint64_t* ds_full = bars + 11;   // [2] per group: dS in smem
+  uint64_t* ds_free = bars + 13;   // [2] per group: dQ product done with it
+  uint64_t* acc_done = bars + 15;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
@@ -346,14 +355,16 @@ flash_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tm_qkv_big, const __g
 
   if (threadIdx.x == 0) {
     mbar_init(qdo_full, 1);
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < Q_STAGES; ++i) {
       mbar_init(&kv_full[i], 1);
       mbar_init(&kv_empty[i], 1);
-      mbar_init(&s_full[i], 1);
-      mbar_init(&s_free[i], 128);
     }
-    mbar_init(ds_full, 128);
-    mbar_init(ds_free, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&st_full[i], 1);
+      mbar_init(&st_free[i], 128);
+      mbar_init(&ds_full[i], 128);
+      mbar_init(&ds_free[i], 1);
+    }
     mbar_init(acc_done, 1);
     *abort_flag = 0;
     fence_barrier_init();
@@ -365,19 +376,20 @@ flash_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tm_qkv_big, const __g
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const uint32_t tmem = *tmem_slot;  // S [0,64)+[64,128), dP [128,192)+[192,256), dQ [256,384)
+  // TMEM columns: S of group g at 64g, dP of group g at 128 + 64g, dQ at 256
+  const uint32_t tmem = *tmem_slot;
   const uint32_t sbase = smem_u32(smem);
 
   if (warp == 0 && lane == 0) {
-    int issued[2] = {-1, -1};
+    int issued[Q_STAGES] = {-1, -1, -1};
     mbar_arrive_expect_tx(qdo_full, 2 * TILE_BIG);
     tma_load_3d(smem + Q_OFF_Q, &tm_qkv_big, qdo_full, q_col, b, qb * BIG);
     tma_load_3d(smem + Q_OFF_Q + HALF_BIG, &tm_qkv_big, qdo_full, q_col + 64, b, qb * BIG);
     tma_load_3d(smem + Q_OFF_DO, &tm_do_big, qdo_full, do_col, b, qb * BIG);
     tma_load_3d(smem + Q_OFF_DO + HALF_BIG, &tm_do_big, qdo_full, do_col + 64, b, qb * BIG);
     for (int j = 0; j < nblk; ++j) {
-      const int st = j & 1;
-      if (!lane_wait(&kv_empty[st], ((j >> 1) & 1) ^ 1, a.err, abort_flag)) break;
+      const int st = j % Q_STAGES;
+      if (!lane_wait(&kv_empty[st], ((j / Q_STAGES) & 1) ^ 1, a.err, abort_flag)) break;
       uint8_t* kd = smem + Q_OFF_K + st * TILE_SMALL;
       uint8_t* vd = smem + Q_OFF_V + st * TILE_SMALL;
       mbar_arrive_expect_tx(&kv_full[st], 2 * TILE_SMALL);
@@ -385,64 +397,82 @@ flash_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tm_qkv_big, const __g
       tma_load_3d(kd + HALF_SMALL, &tm_qkv_small, &kv_full[st], k_col + 64, b, j * SMALL);
       tma_load_3d(vd, &tm_qkv_small, &kv_full[st], v_col, b, j * SMALL);
       tma_load_3d(vd + HALF_SMALL, &tm_qkv_small, &kv_full[st], v_col + 64, b, j * SMALL);
-      issued[st] = (j >> 1) & 1;
+      issued[st] = (j / Q_STAGES) & 1;
     }
     mbar_wait(qdo_full, 0, nullptr, 1000000000ull);
-    for (int st = 0; st < 2; ++st)
+    for (int st = 0; st < Q_STAGES; ++st)
       if (issued[st] >= 0) mbar_wait(&kv_full[st], issued[st], nullptr, 1000000000ull);
   } else if (warp == 1 && lane == 0) {
     constexpr uint32_t idesc_s = idesc_bf16_f32(BIG, SMALL, false, false);  // S, dP
     constexpr uint32_t idesc_q = idesc_bf16_f32(BIG, HD, false, true);      // dQ
     bool ok = lane_wait(qdo_full, 0, a.err, abort_flag);
-    for (int j = 0; ok && j <= nblk; ++j) {
-      if (j < nblk) {
-        const int st = j & 1;
-        if (!lane_wait(&kv_full[st], (j >> 1) & 1, a.err, abort_flag)) break;
-        if (!lane_wait(&s_free[st], ((j >> 1) & 1) ^ 1, a.err, abort_flag)) break;
-        tc_fence_after();
-        const uint32_t ks = sbase + Q_OFF_K + st * TILE_SMALL, vs = sbase + Q_OFF_V + st * TILE_SMALL;
+    int ns = 0, na = 0;
+    uint64_t idle_since = 0;
+    while (ok && na < nblk) {
+      bool progressed = false;
+      if (ns < nblk && ns < na + 2) {
+        const int g = ns & 1, st = ns % Q_STAGES;
+        if (mbar_try_wait(&kv_full[st], (ns / Q_STAGES) & 1) && mbar_try_wait(&st_free[g], ((ns >> 1) & 1) ^ 1)) {
+          tc_fence_after();
+          const uint32_t ks = sbase + Q_OFF_K + st * TILE_SMALL, vs = sbase + Q_OFF_V + st * TILE_SMALL;
 #pragma unroll
-        for (int kk = 0; kk < HD / 16; ++kk) {
-          mma_bf16_ss(tmem + st * SMALL, kmajor_desc(sbase + Q_OFF_Q, kk, HALF_BIG), kmajor_desc(ks, kk, HALF_SMALL),
-                      idesc_s, kk > 0);
-          mma_bf16_ss(tmem + 128 + st * SMALL, kmajor_desc(sbase + Q_OFF_DO, kk, HALF_BIG),
-                      kmajor_desc(vs, kk, HALF_SMALL), idesc_s, kk > 0);
+          for (int kk = 0; kk < HD / 16; ++kk) {
+            mma_bf16_ss(tmem + g * SMALL, kmajor_desc(sbase + Q_OFF_Q, kk, HALF_BIG),
+                        kmajor_desc(ks, kk, HALF_SMALL), idesc_s, kk > 0);
+            mma_bf16_ss(tmem + 128 + g * SMALL, kmajor_desc(sbase + Q_OFF_DO, kk, HALF_BIG),
+                        kmajor_desc(vs, kk, HALF_SMALL), idesc_s, kk > 0);
+          }
+          mma_commit(&st_full[g]);
+          ++ns;
+          progressed = true;
         }
-        mma_commit(&s_full[st]);
       }
-      if (j >= 1) {
-        const int p = j - 1, st = p & 1;
-        if (!lane_wait(ds_full, p & 1, a.err, abort_flag)) break;
-        tc_fence_after();
-        const uint32_t ks = sbase + Q_OFF_K + st * TILE_SMALL;
+      if (na < ns) {
+        const int g = na & 1, st = na % Q_STAGES;
+        if (mbar_try_wait(&ds_full[g], (na >> 1) & 1)) {
+          tc_fence_after();
+          const uint32_t ks = sbase + Q_OFF_K + st * TILE_SMALL, ds = sbase + Q_OFF_DS + g * BIG * 128;
 #pragma unroll
-        for (int kk = 0; kk < SMALL / 16; ++kk)
-          mma_bf16_ss(tmem + 256, smem_desc_sw128(sbase + Q_OFF_DS + kk * 32, 0, 1024),
-                      smem_desc_sw128(ks + kk * 2048, HALF_SMALL, 1024), idesc_q, (p > 0 || kk > 0));
-        mma_commit(ds_free);
-        mma_commit(&kv_empty[st]);
+          for (int kk = 0; kk < SMALL / 16; ++kk)
+            mma_bf16_ss(tmem + 256, smem_desc_sw128(ds + kk * 32, 0, 1024),
+                        smem_desc_sw128(ks + kk * 2048, HALF_SMALL, 1024), idesc_q, (na > 0 || kk > 0));
+          mma_commit(&ds_free[g]);
+          mma_commit(&kv_empty[st]);
+          ++na;
+          progressed = true;
+        }
+      }
+      if (progressed) {
+        idle_since = 0;
+      } else if (idle_since == 0) {
+        idle_since = globaltimer_ns();
+      } else if (*abort_flag || globaltimer_ns() - idle_since > 2000000000ull) {
+        report_error(a.err, kBarrierTimeout);
+        *abort_flag = 1;
+        ok = false;
       }
     }
     mma_commit(acc_done);
   } else if (warp >= 2) {
-    const int quarter = warp & 3;
+    const int g = (warp - 2) / 4;       // elementwise group
+    const int quarter = warp & 3;       // TMEM lane quarter this warp may access
     const int r = quarter * 32 + lane;  // query row
     const int q = qb * BIG + r;
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
     const float sl2 = a.scale * LOG2E;
-    const float lse2 = a.lse[(long)bh * a.S + q] * LOG2E;
+    const float lse2 = a.lse2[(long)bh * a.S + q];
     const float dq = a.dvec[(long)bh * a.S + q];
+    uint8_t* ds_tile = smem + Q_OFF_DS + g * BIG * 128;
     bool ok = true;
-    for (int j = 0; j < nblk && ok; ++j) {
-      const int st = j & 1;
-      ok = warp_wait(&s_full[st], (j >> 1) & 1, a.err, abort_flag);
+    for (int j = g, n = 0; j < nblk && ok; j += 2, ++n) {
+      ok = warp_wait(&st_full[g], n & 1, a.err, abort_flag);
       if (!ok) break;
       tc_fence_after();
       float s[SMALL], dp[SMALL];
-      ld_row64(tmem + lane_off + st * SMALL, s);
-      ld_row64(tmem + lane_off + 128 + st * SMALL, dp);
+      ld_row64(tmem + lane_off + g * SMALL, s);
+      ld_row64(tmem + lane_off + 128 + g * SMALL, dp);
       tc_fence_before();
-      mbar_arrive(&s_free[st]);
+      mbar_arrive(&st_free[g]);
       const bool diagonal = j * SMALL + SMALL > qb * BIG;
 #pragma unroll
       for (int c = 0; c < SMALL; ++c) {
@@ -450,18 +480,34 @@ flash_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tm_qkv_big, const __g
         if (diagonal && j * SMALL + c > q) pr = 0.f;
         dp[c] = pr * (dp[c] - dq);
       }
-      if (j > 0) {
-        ok = warp_wait(ds_free, (j - 1) & 1, a.err, abort_flag);
-        if (!ok) break;
-      }
-      store_row64(smem + Q_OFF_DS, r, dp);
+      if (n > 0) ok = warp_wait(&ds_free[g], (n - 1) & 1, a.err, abort_flag);
+      if (!ok) break;
+      store_row64(ds_tile, r, dp);
       fence_proxy_async_smem();
       tc_fence_before();
-      mbar_arrive(ds_full);
+      mbar_arrive(&ds_full[g]);
     }
     if (ok) ok = warp_wait(acc_done, 0, a.err, abort_flag);
     tc_fence_after();
-    store_tmem_row(tmem + lane_off + 256, a.dqkv + ((long)q * a.batch + b) * 3L * a.heads * HD + q_col, a.scale, ok);
+    // group g writes columns [64g, 64g + 64) of the dQ row
+    __nv_bfloat16* dst = a.dqkv + ((long)q * a.batch + b) * 3L * a.heads * HD + q_col + g * 64;
+#pragma unroll
+    for (int c = 0; c < 64; c += 32) {
+      uint32_t v[32];
+      tmem_ld_32x32b_x32(tmem + lane_off + 256 + g * 64 + c, v);
+      tmem_wait_ld_regs(v);
+      if (ok) {
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          uint4 u;
+          u.x = pack_bf16x2(__uint_as_float(v[8 * k + 0]) * a.scale, __uint_as_float(v[8 * k + 1]) * a.scale);
+          u.y = pack_bf16x2(__uint_as_float(v[8 * k + 2]) * a.scale, __uint_as_float(v[8 * k + 3]) * a.scale);
+          u.z = pack_bf16x2(__uint_as_float(v[8 * k + 4]) * a.scale, __uint_as_float(v[8 * k + 5]) * a.scale);
+          u.w = pack_bf16x2(__uint_as_float(v[8 * k + 6]) * a.scale, __uint_as_float(v[8 * k + 7]) * a.scale);
+          *reinterpret_cast<uint4*>(dst + c + 8 * k) = u;
+        }
+      }
+    }
   }
 
   tc_fence_before();
@@ -515,7 +561,7 @@ cudaError_t flash_attn_bwd_tc(const __nv_bfloat16* dout, const __nv_bfloat16* qk
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   dim3 grid_q(S / BIG, batch * heads);
-  flash_bwd_dq_tc_kernel<<<grid_q, THREADS, Q_SMEM, stream>>>(qkv_big, qkv_small, do_big, a);
+  flash_bwd_dq_tc_kernel<<<grid_q, Q_THREADS, Q_SMEM, stream>>>(qkv_big, qkv_small, do_big, a);
   return cudaGetLastError();
 }
 
