@@ -58,14 +58,22 @@ __device__ __forceinline__ void store_row64(uint8_t* tile, int r, const float (&
   }
 }
 
-__device__ __forceinline__ void ld_row64(uint32_t taddr, float (&v)[SMALL]) {
+// Two 64-column fp32 TMEM rows (S and dP of one block): all four loads are in
+// flight before the single wait.
+__device__ __forceinline__ void ld_two_rows64(uint32_t ta, uint32_t tb, float (&x)[SMALL], float (&y)[SMALL]) {
+  uint32_t u[4][32];
+  tmem_ld_32x32b_x32(ta, u[0]);
+  tmem_ld_32x32b_x32(ta + 32, u[1]);
+  tmem_ld_32x32b_x32(tb, u[2]);
+  tmem_ld_32x32b_x32(tb + 32, u[3]);
 #pragma unroll
-  for (int c = 0; c < SMALL; c += 32) {
-    uint32_t u[32];
-    tmem_ld_32x32b_x32(taddr + c, u);
-    tmem_wait_ld();
+  for (int c = 0; c < 4; ++c) tmem_wait_ld_regs(u[c]);
 #pragma unroll
-    for (int i = 0; i < 32; ++i) v[c + i] = __uint_as_float(u[i]);
+  for (int i = 0; i < 32; ++i) {
+    x[i] = __uint_as_float(u[0][i]);
+    x[32 + i] = __uint_as_float(u[1][i]);
+    y[i] = __uint_as_float(u[2][i]);
+    y[32 + i] = __uint_as_float(u[3][i]);
   }
 }
 
@@ -243,12 +251,16 @@ flash_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tm_qkv_big, const __gr
       }
       if (progressed) {
         idle_since = 0;
-      } else if (idle_since == 0) {
-        idle_since = globaltimer_ns();
-      } else if (*abort_flag || globaltimer_ns() - idle_since > 2000000000ull) {
-        report_error(a.err, kBarrierTimeout);
-        *abort_flag = 1;
-        ok = false;
+      } else {
+        // nothing ready: back off briefly so the elementwise warps keep the issue slots
+        if (idle_since == 0) {
+          idle_since = globaltimer_ns();
+        } else if (*abort_flag || globaltimer_ns() - idle_since > 2000000000ull) {
+          report_error(a.err, kBarrierTimeout);
+          *abort_flag = 1;
+          ok = false;
+        }
+        __nanosleep(32);
       }
     }
     mma_commit(acc_done);
@@ -271,8 +283,7 @@ flash_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tm_qkv_big, const __gr
       if (!ok) break;
       tc_fence_after();
       float s[SMALL], dp[SMALL];
-      ld_row64(tmem + lane_off + g * SMALL, s);
-      ld_row64(tmem + lane_off + 128 + g * SMALL, dp);
+      ld_two_rows64(tmem + lane_off + g * SMALL, tmem + lane_off + 128 + g * SMALL, s, dp);
       tc_fence_before();
       mbar_arrive(&st_free[g]);
       const bool diagonal = q0 < kb * BIG + BIG;  // some key of this block is after some query
@@ -444,12 +455,16 @@ flash_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tm_qkv_big, const __g
       }
       if (progressed) {
         idle_since = 0;
-      } else if (idle_since == 0) {
-        idle_since = globaltimer_ns();
-      } else if (*abort_flag || globaltimer_ns() - idle_since > 2000000000ull) {
-        report_error(a.err, kBarrierTimeout);
-        *abort_flag = 1;
-        ok = false;
+      } else {
+        // nothing ready: back off briefly so the elementwise warps keep the issue slots
+        if (idle_since == 0) {
+          idle_since = globaltimer_ns();
+        } else if (*abort_flag || globaltimer_ns() - idle_since > 2000000000ull) {
+          report_error(a.err, kBarrierTimeout);
+          *abort_flag = 1;
+          ok = false;
+        }
+        __nanosleep(32);
       }
     }
     mma_commit(acc_done);
@@ -469,8 +484,7 @@ flash_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tm_qkv_big, const __g
       if (!ok) break;
       tc_fence_after();
       float s[SMALL], dp[SMALL];
-      ld_row64(tmem + lane_off + g * SMALL, s);
-      ld_row64(tmem + lane_off + 128 + g * SMALL, dp);
+      ld_two_rows64(tmem + lane_off + g * SMALL, tmem + lane_off + 128 + g * SMALL, s, dp);
       tc_fence_before();
       mbar_arrive(&st_free[g]);
       const bool diagonal = j * SMALL + SMALL > qb * BIG;
