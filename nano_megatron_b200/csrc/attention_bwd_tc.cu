@@ -43,19 +43,12 @@ constexpr int HALF_SMALL = SMALL * 128;        // 8 KB: one 64-column half of a 
 constexpr int TILE_BIG = 2 * HALF_BIG, TILE_SMALL = 2 * HALF_SMALL;
 constexpr float LOG2E = 1.4426950408889634f;
 
-// Row `r` of a [rows][64] bf16 K-major SW128 operand (128-byte rows): 16-byte
-// chunk `ch` of the row is stored at chunk position ch ^ (r % 8).
-__device__ __forceinline__ void store_row64(uint8_t* tile, int r, const float (&v)[SMALL]) {
-  uint8_t* row = tile + r * 128;
+// 64 values of a row as bf16 pairs into 32 TMEM columns at `taddr`.
+__device__ __forceinline__ void st_row64(uint32_t taddr, const float (&v)[SMALL]) {
+  uint32_t u[32];
 #pragma unroll
-  for (int ch = 0; ch < SMALL / 8; ++ch) {
-    uint4 u;
-    u.x = pack_bf16x2(v[8 * ch + 0], v[8 * ch + 1]);
-    u.y = pack_bf16x2(v[8 * ch + 2], v[8 * ch + 3]);
-    u.z = pack_bf16x2(v[8 * ch + 4], v[8 * ch + 5]);
-    u.w = pack_bf16x2(v[8 * ch + 6], v[8 * ch + 7]);
-    *reinterpret_cast<uint4*>(row + ((ch ^ (r & 7)) << 4)) = u;
-  }
+  for (int i = 0; i < 32; ++i) u[i] = pack_bf16x2(v[2 * i], v[2 * i + 1]);
+  tmem_st_32x32b_x32(taddr, u);
 }
 
 // Two 64-column fp32 TMEM rows (S and dP of one block): all four loads are in
@@ -111,16 +104,17 @@ struct BwdArgs {
 
 // ============================================================ dK / dV kernel
 // Two elementwise warpgroups (warps 2-5 and 6-9) take alternate 64-query
-// blocks, each with its own S^T/dP^T TMEM columns and P^T/dS^T smem tiles, so
-// one group's exp/convert work overlaps the tensor core's work for the other.
-// smem: K 32K | V 32K | Q[3] 3x16K | dO[3] 3x16K | P^T[2] 2x16K | dS^T[2] 2x16K | lse2,D[3]
+// blocks, each with its own S^T/dP^T TMEM columns, so one group's exp/convert
+// work overlaps the tensor core's work for the other. P^T and dS^T go back
+// into TMEM (bf16, over the S^T/dP^T columns just read) and are the A
+// operands of the dV/dK products: no shared-memory round trip.
+// smem: K 32K | V 32K | Q[4] 4x16K | dO[4] 4x16K | lse2,D[4]
 // (lse2 = lse * log2(e) and D of a query block travel with its Q/dO stage)
 constexpr int KV_THREADS = 320;
-constexpr int KV_STAGES = 3;
+constexpr int KV_STAGES = 4;
 constexpr int KV_OFF_K = 0, KV_OFF_V = TILE_BIG, KV_OFF_Q = 2 * TILE_BIG,
-              KV_OFF_DO = KV_OFF_Q + KV_STAGES * TILE_SMALL, KV_OFF_PT = KV_OFF_DO + KV_STAGES * TILE_SMALL,
-              KV_OFF_DST = KV_OFF_PT + 2 * BIG * 128,
-              KV_OFF_LD = KV_OFF_DST + 2 * BIG * 128, KV_OFF_BAR = KV_OFF_LD + KV_STAGES * 2 * SMALL * 4;
+              KV_OFF_DO = KV_OFF_Q + KV_STAGES * TILE_SMALL,
+              KV_OFF_LD = KV_OFF_DO + KV_STAGES * TILE_SMALL, KV_OFF_BAR = KV_OFF_LD + KV_STAGES * 2 * SMALL * 4;
 constexpr int KV_SMEM = KV_OFF_BAR + 256 + 1024;
 
 __global__ void __launch_bounds__(KV_THREADS, 1)
@@ -129,15 +123,13 @@ flash_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tm_qkv_big, const __gr
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + KV_OFF_BAR);
-  uint64_t* kv_full = bars;         // K and V
-  uint64_t* qdo_full = bars + 1;    // [3] Q/dO stage i % 3
-  uint64_t* qdo_empty = bars + 4;   // [3]
-  uint64_t* st_full = bars + 7;     // [2] per group: S^T and dP^T ready
-  uint64_t* st_free = bars + 9;     // [2] per group: S^T and dP^T read
-  uint64_t* pds_full = bars + 11;   // [2] per group: P^T and dS^T in smem
-  uint64_t* pds_free = bars + 13;   // [2] per group: dV/dK products done with them
-  uint64_t* acc_done = bars + 15;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
+  uint64_t* kv_full = bars;                        // K and V
+  uint64_t* qdo_full = bars + 1;                   // [KV_STAGES] Q/dO stage i % KV_STAGES
+  uint64_t* qdo_empty = qdo_full + KV_STAGES;      // [KV_STAGES]
+  uint64_t* st_full = qdo_empty + KV_STAGES;       // [2] per group: S^T and dP^T ready
+  uint64_t* pds_full = st_full + 2;                // [2] per group: P^T and dS^T in TMEM
+  uint64_t* acc_done = pds_full + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_done + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
@@ -155,9 +147,7 @@ flash_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tm_qkv_big, const __gr
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&st_full[i], 1);
-      mbar_init(&st_free[i], 128);
       mbar_init(&pds_full[i], 128);
-      mbar_init(&pds_free[i], 1);
     }
     mbar_init(acc_done, 1);
     *abort_flag = 0;
@@ -170,12 +160,14 @@ flash_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tm_qkv_big, const __gr
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  // TMEM columns: S^T of group g at 64g, dP^T of group g at 128 + 64g, dV 256, dK 384
+  // TMEM columns: S^T|P^T of group g at 64g, dP^T|dS^T of group g at 128 + 64g, dV 256, dK 384
   const uint32_t tmem = *tmem_slot;
   const uint32_t sbase = smem_u32(smem);
 
   if (warp == 0 && lane == 0) {
-    int issued[KV_STAGES] = {-1, -1, -1};
+    int issued[KV_STAGES];
+#pragma unroll
+    for (int st = 0; st < KV_STAGES; ++st) issued[st] = -1;
     mbar_arrive_expect_tx(kv_full, 2 * TILE_BIG);
     tma_load_3d(smem + KV_OFF_K, &tm_qkv_big, kv_full, k_col, b, kb * BIG);
     tma_load_3d(smem + KV_OFF_K + HALF_BIG, &tm_qkv_big, kv_full, k_col + 64, b, kb * BIG);
@@ -212,9 +204,11 @@ flash_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tm_qkv_big, const __gr
     uint64_t idle_since = 0;
     while (ok && na < nblk) {
       bool progressed = false;
+      // S^T(ns) reuses the TMEM columns of block ns-2 of the same group, whose
+      // dV/dK products (the readers of P^T/dS^T there) were issued before it.
       if (ns < nblk && ns < na + 2) {
         const int g = ns & 1, st = ns % KV_STAGES;
-        if (mbar_try_wait(&qdo_full[st], (ns / KV_STAGES) & 1) && mbar_try_wait(&st_free[g], ((ns >> 1) & 1) ^ 1)) {
+        if (mbar_try_wait(&qdo_full[st], (ns / KV_STAGES) & 1)) {
           tc_fence_after();
           const uint32_t qs = sbase + KV_OFF_Q + st * TILE_SMALL, ds = sbase + KV_OFF_DO + st * TILE_SMALL;
 #pragma unroll
@@ -234,16 +228,15 @@ flash_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tm_qkv_big, const __gr
         if (mbar_try_wait(&pds_full[g], (na >> 1) & 1)) {
           tc_fence_after();
           const uint32_t qs = sbase + KV_OFF_Q + st * TILE_SMALL, ds = sbase + KV_OFF_DO + st * TILE_SMALL;
-          const uint32_t pt = sbase + KV_OFF_PT + g * BIG * 128, dst = sbase + KV_OFF_DST + g * BIG * 128;
 #pragma unroll
           for (int kk = 0; kk < SMALL / 16; ++kk) {
+            // A = P^T / dS^T in TMEM (bf16 pairs, 8 columns per k-step);
             // B = dO / Q block viewed N-major: [2 d-halves][64 q rows][128 B]
-            mma_bf16_ss(tmem + 256, smem_desc_sw128(pt + kk * 32, 0, 1024),
-                        smem_desc_sw128(ds + kk * 2048, HALF_SMALL, 1024), idesc_acc, (na > 0 || kk > 0));
-            mma_bf16_ss(tmem + 384, smem_desc_sw128(dst + kk * 32, 0, 1024),
+            mma_bf16_ts(tmem + 256, tmem + g * SMALL + kk * 8, smem_desc_sw128(ds + kk * 2048, HALF_SMALL, 1024),
+                        idesc_acc, (na > 0 || kk > 0));
+            mma_bf16_ts(tmem + 384, tmem + 128 + g * SMALL + kk * 8,
                         smem_desc_sw128(qs + kk * 2048, HALF_SMALL, 1024), idesc_acc, (na > 0 || kk > 0));
           }
-          mma_commit(&pds_free[g]);
           mma_commit(&qdo_empty[st]);
           ++na;
           progressed = true;
@@ -271,8 +264,6 @@ flash_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tm_qkv_big, const __gr
     const int key = kb * BIG + r;
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
     const float sl2 = a.scale * LOG2E;
-    uint8_t* pt_tile = smem + KV_OFF_PT + g * BIG * 128;
-    uint8_t* dst_tile = smem + KV_OFF_DST + g * BIG * 128;
     bool ok = true;
     for (int i = g, n = 0; i < nblk && ok; i += 2, ++n) {
       const int q0 = (first_qb + i) * SMALL;
@@ -283,9 +274,8 @@ flash_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tm_qkv_big, const __gr
       if (!ok) break;
       tc_fence_after();
       float s[SMALL], dp[SMALL];
-      ld_two_rows64(tmem + lane_off + g * SMALL, tmem + lane_off + 128 + g * SMALL, s, dp);
-      tc_fence_before();
-      mbar_arrive(&st_free[g]);
+      const uint32_t s_addr = tmem + lane_off + g * SMALL, dp_addr = tmem + lane_off + 128 + g * SMALL;
+      ld_two_rows64(s_addr, dp_addr, s, dp);
       const bool diagonal = q0 < kb * BIG + BIG;  // some key of this block is after some query
 #pragma unroll
       for (int c = 0; c < SMALL; c += 4) {
@@ -300,11 +290,10 @@ flash_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tm_qkv_big, const __gr
           dp[c + k] = pr * (dp[c + k] - dv[k]);
         }
       }
-      if (n > 0) ok = warp_wait(&pds_free[g], (n - 1) & 1, a.err, abort_flag);
-      if (!ok) break;
-      store_row64(pt_tile, r, s);
-      store_row64(dst_tile, r, dp);
-      fence_proxy_async_smem();
+      // P^T and dS^T (bf16) over the first half of the S^T / dP^T columns just read
+      st_row64(s_addr, s);
+      st_row64(dp_addr, dp);
+      tmem_wait_st();
       tc_fence_before();
       mbar_arrive(&pds_full[g]);
     }
@@ -327,17 +316,19 @@ flash_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tm_qkv_big, const __gr
 // ================================================================= dQ kernel
 // One CTA = 128 queries of one (batch, head), looping over the 64-key blocks
 // up to the diagonal. Two elementwise warpgroups (warps 2-5 and 6-9) take
-// alternate key blocks, each with its own S/dP TMEM columns and dS smem tile,
-// so one group's exp/convert work overlaps the tensor core's work for the
-// other; warp 1 issues the MMAs from an event loop (S/dP of block ns as soon as
-// its group's columns are free and its K/V stage has landed, dQ += dS K of
-// block na as soon as its group published dS), and warp 0 streams K/V through
-// a 3-stage ring. dQ accumulates in TMEM in key-block order (deterministic).
-// smem: Q 32K | dO 32K | K[3] 3x16K | V[3] 3x16K | dS[2] 2x16K
+// alternate key blocks, each with its own S/dP TMEM columns, so one group's
+// exp/convert work overlaps the tensor core's work for the other; dS goes back
+// into TMEM (bf16, over the dP columns just read) as the A operand of the dQ
+// product. Warp 1 issues the MMAs from an event loop (S/dP of block ns as soon
+// as its K/V stage has landed and block ns-2's dQ product was issued, dQ += dS
+// K of block na as soon as its group published dS), and warp 0 streams K/V
+// through a 4-stage ring. dQ accumulates in TMEM in key-block order
+// (deterministic).
+// smem: Q 32K | dO 32K | K[4] 4x16K | V[4] 4x16K
 constexpr int Q_THREADS = 320;
-constexpr int Q_STAGES = 3;
+constexpr int Q_STAGES = 4;
 constexpr int Q_OFF_Q = 0, Q_OFF_DO = TILE_BIG, Q_OFF_K = 2 * TILE_BIG, Q_OFF_V = Q_OFF_K + Q_STAGES * TILE_SMALL,
-              Q_OFF_DS = Q_OFF_V + Q_STAGES * TILE_SMALL, Q_OFF_BAR = Q_OFF_DS + 2 * BIG * 128;
+              Q_OFF_BAR = Q_OFF_V + Q_STAGES * TILE_SMALL;
 constexpr int Q_SMEM = Q_OFF_BAR + 256 + 1024;
 
 __global__ void __launch_bounds__(Q_THREADS, 1)
@@ -347,14 +338,12 @@ flash_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tm_qkv_big, const __g
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Q_OFF_BAR);
   uint64_t* qdo_full = bars;
-  uint64_t* kv_full = bars + 1;    // [3]
-  uint64_t* kv_empty = bars + 4;   // [3]
-  uint64_t* st_full = bars + 7;    // [2] per group: S and dP ready
-  uint64_t* st_free = bars + 9;    // [2] per group: S and dP read
-  uint64_t* ds_full = bars + 11;   // [2] per group: dS in smem
-  uint64_t* ds_free = bars + 13;   // [2] per group: dQ product done with it
-  uint64_t* acc_done = bars + 15;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
+  uint64_t* kv_full = bars + 1;                // [Q_STAGES]
+  uint64_t* kv_empty = kv_full + Q_STAGES;     // [Q_STAGES]
+  uint64_t* st_full = kv_empty + Q_STAGES;     // [2] per group: S and dP ready
+  uint64_t* ds_full = st_full + 2;             // [2] per group: dS in TMEM
+  uint64_t* acc_done = ds_full + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_done + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
@@ -372,9 +361,7 @@ flash_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tm_qkv_big, const __g
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&st_full[i], 1);
-      mbar_init(&st_free[i], 128);
       mbar_init(&ds_full[i], 128);
-      mbar_init(&ds_free[i], 1);
     }
     mbar_init(acc_done, 1);
     *abort_flag = 0;
@@ -387,12 +374,14 @@ flash_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tm_qkv_big, const __g
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  // TMEM columns: S of group g at 64g, dP of group g at 128 + 64g, dQ at 256
+  // TMEM columns: S of group g at 64g, dP|dS of group g at 128 + 64g, dQ at 256
   const uint32_t tmem = *tmem_slot;
   const uint32_t sbase = smem_u32(smem);
 
   if (warp == 0 && lane == 0) {
-    int issued[Q_STAGES] = {-1, -1, -1};
+    int issued[Q_STAGES];
+#pragma unroll
+    for (int st = 0; st < Q_STAGES; ++st) issued[st] = -1;
     mbar_arrive_expect_tx(qdo_full, 2 * TILE_BIG);
     tma_load_3d(smem + Q_OFF_Q, &tm_qkv_big, qdo_full, q_col, b, qb * BIG);
     tma_load_3d(smem + Q_OFF_Q + HALF_BIG, &tm_qkv_big, qdo_full, q_col + 64, b, qb * BIG);
@@ -423,7 +412,7 @@ flash_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tm_qkv_big, const __g
       bool progressed = false;
       if (ns < nblk && ns < na + 2) {
         const int g = ns & 1, st = ns % Q_STAGES;
-        if (mbar_try_wait(&kv_full[st], (ns / Q_STAGES) & 1) && mbar_try_wait(&st_free[g], ((ns >> 1) & 1) ^ 1)) {
+        if (mbar_try_wait(&kv_full[st], (ns / Q_STAGES) & 1)) {
           tc_fence_after();
           const uint32_t ks = sbase + Q_OFF_K + st * TILE_SMALL, vs = sbase + Q_OFF_V + st * TILE_SMALL;
 #pragma unroll
@@ -442,12 +431,11 @@ flash_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tm_qkv_big, const __g
         const int g = na & 1, st = na % Q_STAGES;
         if (mbar_try_wait(&ds_full[g], (na >> 1) & 1)) {
           tc_fence_after();
-          const uint32_t ks = sbase + Q_OFF_K + st * TILE_SMALL, ds = sbase + Q_OFF_DS + g * BIG * 128;
+          const uint32_t ks = sbase + Q_OFF_K + st * TILE_SMALL;
 #pragma unroll
           for (int kk = 0; kk < SMALL / 16; ++kk)
-            mma_bf16_ss(tmem + 256, smem_desc_sw128(ds + kk * 32, 0, 1024),
-                        smem_desc_sw128(ks + kk * 2048, HALF_SMALL, 1024), idesc_q, (na > 0 || kk > 0));
-          mma_commit(&ds_free[g]);
+            mma_bf16_ts(tmem + 256, tmem + 128 + g * SMALL + kk * 8, smem_desc_sw128(ks + kk * 2048, HALF_SMALL, 1024),
+                        idesc_q, (na > 0 || kk > 0));
           mma_commit(&kv_empty[st]);
           ++na;
           progressed = true;
@@ -477,16 +465,14 @@ flash_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tm_qkv_big, const __g
     const float sl2 = a.scale * LOG2E;
     const float lse2 = a.lse2[(long)bh * a.S + q];
     const float dq = a.dvec[(long)bh * a.S + q];
-    uint8_t* ds_tile = smem + Q_OFF_DS + g * BIG * 128;
     bool ok = true;
     for (int j = g, n = 0; j < nblk && ok; j += 2, ++n) {
       ok = warp_wait(&st_full[g], n & 1, a.err, abort_flag);
       if (!ok) break;
       tc_fence_after();
       float s[SMALL], dp[SMALL];
-      ld_two_rows64(tmem + lane_off + g * SMALL, tmem + lane_off + 128 + g * SMALL, s, dp);
-      tc_fence_before();
-      mbar_arrive(&st_free[g]);
+      const uint32_t dp_addr = tmem + lane_off + 128 + g * SMALL;
+      ld_two_rows64(tmem + lane_off + g * SMALL, dp_addr, s, dp);
       const bool diagonal = j * SMALL + SMALL > qb * BIG;
 #pragma unroll
       for (int c = 0; c < SMALL; ++c) {
@@ -494,10 +480,8 @@ flash_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tm_qkv_big, const __g
         if (diagonal && j * SMALL + c > q) pr = 0.f;
         dp[c] = pr * (dp[c] - dq);
       }
-      if (n > 0) ok = warp_wait(&ds_free[g], (n - 1) & 1, a.err, abort_flag);
-      if (!ok) break;
-      store_row64(ds_tile, r, dp);
-      fence_proxy_async_smem();
+      st_row64(dp_addr, dp);  // dS (bf16) over the dP columns just read
+      tmem_wait_st();
       tc_fence_before();
       mbar_arrive(&ds_full[g]);
     }
