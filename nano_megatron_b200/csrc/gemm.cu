@@ -8,7 +8,11 @@
 //   warp 1      MMA issuer: tcgen05.mma 128x256x16 per k-step into one of two
 //               TMEM accumulators (2 x 256 columns), commits free the smem
 //               stage and, at the end of a tile, hand the accumulator over.
-//   warps 2-5   epilogue: tcgen05.ld 32 columns at a time, convert, store;
+//   warps 2-5   epilogue: tcgen05.ld the accumulator rows, convert, and stage
+//               32-row boxes in 128-byte-swizzled shared memory (two 4 KB
+//               buffers per warp), from which TMA stores them -- or, for the
+//               fp32 accumulate mode, TMA-reduce-adds them into C, so the
+//               read-modify-write happens in L2 instead of through the SMs;
 //               overlaps the next tile's MMAs (double-buffered accumulator).
 //
 // Operand majorness is a template parameter, so one kernel covers the three
@@ -37,7 +41,9 @@ constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4;
 constexpr int A_TILE_BYTES = BM * BK * 2;  // 16 KB
 constexpr int B_TILE_BYTES = BN * BK * 2;  // 32 KB
 constexpr int STAGE_BYTES = A_TILE_BYTES + B_TILE_BYTES;
-constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+constexpr int STG_BUF = 4096;                 // one staged box: 32 rows x 128 B
+constexpr int STAGING_BYTES = 4 * 2 * STG_BUF;  // two buffers per epilogue warp
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + STAGING_BYTES + 1024 /*align*/ + 256 /*barriers*/;
 constexpr int THREADS = 192;
 constexpr int GROUP_M = 16;
 
@@ -53,11 +59,12 @@ __device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int& tm
 
 template <bool A_MN, bool B_MN, int OUT>
 __global__ void __launch_bounds__(THREADS, 1)
-gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, void* C,
-                 long ldc, int M, int N, int K, int* err) {
+gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                 const __grid_constant__ CUtensorMap tmC, int M, int N, int K, int* err) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+  uint8_t* staging = smem + STAGES * STAGE_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(staging + STAGING_BYTES);
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
@@ -158,6 +165,9 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
   } else if (warp >= 2) {
     // ------------------------------------------------------------- epilogue
     const int quarter = warp & 3;  // TMEM lanes [32*quarter, 32*quarter+32)
+    uint8_t* stg = staging + quarter * 2 * STG_BUF;
+    constexpr int CW = OUT == 0 ? 64 : 32;  // columns per staged box (128 B of a row)
+    int nbox = 0;
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
@@ -166,49 +176,51 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
       tile_coords(t, num_m, num_n, tm, tn);
       if (!mbar_wait(&tfull[acc], acc_phase, err)) { *abort_flag = 1; break; }
       tc_fence_after();
-      const int row = tm * BM + quarter * 32 + lane;
+      const int row0 = tm * BM + quarter * 32;
       const uint32_t t_row = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN;
 #pragma unroll 1
-      for (int c = 0; c < BN; c += 32) {
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(t_row + c, r);
-        tmem_wait_ld();
-        const int col = tn * BN + c;
-        if (row < M && col < N) {
+      for (int c = 0; c < BN; c += CW) {
+        uint32_t r[CW];
+        tmem_ld_32x32b_x32(t_row + c, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
+        if (OUT == 0) tmem_ld_32x32b_x32(t_row + c + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32 % CW]));
+        tmem_wait_ld_regs(*reinterpret_cast<uint32_t(*)[32]>(&r[0]));
+        if (OUT == 0) tmem_wait_ld_regs(*reinterpret_cast<uint32_t(*)[32]>(&r[32 % CW]));
+        uint8_t* buf = stg + (nbox & 1) * STG_BUF;
+        // the box stored from this buffer two boxes ago must have been read out
+        if (lane == 0) bulk_wait_group_read<1>();
+        __syncwarp();
+        uint8_t* row = buf + lane * 128;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          uint4 u;
           if (OUT == 0) {
-            __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(C) + (long)row * ldc + col;
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              if (col + 8 * j < N) {
-                uint4 v;
-                v.x = pack_bf16x2(__uint_as_float(r[8 * j + 0]), __uint_as_float(r[8 * j + 1]));
-                v.y = pack_bf16x2(__uint_as_float(r[8 * j + 2]), __uint_as_float(r[8 * j + 3]));
-                v.z = pack_bf16x2(__uint_as_float(r[8 * j + 4]), __uint_as_float(r[8 * j + 5]));
-                v.w = pack_bf16x2(__uint_as_float(r[8 * j + 6]), __uint_as_float(r[8 * j + 7]));
-                *reinterpret_cast<uint4*>(out + 8 * j) = v;
-              }
-            }
+            u.x = pack_bf16x2(__uint_as_float(r[8 * j + 0]), __uint_as_float(r[8 * j + 1]));
+            u.y = pack_bf16x2(__uint_as_float(r[8 * j + 2]), __uint_as_float(r[8 * j + 3]));
+            u.z = pack_bf16x2(__uint_as_float(r[8 * j + 4]), __uint_as_float(r[8 * j + 5]));
+            u.w = pack_bf16x2(__uint_as_float(r[8 * j + 6]), __uint_as_float(r[8 * j + 7]));
           } else {
-            float* out = reinterpret_cast<float*>(C) + (long)row * ldc + col;
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-              if (col + 4 * j < N) {
-                float4 v = make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
-                                       __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3]));
-                if (OUT == 2) {
-                  const float4 o = *reinterpret_cast<const float4*>(out + 4 * j);
-                  v.x += o.x; v.y += o.y; v.z += o.z; v.w += o.w;
-                }
-                *reinterpret_cast<float4*>(out + 4 * j) = v;
-              }
-            }
+            u = make_uint4(r[4 * j], r[4 * j + 1], r[4 * j + 2], r[4 * j + 3]);
           }
+          *reinterpret_cast<uint4*>(row + ((j ^ (lane & 7)) << 4)) = u;
         }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          const int col = tn * BN + c;
+          if (col < N && row0 < M) {  // boxes past the edge are skipped; partial ones are clipped by TMA
+            if (OUT == 2) tma_reduce_add_2d(&tmC, buf, col, row0);
+            else tma_store_2d(&tmC, buf, col, row0);
+          }
+          bulk_commit_group();
+        }
+        ++nbox;
       }
       tc_fence_before();
       mbar_arrive(&tempty[acc]);
       if (++acc == 2) { acc = 0; acc_phase ^= 1; }
     }
+    // every store / reduce must be complete before the CTA (and its smem) goes
+    if (lane == 0) bulk_wait_group<0>();
   }
 
   tc_fence_before();
@@ -250,7 +262,9 @@ cudaError_t launch(const GemmArgs& g, cudaStream_t stream) {
   if (!make_tmap_bf16_2d(&tb, g.B, B_MN ? g.N : g.K, B_MN ? g.K : g.N, g.ldb, 64, B_MN ? 64 : BN)) return cudaErrorInvalidValue;
   const int tiles = ((g.M + BM - 1) / BM) * ((g.N + BN - 1) / BN);
   const int grid = tiles < g.num_sms ? tiles : g.num_sms;
-  kernel<<<grid, THREADS, SMEM_BYTES, stream>>>(ta, tb, g.C, g.ldc, g.M, g.N, g.K, g.err);
+  CUtensorMap tc;
+  if (!make_tmap_out_2d(&tc, g.C, OUT != 0, g.N, g.M, g.ldc * (OUT != 0 ? 4 : 2), 32)) return cudaErrorInvalidValue;
+  kernel<<<grid, THREADS, SMEM_BYTES, stream>>>(ta, tb, tc, g.M, g.N, g.K, g.err);
   return cudaGetLastError();
 }
 
@@ -267,6 +281,20 @@ bool make_tmap_bf16_2d(CUtensorMap* map, const void* base, uint64_t inner, uint6
   CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+bool make_tmap_out_2d(CUtensorMap* map, const void* base, bool fp32, uint64_t inner, uint64_t outer,
+                      uint64_t row_stride_bytes, uint32_t box_outer) {
+  auto fn = encode_fn();
+  if (fn == nullptr) return false;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {row_stride_bytes};
+  cuuint32_t box[2] = {fp32 ? 32u : 64u, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, fp32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+                  const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
 }
 

@@ -28,6 +28,12 @@ cudaError_t gemm_bf16(const GemmArgs& args, cudaStream_t stream);
 bool make_tmap_bf16_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint64_t row_stride_elems,
                        uint32_t box_inner, uint32_t box_outer);
 
+// 2-D TMA descriptor of an output matrix [outer][inner] (row stride in bytes)
+// for 128-byte-swizzled stores / reduce-adds: fp32 (box 32 x box_outer) or
+// bf16 (box 64 x box_outer).
+bool make_tmap_out_2d(CUtensorMap* map, const void* base, bool fp32, uint64_t inner, uint64_t outer,
+                      uint64_t row_stride_bytes, uint32_t box_outer);
+
 // 3-D bf16 TMA descriptor with 128-byte swizzle; dims[0] is contiguous, strides
 // (bytes) of dims 1 and 2 must be multiples of 16.
 bool make_tmap_bf16_3d(CUtensorMap* map, const void* base, const uint64_t dims[3], const uint64_t strides_bytes[2],
