@@ -76,7 +76,8 @@ constexpr int STAGING_BYTES = 4 * 32 * BN * 2;
 template <int MODE>
 struct Cfg {
   static constexpr int STAGES = MODE == kReduceScatterGemm ? 3 : 4;
-  static constexpr int STAGING = MODE == kReduceScatterGemm ? STAGING_BYTES : 0;
+  // all-gather modes: two 4 KB output boxes (32 rows x 128 B) per epilogue warp
+  static constexpr int STAGING = MODE == kReduceScatterGemm ? STAGING_BYTES : 4 * 2 * 4096;
   static constexpr int SMEM = STAGES * STAGE_BYTES + STAGING + 1024 + 256;
 };
 constexpr int THREADS = 224;  // 7 warps: producer, MMA, 4 epilogue, comm
@@ -161,7 +162,8 @@ __device__ __forceinline__ TileInfo tile_of(int t, const FusedTpArgs& a, int mt_
 template <int MODE, bool B_MN>
 __global__ void __launch_bounds__(THREADS, 1)
 fused_tp_kernel(const __grid_constant__ CUtensorMap tmA_local, const __grid_constant__ CUtensorMap tmA_gather,
-                const __grid_constant__ CUtensorMap tmB, const FusedTpArgs a) {
+                const __grid_constant__ CUtensorMap tmB, const __grid_constant__ CUtensorMap tmOut,
+                const FusedTpArgs a) {
   constexpr int STAGES = Cfg<MODE>::STAGES;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -350,6 +352,10 @@ fused_tp_kernel(const __grid_constant__ CUtensorMap tmA_local, const __grid_cons
     int acc = 0;
     uint32_t acc_phase = 0;
     uint32_t ready_mask = 1u << a.rank;
+    // all-gather modes: output rows go through swizzled 64-column boxes that
+    // TMA stores (two buffers per warp, one box per two 32-column chunks)
+    uint8_t* box_stg = staging + quarter * 2 * 4096;
+    int nbox = 0;
     // Control flow here is uniform over the 128 epilogue threads (named
     // barriers): after an abort the loop still runs to the end, skipping waits.
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
@@ -384,12 +390,12 @@ fused_tp_kernel(const __grid_constant__ CUtensorMap tmA_local, const __grid_cons
         tmem_ld_32x32b_x32(t_row + c, r);
         tmem_wait_ld();
         const int col = ti.tn * BN + c;
-        if (col >= a.N) continue;
+        if (!is_ag<MODE>() && col >= a.N) continue;
         float v[32];
 #pragma unroll
         for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
         __nv_bfloat16* dst;
-        if (MODE == kAllGatherGemmCE) {
+        if (MODE == kAllGatherGemmCE && col < a.N) {
           const int nv = min(32, a.N - col);
 #pragma unroll
           for (int j = 0; j < 32; ++j) v[j] = __bfloat162float(__float2bfloat16_rn(v[j]));
@@ -417,7 +423,34 @@ fused_tp_kernel(const __grid_constant__ CUtensorMap tmA_local, const __grid_cons
           }
         }
         if (is_ag<MODE>()) {
-          dst = a.out + (long)row * a.ldo + col;
+          const int half = (c >> 5) & 1;
+          uint8_t* buf = box_stg + (nbox & 1) * 4096;
+          if (half == 0) {
+            // the box stored from this buffer two boxes ago must have been read out
+            if (lane == 0) bulk_wait_group_read<1>();
+            __syncwarp();
+          }
+          uint8_t* brow = buf + lane * 128;
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            uint4 u;
+            u.x = pack_bf16x2(v[8 * j + 0], v[8 * j + 1]);
+            u.y = pack_bf16x2(v[8 * j + 2], v[8 * j + 3]);
+            u.z = pack_bf16x2(v[8 * j + 4], v[8 * j + 5]);
+            u.w = pack_bf16x2(v[8 * j + 6], v[8 * j + 7]);
+            *reinterpret_cast<uint4*>(brow + (((4 * half + j) ^ (lane & 7)) << 4)) = u;
+          }
+          if (half == 1) {
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+              const int bcol = col - 32;
+              if (bcol < a.N) tma_store_2d(&tmOut, buf, bcol, ti.tm * BM + quarter * 32);
+              bulk_commit_group();
+            }
+            ++nbox;
+          }
+          continue;
         } else if (ti.chunk != a.rank) {
           // stage this thread's 32 columns (row `lane` of the warp's 32 rows);
           // 16-byte chunk j of a row sits at position j ^ (row % 8)
@@ -487,6 +520,8 @@ fused_tp_kernel(const __grid_constant__ CUtensorMap tmA_local, const __grid_cons
       }
       if (++acc == 2) { acc = 0; acc_phase ^= 1; }
     }
+    // every TMA store of an output box must be complete before the CTA goes
+    if (is_ag<MODE>() && lane == 0) bulk_wait_group<0>();
   }
 
   tc_fence_before();
@@ -520,10 +555,13 @@ cudaError_t launch(const FusedTpArgs& a, const void* B, long ldb, int num_sms, c
   }
   if (!make_tmap_bf16_2d(&tb, B, B_MN ? a.N : a.K, B_MN ? a.K : a.N, ldb, 64, B_MN ? 64 : BN))
     return cudaErrorInvalidValue;
+  CUtensorMap tout = tb;  // reduce-scatter writes its rows itself
+  if (is_ag<MODE>() && !make_tmap_out_2d(&tout, a.out, false, a.N, a.M, (uint64_t)a.ldo * 2, 32))
+    return cudaErrorInvalidValue;
   const int tiles = a.world * (a.m_chunk / BM) * ((a.N + BN - 1) / BN);
   int grid = tiles < num_sms ? tiles : num_sms;
   if (grid > kMaxCtas) grid = kMaxCtas;
-  kernel<<<grid, THREADS, Cfg<MODE>::SMEM, stream>>>(ta_local, ta_gather, tb, a);
+  kernel<<<grid, THREADS, Cfg<MODE>::SMEM, stream>>>(ta_local, ta_gather, tb, tout, a);
   return cudaGetLastError();
 }
 
