@@ -9,6 +9,7 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
 
+#include "dp_reduce.cuh"
 #include "fused_tp.cuh"
 #include "gemm.cuh"
 #include "kernels.cuh"
@@ -192,6 +193,33 @@ void ce_merge(const at::Tensor& part, const at::Tensor& target_logit, const at::
   check_ok(nmb::ce_merge(a, at::cuda::getCurrentCUDAStream()), "ce_merge");
 }
 
+// Data-parallel averaging of one span of the flat gradient buffer (see
+// dp_reduce.cu); `bufs` / `flags` hold every DP rank's mapped pointers.
+void dp_allreduce(const std::vector<int64_t>& bufs, const std::vector<int64_t>& flags, int64_t rank,
+                  int64_t offset, int64_t n, int64_t epoch, const at::Tensor& err, double timeout_s) {
+  const int world = (int)bufs.size();
+  TORCH_CHECK(world >= 1 && world <= nmb::kDpMaxRanks && (int)flags.size() == world, "bad DP group");
+  TORCH_CHECK(rank >= 0 && rank < world, "bad rank");
+  TORCH_CHECK(offset % 4 == 0 && n % 4 == 0, "span must be a multiple of 4 elements");
+  nmb::DpReduceArgs a{};
+  for (int r = 0; r < world; ++r) {
+    a.buf[r] = reinterpret_cast<float*>(bufs[r]);
+    a.flags[r] = reinterpret_cast<int*>(flags[r]);
+  }
+  a.offset = offset;
+  a.n = n;
+  a.rank = (int)rank;
+  a.world = world;
+  a.epoch = (int)epoch;
+  a.scale = 1.0f / (float)world;
+  a.err = err.data_ptr<int>();
+  a.timeout_ns = (uint64_t)(timeout_s * 1e9);
+  const at::cuda::CUDAGuard guard(err.device());
+  check_ok(nmb::dp_allreduce(a, at::cuda::getCurrentCUDAStream()), "dp_allreduce");
+}
+
+int64_t dp_flag_bytes() { return nmb::kDpFlagInts * 4; }
+
 }  // namespace
 
 void register_elementwise(pybind11::module& m);
@@ -208,6 +236,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         pybind11::arg("vocab_start") = 0, pybind11::arg("ce_part") = pybind11::none(),
         pybind11::arg("ce_target") = pybind11::none());
   m.def("ce_merge", &ce_merge);
+  m.def("dp_allreduce", &dp_allreduce);
+  m.def("dp_flag_bytes", &dp_flag_bytes);
   m.def("fused_tp_flag_bytes", &fused_tp_flag_bytes);
   register_elementwise(m);
 }

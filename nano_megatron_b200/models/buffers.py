@@ -125,6 +125,17 @@ class FlatBuffers:
         if self.compute is not None:
             self.compute.copy_(self.data)
 
+    def rehome_grad(self, new_grad: torch.Tensor) -> None:
+        """Move the flat gradient into ``new_grad`` (same numel, fp32, same device),
+        e.g. a symmetric-memory allocation that peers map, and re-point every view."""
+        if new_grad.numel() != self.numel or new_grad.dtype != self.grad.dtype:
+            raise ValueError("replacement gradient buffer has the wrong size or dtype")
+        new_grad.copy_(self.grad)
+        self.grad = new_grad
+        for region in self.regions:
+            region.grad_block, _ = self._views(self.grad, region)
+        self.reattach_grads()
+
     def reattach_grads(self) -> None:
         """Point ``param.grad`` back at the flat views (after ``zero_grad(set_to_none)``)."""
         for region in self.regions:

@@ -95,9 +95,11 @@ class GradBucketer:
     region receives per microbatch (two for an embedding tied to the LM head
     on one stage), and during the final microbatch's backward a region is
     complete once it received that many. When every region of a bucket is
-    complete, the bucket's all-reduce starts: on CUDA on a communication
-    stream that first waits for an event recorded after the last write, with
-    ``ReduceOp.AVG`` so NCCL folds the ``1/dp`` scale into the reduction.
+    complete, the bucket's reduction starts: on CUDA on a communication
+    stream that first waits for an event recorded after the last write. The
+    reduction is ``reducer(start, end)`` when given -- on CUDA the NVLink
+    kernel of :mod:`nano_megatron_b200.ops.dp_reduce`, which applies the
+    ``1/dp`` scale in the same pass -- else NCCL ``ReduceOp.AVG``.
     :meth:`finish` starts whatever is left (a step with one microbatch learns
     nothing the first time and reduces everything there) and makes the compute
     stream wait for all of it.
@@ -113,7 +115,8 @@ class GradBucketer:
     after the whole backward, then a division by ``dp``).
     """
 
-    def __init__(self, model, ctx: ParallelContext, bucket_bytes: int = 128 << 20, overlap: bool = True):
+    def __init__(self, model, ctx: ParallelContext, bucket_bytes: int = 128 << 20, overlap: bool = True,
+                 reducer=None):
         buffers = _flat_buffers(model)
         if buffers is None:
             raise ValueError("the bucketer needs a model with flat gradient buffers")
@@ -142,6 +145,9 @@ class GradBucketer:
                 for r in current:
                     self.bucket_of[r] = b
                 end, current = start, []
+        # ``reducer(start, end)`` averages one span in place on the current
+        # stream (our NVLink kernel); None means NCCL all_reduce(AVG).
+        self.reducer = reducer
         self.overlap = overlap and self.grad.is_cuda
         self.stream = torch.cuda.Stream(device=self.grad.device) if self.overlap else None
         self.per_microbatch: list[int] | None = None
@@ -188,7 +194,15 @@ class GradBucketer:
         self.started[b] = True
         start, end = self.buckets[b]
         view = self.grad[start:end]
-        if self.stream is not None:
+        if self.reducer is not None and self.stream is not None:
+            ready = torch.cuda.Event()
+            ready.record(torch.cuda.current_stream(self.grad.device))
+            self.stream.wait_event(ready)
+            with torch.cuda.stream(self.stream):
+                self.reducer(start, end)
+        elif self.reducer is not None:
+            self.reducer(start, end)
+        elif self.stream is not None:
             ready = torch.cuda.Event()
             ready.record(torch.cuda.current_stream(self.grad.device))
             self.stream.wait_event(ready)

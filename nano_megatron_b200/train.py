@@ -61,8 +61,14 @@ class Trainer:
         if ctx.dp_size > 1 and dp_bucket_mb > 0 and getattr(self.model, "flat_buffers", None) is not None:
             fused_in_backward = (self.device.type == "cuda" and fused_tp and ctx.tp_size > 1
                                  and config.activation_dtype == torch.bfloat16)
+            reducer = None
+            if self.device.type == "cuda":
+                # our NVLink averaging kernel over a symmetric gradient buffer
+                from .ops.dp_reduce import DPWorkspace
+                self.dp_workspace = DPWorkspace(ctx, self.model.flat_buffers)
+                reducer = self.dp_workspace.all_reduce_avg
             self.bucketer = GradBucketer(self.model, ctx, bucket_bytes=int(dp_bucket_mb * (1 << 20)),
-                                         overlap=not fused_in_backward)
+                                         overlap=not fused_in_backward, reducer=reducer)
             set_grad_observer(self.bucketer.observe)
 
     def to_device(self, batches):

@@ -22,7 +22,7 @@ SOURCES = [
     "attention.cu",
     "attention_tc.cu",
     "attention_bwd_tc.cu",
-    "fused_tp.cu",
+    "fused_tp.cu", "dp_reduce.cu",
     "noalloc.cu",
     "fp32.cu",
 ]
