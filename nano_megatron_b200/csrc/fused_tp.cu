@@ -68,14 +68,16 @@ constexpr int BM = 128, BN = 256, BK = 64;
 constexpr int A_TILE_BYTES = BM * BK * 2;
 constexpr int B_TILE_BYTES = BN * BK * 2;
 constexpr int STAGE_BYTES = A_TILE_BYTES + B_TILE_BYTES;
-// The reduce-scatter variant trades one pipeline stage for a 64 KB staging
-// area in which each epilogue warp assembles 32 full 512-byte output rows, so
-// partial tiles cross NVLink as whole rows (one warp instruction = 512
-// contiguous bytes) instead of 64-byte pieces of 32 different rows.
-constexpr int STAGING_BYTES = 4 * 32 * BN * 2;
+// The reduce-scatter variant has a 32 KB staging area in which each epilogue
+// warp assembles half rows (128 columns, 256 B) of its 32 output rows; a
+// partial tile crosses NVLink as two such halves, each warp instruction
+// writing two contiguous 256-byte row pieces instead of 64-byte pieces of 32
+// different rows.
+constexpr int HALF_ROW = BN / 2 * 2;                   // 256 B
+constexpr int STAGING_BYTES = 4 * 32 * HALF_ROW;
 template <int MODE>
 struct Cfg {
-  static constexpr int STAGES = MODE == kReduceScatterGemm ? 3 : 4;
+  static constexpr int STAGES = 4;
   // all-gather modes: two 4 KB output boxes (32 rows x 128 B) per epilogue warp
   static constexpr int STAGING = MODE == kReduceScatterGemm ? STAGING_BYTES : 4 * 2 * 4096;
   static constexpr int SMEM = STAGES * STAGE_BYTES + STAGING + 1024 + 256;
@@ -356,6 +358,25 @@ fused_tp_kernel(const __grid_constant__ CUtensorMap tmA_local, const __grid_cons
     // TMA stores (two buffers per warp, one box per two 32-column chunks)
     uint8_t* box_stg = staging + quarter * 2 * 4096;
     int nbox = 0;
+    // reduce-scatter: write half h (columns [128h, 128h + 128)) of the warp's
+    // 32 staged rows to the owner of a foreign tile; lanes 0-15 take one row,
+    // lanes 16-31 the next, so each instruction writes two 256-byte pieces
+    auto flush_half = [&](const TileInfo& ft, int h) {
+      __syncwarp();
+      const int sub = lane >> 4, ch = lane & 15;
+      const int col = ft.tn * BN + h * (BN / 2) + ch * 8;
+      const int row0 = ft.tm * BM + quarter * 32 - ft.chunk * a.m_chunk;
+      __nv_bfloat16* dst0 = reinterpret_cast<__nv_bfloat16*>(a.ws[ft.chunk] + a.recv_off) +
+                            ((long)a.rank * a.m_chunk + row0) * a.N + col;
+#pragma unroll 4
+      for (int r2 = 0; r2 < 16; ++r2) {
+        const int rr = 2 * r2 + sub;
+        const uint4 u = *reinterpret_cast<const uint4*>(staging + (quarter * 32 + rr) * HALF_ROW +
+                                                         ((ch ^ (rr & 7)) << 4));
+        if (col < a.N) *reinterpret_cast<uint4*>(dst0 + (long)rr * a.N) = u;
+      }
+      __syncwarp();
+    };
     // Control flow here is uniform over the 128 epilogue threads (named
     // barriers): after an abort the loop still runs to the end, skipping waits.
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
@@ -386,6 +407,7 @@ fused_tp_kernel(const __grid_constant__ CUtensorMap tmA_local, const __grid_cons
       }
 #pragma unroll 1
       for (int c = 0; c < BN; c += 32) {
+        if (MODE == kReduceScatterGemm && ti.chunk != a.rank && c == BN / 2) flush_half(ti, 0);
         uint32_t r[32];
         tmem_ld_32x32b_x32(t_row + c, r);
         tmem_wait_ld();
@@ -454,7 +476,7 @@ fused_tp_kernel(const __grid_constant__ CUtensorMap tmA_local, const __grid_cons
         } else if (ti.chunk != a.rank) {
           // stage this thread's 32 columns (row `lane` of the warp's 32 rows);
           // 16-byte chunk j of a row sits at position j ^ (row % 8)
-          uint8_t* srow = staging + (quarter * 32 + lane) * (BN * 2);
+          uint8_t* srow = staging + (quarter * 32 + lane) * HALF_ROW;
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
             uint4 u;
@@ -462,7 +484,7 @@ fused_tp_kernel(const __grid_constant__ CUtensorMap tmA_local, const __grid_cons
             u.y = pack_bf16x2(v[8 * j + 2], v[8 * j + 3]);
             u.z = pack_bf16x2(v[8 * j + 4], v[8 * j + 5]);
             u.w = pack_bf16x2(v[8 * j + 6], v[8 * j + 7]);
-            const int chunk = c / 8 + j;
+            const int chunk = (c & (BN / 2 - 1)) / 8 + j;  // 16-byte chunk within the half row
             *reinterpret_cast<uint4*>(srow + ((chunk ^ (lane & 7)) << 4)) = u;
           }
           continue;
@@ -501,19 +523,7 @@ fused_tp_kernel(const __grid_constant__ CUtensorMap tmA_local, const __grid_cons
       mbar_arrive(&tempty[acc]);
       if (MODE == kAllGatherGemmCE) a.ce_part[(long)ti.tn * a.M + row] = make_float2(ce_m, ce_s);
       if (MODE == kReduceScatterGemm && ti.chunk != a.rank) {
-        // write the warp's 32 staged rows to the owner, one 512-byte row per instruction
-        __syncwarp();
-        const int col = ti.tn * BN + lane * 8;
-        const int row0 = ti.tm * BM + quarter * 32 - ti.chunk * a.m_chunk;
-        __nv_bfloat16* dst0 = reinterpret_cast<__nv_bfloat16*>(a.ws[ti.chunk] + a.recv_off) +
-                              ((long)a.rank * a.m_chunk + row0) * a.N + col;
-#pragma unroll 4
-        for (int r = 0; r < 32; ++r) {
-          const uint4 u = *reinterpret_cast<const uint4*>(staging + (quarter * 32 + r) * (BN * 2) +
-                                                           ((lane ^ (r & 7)) << 4));
-          if (col < a.N) *reinterpret_cast<uint4*>(dst0 + (long)r * a.N) = u;
-        }
-        __syncwarp();
+        flush_half(ti, 1);
         __threadfence_system();
         epilogue_bar();
         if (leader) st_release_sys(flags_of(a, ti.chunk) + kRsDoneOff + ti.local * kMaxRanks + a.rank, epoch);
