@@ -105,72 +105,94 @@ __global__ void rmsnorm_fwd_kernel(const T* __restrict__ x, const float* __restr
 
 constexpr int NORM_BWD_THREADS = 256;
 
-template <typename T, int CHUNKS>
+// One block works on one row at a time with all its threads: thread t owns
+// columns (t + 256 j) * 8 .. + 8 for j < CH, so the weight gradient of those
+// columns accumulates in the thread's registers over all the block's rows
+// (written once at the end, no shared-memory reduction) and the row's
+// x / dy stay in registers between the dot product and dx. One barrier per
+// pair of rows: the per-warp dot partials alternate between two shared slots.
+template <typename T, int CH>
 __global__ void __launch_bounds__(NORM_BWD_THREADS)
 rmsnorm_bwd_kernel(const T* __restrict__ dy, const T* __restrict__ x, const float* __restrict__ w,
                    const float* __restrict__ rstd, T* __restrict__ dx, float* __restrict__ dw_partial, int rows,
                    int cols) {
-  extern __shared__ float red[];  // [cols]
-  const int warps = NORM_BWD_THREADS / 32;
+  __shared__ float red[2][2 * (NORM_BWD_THREADS / 32)];
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  float acc[CHUNKS][8];
+  float wv[CH][8], acc[CH][8];
 #pragma unroll
-  for (int j = 0; j < CHUNKS; ++j)
+  for (int j = 0; j < CH; ++j) {
+    const int c = (threadIdx.x + j * NORM_BWD_THREADS) * 8;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) acc[j][i] = 0.f;
-
-  for (long row = (long)blockIdx.x * warps + warp; row < rows; row += (long)gridDim.x * warps) {
-    const T* xr = x + row * cols;
-    const T* dyr = dy + row * cols;
-    const float r = rstd[row];
-    float dot = 0.f;
+    for (int i = 0; i < 8; ++i) {
+      acc[j][i] = 0.f;
+      wv[j][i] = 0.f;
+    }
+    if (c < cols) V8<float>::load(w + c, wv[j]);
+  }
+  // two rows per iteration (rows r and r + gridDim.x): twice the loads in flight
+  int parity = 0;
+  for (long row0 = blockIdx.x; row0 < rows; row0 += 2L * gridDim.x, parity ^= 1) {
+    float xh[2][CH][8], gv[2][CH][8], r[2], dot[2];
 #pragma unroll
-    for (int j = 0; j < CHUNKS; ++j) {
-      const int c = lane * 8 + j * 256;
-      if (c < cols) {
-        float xv[8], gv[8], wv[8];
-        V8<T>::load(xr + c, xv);
-        V8<T>::load(dyr + c, gv);
-        V8<float>::load(w + c, wv);
+    for (int q = 0; q < 2; ++q) {
+      const long row = row0 + q * (long)gridDim.x;
+      const bool live = row < rows;
+      r[q] = live ? rstd[row] : 0.f;
+#pragma unroll
+      for (int j = 0; j < CH; ++j) {
+        const int c = (threadIdx.x + j * NORM_BWD_THREADS) * 8;
+        if (live && c < cols) {
+          V8<T>::load(x + row * cols + c, xh[q][j]);
+          V8<T>::load(dy + row * cols + c, gv[q][j]);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 8; ++i) xh[q][j][i] = gv[q][j][i] = 0.f;
+        }
+      }
+    }
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+      dot[q] = 0.f;
+#pragma unroll
+      for (int j = 0; j < CH; ++j)
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-          const float xh = xv[i] * r;
-          acc[j][i] += gv[i] * V8<T>::round(xh);
-          dot += gv[i] * wv[i] * xh;
+          xh[q][j][i] *= r[q];
+          acc[j][i] += gv[q][j][i] * V8<T>::round(xh[q][j][i]);
+          dot[q] += gv[q][j][i] * wv[j][i] * xh[q][j][i];
         }
-      }
+      dot[q] = warp_sum(dot[q]);
     }
-    dot = warp_sum(dot) / cols;
-    T* dxr = dx + row * cols;
-#pragma unroll
-    for (int j = 0; j < CHUNKS; ++j) {
-      const int c = lane * 8 + j * 256;
-      if (c < cols) {
-        float xv[8], gv[8], wv[8], o[8];
-        V8<T>::load(xr + c, xv);
-        V8<T>::load(dyr + c, gv);
-        V8<float>::load(w + c, wv);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) o[i] = r * (gv[i] * wv[i] - xv[i] * r * dot);
-        V8<T>::store(dxr + c, o);
-      }
-    }
-  }
-  // Deterministic block reduction of the weight gradient: warps add in order.
-  for (int wi = 0; wi < warps; ++wi) {
-    if (warp == wi) {
-#pragma unroll
-      for (int j = 0; j < CHUNKS; ++j) {
-        const int c = lane * 8 + j * 256;
-        if (c < cols) {
-#pragma unroll
-          for (int i = 0; i < 8; ++i) red[c + i] = (wi == 0 ? 0.f : red[c + i]) + acc[j][i];
-        }
-      }
+    if (lane == 0) {
+      red[parity][warp] = dot[0];
+      red[parity][NORM_BWD_THREADS / 32 + warp] = dot[1];
     }
     __syncthreads();
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+      float d = 0.f;
+#pragma unroll
+      for (int i = 0; i < NORM_BWD_THREADS / 32; ++i) d += red[parity][q * (NORM_BWD_THREADS / 32) + i];
+      d /= cols;
+      const long row = row0 + q * (long)gridDim.x;
+      if (row >= rows) continue;
+#pragma unroll
+      for (int j = 0; j < CH; ++j) {
+        const int c = (threadIdx.x + j * NORM_BWD_THREADS) * 8;
+        if (c < cols) {
+          float o[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) o[i] = r[q] * (gv[q][j][i] * wv[j][i] - xh[q][j][i] * d);
+          V8<T>::store(dx + row * cols + c, o);
+        }
+      }
+    }
   }
-  for (int c = threadIdx.x; c < cols; c += NORM_BWD_THREADS) dw_partial[(long)blockIdx.x * cols + c] = red[c];
+#pragma unroll
+  for (int j = 0; j < CH; ++j) {
+    const int c = (threadIdx.x + j * NORM_BWD_THREADS) * 8;
+    if (c < cols) V8<float>::store(dw_partial + (long)blockIdx.x * cols + c, acc[j]);
+  }
 }
 
 __global__ void reduce_rows_add_kernel(const float* __restrict__ partial, float* __restrict__ out, int nrows,
@@ -449,8 +471,7 @@ cudaError_t rmsnorm_fwd(const void* x, const float* w, void* y, float* rstd, int
 }
 
 int rmsnorm_bwd_blocks(int rows) {
-  const int warps = NORM_BWD_THREADS / 32;
-  int b = (rows + warps * 8 - 1) / (warps * 8);  // >= 8 rows per warp
+  int b = (rows + 7) / 8;  // >= 8 rows per block (one row at a time)
   return b < 296 ? (b < 1 ? 1 : b) : 296;
 }
 
@@ -458,26 +479,22 @@ template <typename T, int C>
 static cudaError_t launch_norm_bwd(const void* dy, const void* x, const float* w, const float* rstd, void* dx,
                                    float* part, int rows, int cols, cudaStream_t s) {
   const int blocks = rmsnorm_bwd_blocks(rows);
-  const size_t smem = (size_t)cols * sizeof(float);
-  auto k = rmsnorm_bwd_kernel<T, C>;
-  if (smem > 48 * 1024) cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  k<<<blocks, NORM_BWD_THREADS, smem, s>>>(static_cast<const T*>(dy), static_cast<const T*>(x), w, rstd,
-                                           static_cast<T*>(dx), part, rows, cols);
+  rmsnorm_bwd_kernel<T, C><<<blocks, NORM_BWD_THREADS, 0, s>>>(static_cast<const T*>(dy), static_cast<const T*>(x),
+                                                               w, rstd, static_cast<T*>(dx), part, rows, cols);
   return cudaGetLastError();
 }
 
 cudaError_t rmsnorm_bwd(const void* dy, const void* x, const float* w, const float* rstd, void* dx, float* part,
                         int rows, int cols, int dtype, cudaStream_t s) {
   if (cols % 8) return cudaErrorInvalidValue;
-  const int chunks = (cols + 255) / 256;
-  if (chunks > 32) return cudaErrorInvalidValue;
+  const int chunks = (cols + 8 * NORM_BWD_THREADS - 1) / (8 * NORM_BWD_THREADS);  // 8-column chunks per thread
+  if (chunks > 4) return cudaErrorInvalidValue;  // up to 8192 columns
 #define NMB_NORM(C)                                                                                  \
   return dtype == 1 ? launch_norm_bwd<__nv_bfloat16, C>(dy, x, w, rstd, dx, part, rows, cols, s)      \
                     : launch_norm_bwd<float, C>(dy, x, w, rstd, dx, part, rows, cols, s);
-  if (chunks <= 4) { NMB_NORM(4) }
-  if (chunks <= 8) { NMB_NORM(8) }
-  if (chunks <= 16) { NMB_NORM(16) }
-  NMB_NORM(32)
+  if (chunks <= 1) { NMB_NORM(1) }
+  if (chunks <= 2) { NMB_NORM(2) }
+  NMB_NORM(4)
 #undef NMB_NORM
 }
 
