@@ -133,8 +133,10 @@ flash_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tm_qkv_big, const __gr
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  const int kb = blockIdx.x;  // key block of 128; low index = most query blocks
-  const int bh = blockIdx.y, b = bh / a.heads, h = bh % a.heads;
+  // grid (batch*heads, key blocks): heads vary fastest, so the key blocks with
+  // the most query blocks (low index) of every head are handed out first
+  const int kb = blockIdx.y;  // key block of 128; low index = most query blocks
+  const int bh = blockIdx.x, b = bh / a.heads, h = bh % a.heads;
   const int first_qb = 2 * kb, nqb = a.S / SMALL;
   const int nblk = nqb - first_qb;
   const int q_col = h * HD, k_col = a.heads * HD + h * HD, v_col = 2 * a.heads * HD + h * HD, do_col = h * HD;
@@ -348,8 +350,8 @@ flash_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tm_qkv_big, const __g
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int nqb = a.S / BIG;
-  const int qb = nqb - 1 - blockIdx.x;  // longest rows first
-  const int bh = blockIdx.y, b = bh / a.heads, h = bh % a.heads;
+  const int qb = nqb - 1 - blockIdx.y;  // longest rows first (heads vary fastest in the grid)
+  const int bh = blockIdx.x, b = bh / a.heads, h = bh % a.heads;
   const int nblk = 2 * qb + 2;          // 64-key blocks up to the diagonal
   const int q_col = h * HD, k_col = a.heads * HD + h * HD, v_col = 2 * a.heads * HD + h * HD, do_col = h * HD;
 
@@ -554,11 +556,11 @@ cudaError_t flash_attn_bwd_tc(const __nv_bfloat16* dout, const __nv_bfloat16* qk
   float* lse2 = const_cast<float*>(dvec) + rows;
   scale_kernel<<<(int)((rows + 255) / 256), 256, 0, stream>>>(lse, lse2, rows, LOG2E);
   BwdArgs a{lse, lse2, dvec, dqkv, S, batch, heads, 1.0f / sqrtf((float)HD), err};
-  dim3 grid_kv(S / BIG, batch * heads);
+  dim3 grid_kv(batch * heads, S / BIG);
   flash_bwd_dkdv_kernel<<<grid_kv, KV_THREADS, KV_SMEM, stream>>>(qkv_big, qkv_small, do_small, a);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  dim3 grid_q(S / BIG, batch * heads);
+  dim3 grid_q(batch * heads, S / BIG);
   flash_bwd_dq_tc_kernel<<<grid_q, Q_THREADS, Q_SMEM, stream>>>(qkv_big, qkv_small, do_big, a);
   return cudaGetLastError();
 }

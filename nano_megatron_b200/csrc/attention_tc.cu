@@ -106,8 +106,10 @@ flash_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_qkv, __nv_bfloat16* _
   const int wg = warp / 4, quarter = warp % 4;
   const int nqt = S / TQ;                 // 128-row query tiles
   const int nblk = (nqt + 1) / 2;         // 256-row CTA blocks
-  const int blk = nblk - 1 - blockIdx.x;  // longest rows first
-  const int bh = blockIdx.y, b = bh / heads, h = bh % heads;
+  // grid (batch*heads, blocks): heads vary fastest, so the hardware hands out
+  // the longest (latest) query blocks of every head before any shorter one
+  const int blk = nblk - 1 - blockIdx.y;
+  const int bh = blockIdx.x, b = bh / heads, h = bh % heads;
   const int nkb0 = 2 * blk + 1;                             // tile 0 always exists
   const int nkb1 = (2 * blk + 1 < nqt) ? 2 * blk + 2 : 0;   // tile 1 may not (odd tile count)
   const int nkb_max = nkb1 > nkb0 ? nkb1 : nkb0;
@@ -392,7 +394,7 @@ cudaError_t flash_attn_fwd_tc(const __nv_bfloat16* qkv, __nv_bfloat16* out, floa
   if (!make_tmap_bf16_3d(&tm, qkv, dims, strides, box)) return cudaErrorInvalidValue;
   const float scale_log2 = (1.0f / sqrtf((float)HD)) * 1.4426950408889634f;
   const int nblk = (S / TQ + 1) / 2;
-  dim3 grid(nblk, batch * heads);
+  dim3 grid(batch * heads, nblk);
   flash_fwd_tc_kernel<<<grid, THREADS, SMEM, stream>>>(tm, out, lse, S, batch, heads, scale_log2, err);
   return cudaGetLastError();
 }
