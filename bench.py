@@ -209,6 +209,9 @@ def main():
         dist.barrier()
         kernel_launches = launches() - launches0
         ms = max_over_ranks(start.elapsed_time(end) / args.steps, device)
+        if args.impl != "reference":  # a bounded wait that ran out or a bad token id raises here
+            from nano_megatron_b200.ops import cuda as KC
+            KC.check_status(device)
 
         # End to end through the public API: pinned host inputs, loss read back.
         host = [make_batches(vocab, seq, 100 + s, ctx.dp_rank, pin=True) for s in range(2)]

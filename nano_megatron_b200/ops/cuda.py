@@ -52,14 +52,22 @@ def status_word(device: torch.device) -> torch.Tensor:
     return t
 
 
+class CollectiveTimeout(RuntimeError):
+    """A kernel gave up waiting for another GPU (a peer stopped, or never started)."""
+
+
 def check_status(device: torch.device | None = None) -> None:
-    """Raise if any kernel on ``device`` reported an error since the last check (syncs)."""
+    """Raise if any kernel on ``device`` reported an error since the last check (syncs).
+
+    Code 2 (a cross-GPU flag wait ran out) raises :class:`CollectiveTimeout`.
+    """
     device = device or torch.device("cuda", torch.cuda.current_device())
     word = status_word(device)
     code = int(word[0].item())
     if code:
         word.zero_()
-        raise RuntimeError(f"CUDA kernel error {code}: {ERROR_MESSAGES.get(code, 'unknown')}")
+        cls = CollectiveTimeout if code == 2 else RuntimeError
+        raise cls(f"CUDA kernel error {code}: {ERROR_MESSAGES.get(code, 'unknown')}")
 
 
 def _dtype_ok(t: torch.Tensor) -> None:

@@ -21,6 +21,8 @@ order, loss scaling by ``1/M``).
 
 from __future__ import annotations
 
+import contextlib
+import os
 from collections.abc import Sequence
 
 import torch
@@ -75,7 +77,23 @@ class _P2P:
         self.pending_sends.clear()
 
 
+# NVTX ranges around every microbatch forward / backward (for nsys or ncu
+# range filters) when NMB_NVTX=1; free otherwise.
+_NVTX = os.environ.get("NMB_NVTX", "0") == "1"
+
+
+def _nvtx(name: str):
+    if _NVTX and torch.cuda.is_available():
+        return torch.cuda.nvtx.range(name)
+    return contextlib.nullcontext()
+
+
 def _forward_step(model, batch, hidden, losses, num_microbatches, ctx):
+    with _nvtx(f"forward stage {ctx.pp_rank}"):
+        return _forward_step_impl(model, batch, hidden, losses, num_microbatches, ctx)
+
+
+def _forward_step_impl(model, batch, hidden, losses, num_microbatches, ctx):
     inputs, labels = batch
     stage_input = inputs if ctx.is_first_stage else hidden
     if stage_input is None:
@@ -89,6 +107,11 @@ def _forward_step(model, batch, hidden, losses, num_microbatches, ctx):
 
 
 def _backward_step(input_tensor, output_tensor, output_gradient, ctx):
+    with _nvtx(f"backward stage {ctx.pp_rank}"):
+        return _backward_step_impl(input_tensor, output_tensor, output_gradient, ctx)
+
+
+def _backward_step_impl(input_tensor, output_tensor, output_gradient, ctx):
     if ctx.is_last_stage:
         torch.autograd.backward(output_tensor)
     else:

@@ -75,6 +75,13 @@ class Trainer:
         return [(x.to(self.device, non_blocking=True), y.to(self.device, non_blocking=True))
                 for x, y in batches]
 
+    def check_kernel_status(self) -> None:
+        """Raise if a kernel of this rank reported an error (bounded wait ran out,
+        token out of range, ...) since the last check; one device sync on CUDA."""
+        if self.device.type == "cuda":
+            from . import ops
+            ops.cuda_ops().check_status(self.device)
+
     def train_step(self, batches) -> torch.Tensor | None:
         """Forward, backward, gradient sync, clip and AdamW over one global batch.
 
@@ -162,6 +169,7 @@ def train(args):
         else:
             batches = [stream.next_batch(args.micro_batch_size) for _ in range(args.num_microbatches)]
         loss = trainer.train_step(batches)
+        trainer.check_kernel_status()  # a bounded wait that ran out raises here, after the step
         if timing:
             ev1.record()
             ev1.synchronize()

@@ -216,3 +216,27 @@ def test_weighted_sq_norm():
     got = KC.weighted_sq_norm(ts, ws)
     ref = sum(w * t.double().pow(2).sum() for t, w in zip(ts, ws))
     assert abs(got.item() - ref.item()) / ref.item() < 1e-6
+
+
+def test_bounded_peer_wait_times_out_into_the_status_word():
+    """A cross-GPU flag wait whose flag nothing sets gives up after its bound,
+    records "cross-GPU flag wait timed out" in the status word and returns; the
+    context stays usable. Both "ranks" of the DP averaging kernel here are
+    buffers of this one GPU, and the second never announces itself."""
+    import time
+    from nano_megatron_b200 import _C
+    n = 1024
+    bufs = [torch.ones(n, device=DEV), torch.ones(n, device=DEV)]
+    flags = [torch.zeros(_C.dp_flag_bytes() // 4, dtype=torch.int32, device=DEV) for _ in range(2)]
+    KC.check_status(DEV)
+    t0 = time.monotonic()
+    _C.dp_allreduce([b.data_ptr() for b in bufs], [f.data_ptr() for f in flags], 0, 0, n, 1,
+                    KC.status_word(DEV), 0.25)
+    torch.cuda.synchronize()
+    waited = time.monotonic() - t0
+    assert 0.2 < waited < 30.0, waited
+    with pytest.raises(RuntimeError, match="cross-GPU flag wait timed out"):
+        KC.check_status(DEV)
+    assert torch.equal(bufs[0], torch.ones(n, device=DEV))  # gave up before touching data
+    KC.check_status(DEV)  # cleared; the context still works
+    assert float((bufs[0] + 1).sum()) == 2.0 * n
