@@ -203,11 +203,3 @@ def lm_head_cross_entropy(x, w, labels, vocab_start: int, vocab_end: int, pctx: 
                      gmax, gsum)
     K._count()
     return loss, logits, gmax, gsum, X
-
-
-def all_gather(x_local, pctx: ParallelContext):
-    """Plain sequence all-gather (NCCL), for the weight-gradient input."""
-    out = torch.empty((x_local.shape[0] * pctx.tp_size, *x_local.shape[1:]), dtype=x_local.dtype,
-                      device=x_local.device)
-    dist.all_gather_into_tensor(out, x_local.contiguous(), group=pctx.tp_group)
-    return out
