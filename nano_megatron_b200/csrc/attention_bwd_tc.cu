@@ -4,22 +4,25 @@
 //   dK/dV kernel (one CTA = 128 keys of one (batch, head); loops over the
 //   64-query blocks at or after it):
 //     S^T = K Q^T and dP^T = V dO^T      (tcgen05, M=128 keys, N=64 queries)
-//     P^T = exp(S^T*scale - lse[q]), dS^T = P^T (dP^T - D[q])   (4 warps, one
-//          key row per thread, causal mask on the diagonal blocks)
-//     dV += P^T dO and dK += dS^T Q      (tcgen05, accumulators stay in TMEM)
+//     P^T = exp(S^T*scale - lse[q]), dS^T = P^T (dP^T - D[q])   (one key row
+//          per thread, causal mask on the diagonal blocks; P^T and dS^T go
+//          back into TMEM as bf16)
+//     dV += P^T dO and dK += dS^T Q      (tcgen05 with A from TMEM; the
+//          accumulators stay in TMEM)
 //   dQ kernel (one CTA = 128 queries; loops over the 64-key blocks up to it):
-//     S = Q K^T, dP = dO V^T, dS = P (dP - D[q]), dQ += dS K.
+//     S = Q K^T, dP = dO V^T, dS = P (dP - D[q]) (back into TMEM), dQ += dS K.
 //
 // The dQ kernel recomputes S and dP instead of having the dK/dV kernel add
 // dQ partials with atomics: two extra 128x64x128 products per block pair buy
 // a fixed summation order and no fp32 atomic traffic.
 //
 // Both kernels: warp 0 issues TMA loads (tiles straight out of qkv / dO via
-// 3-D tensor maps) through a 3-stage ring, warp 1 issues the MMAs from an event
+// 3-D tensor maps) through a 4-stage ring, warp 1 issues the MMAs from an event
 // loop, and two elementwise warpgroups (warps 2-5, 6-9) take alternate blocks,
-// each with its own TMEM columns and smem operand tiles, so one group's
-// exp/convert work overlaps the tensor core's products for the other. Every
-// wait is bounded.
+// each with its own TMEM columns, so one group's exp/convert work overlaps the
+// tensor core's products for the other. The grid lists heads fastest, so the
+// CTAs with the most blocks of every head are dispatched first. Every wait is
+// bounded.
 // D[q] = rowsum(dO * O) comes from flash_bwd_dot_kernel (attention.cu).
 
 #include <cuda.h>
