@@ -4,7 +4,7 @@
     torchrun --nproc-per-node 8 bench.py --gpus 8 --steps K --warmup W
     python bench.py --impl reference ...                           # the reference, same config
 
-Model and data: vocab 128256, hidden 4096, 32 layers,
+Model and data (the named headline configuration): vocab 128256, hidden 4096, 32 layers,
 32 heads (head_dim 128), SwiGLU ffn 14336, RoPE theta 500000, untied
 embeddings, seq 8192, micro-batch 1, 16 microbatches of 1F1B, whole-block
 recompute, sequence parallelism, bf16 compute with fp32 master weights,

@@ -1,4 +1,4 @@
-"""Fused-collective microbenchmark on 2/4/8 GPUs.
+"""Fused-collective microbenchmark (the fused-collective configuration of the target) on 2/4/8 GPUs.
 
     torchrun --nproc-per-node N bench_tp.py [--tokens 4096 16384 65536]
 
