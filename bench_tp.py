@@ -21,6 +21,11 @@ For every token count M and (K, N) shape, times on each rank with CUDA events
                 fp32 softmax statistics with three NCCL all-reduces (MAX, SUM,
                 SUM), backward in torch with an NCCL reduce-scatter
 
+* Data-parallel gradient average of one fp32 bucket (``--ops dp``, 64 and 256 MB):
+    ours        the two-shot NVLink kernel of csrc/dp_reduce.cu (1/dp applied in the pass)
+    nccl        NCCL all_reduce with ReduceOp.AVG
+  roofline: every rank receives (t-1)/t of the bucket and sends as much.
+
 The roofline of a fused op is the slower of its FLOPs at the measured bf16
 GEMM peak and the bytes it must move over NVLink at 770 GB/s per direction
 (AG: (t-1)/t of the gathered input arrives; RS: (t-1)/t of the partial output
@@ -123,13 +128,43 @@ def bench_ce(args, pctx, dev, rank, t, timed, peak, peak_src):
     torch.cuda.empty_cache()
 
 
+def bench_dp(dev, rank, t, timed):
+    from nano_megatron_b200.ops import dp_reduce
+    from nano_megatron_b200.parallel import init_parallel
+    ctx = init_parallel(tp_size=1, pp_size=1)  # all ranks form the DP group
+    for mb in (64, 256):
+        n = mb * (1 << 20) // 4
+
+        class _Flat:  # the two members the workspace uses
+            numel = n
+            grad = torch.randn(n, device=dev)
+
+            @classmethod
+            def rehome_grad(cls, g):
+                g.copy_(cls.grad)
+                cls.grad = g
+
+        ws = dp_reduce.DPWorkspace(ctx, _Flat)
+        plain = torch.randn(n, device=dev)
+        res = {"ours": timed(lambda: ws.all_reduce_avg(0, n)),
+               "nccl": timed(lambda: dist.all_reduce(plain, op=dist.ReduceOp.AVG))}
+        roof = (t - 1) / t * n * 4 / (LINK_GBS * 1e6)
+        if rank == 0:
+            print(json.dumps({"op": "dp_allreduce_avg", "ranks": t, "MB": mb,
+                              "ms": {k: round(v, 4) for k, v in res.items()},
+                              "roofline_ms": round(roof, 4), "frac_of_roofline": round(roof / res["ours"], 3),
+                              "speedup_vs_nccl": round(res["nccl"] / res["ours"], 3)}), flush=True)
+        del ws, plain
+        torch.cuda.empty_cache()
+
+
 def main():
     p = argparse.ArgumentParser()
     p.add_argument("--tokens", type=int, nargs="+", default=[4096, 16384, 65536])
     p.add_argument("--shapes", default="4096x12288,4096x14336,14336x4096")
     p.add_argument("--iters", type=int, default=10)
     p.add_argument("--warmup", type=int, default=3)
-    p.add_argument("--ops", default="ag,rs,ce", help="comma list of ag, rs, ce")
+    p.add_argument("--ops", default="ag,rs,ce", help="comma list of ag, rs, ce, dp")
     p.add_argument("--ce-tokens", type=int, default=16384)
     p.add_argument("--ce-hidden", type=int, default=4096)
     p.add_argument("--ce-vocab", type=int, default=128256)
@@ -172,6 +207,8 @@ def main():
     gen = torch.Generator(device=dev).manual_seed(rank)
     if "ce" in ops:
         bench_ce(args, pctx, dev, rank, t, timed, peak, peak_src)
+    if "dp" in ops:
+        bench_dp(dev, rank, t, timed)
     for shape in args.shapes.split(","):
         K, N = (int(v) for v in shape.split("x"))
         for M in args.tokens:
