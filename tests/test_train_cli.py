@@ -1,6 +1,8 @@
 """End-to-end ``torchrun`` CLI: two steps straight through must produce
 bit-identical rank shards (model, optimizer, RNG, data cursor) to one step,
-save, restart from the checkpoint, one more step. TP=2 PP=2 SP recompute bf16."""
+save, restart from the checkpoint, one more step (TP=2 PP=2 SP recompute
+bf16); and DP=2 x PP=2 with the gradient bucketer must match one average
+after backward bit for bit."""
 
 import socket
 import struct
@@ -21,13 +23,13 @@ def _port():
         return s.getsockname()[1]
 
 
-def _run(out, tokens, steps, load=None):
+def _run(out, tokens, steps, load=None, layout=("--tp=2", "--pp=2"), extra=()):
     cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=4",
            "--master-addr=127.0.0.1", f"--master-port={_port()}", "-m", "nano_megatron_b200.train",
-           "--tp=2", "--pp=2", f"--steps={steps}", "--num-microbatches=2", "--micro-batch-size=1",
+           *layout, f"--steps={steps}", "--num-microbatches=2", "--micro-batch-size=1",
            "--n-layer=2", "--n-head=4", "--n-embd=32", "--vocab-size=64", "--seq-len=8",
            "--ffn-hidden-size=48", "--sequence-parallel", "--recompute", "--dtype=bfloat16",
-           f"--data={tokens}", f"--save={out}"]
+           f"--data={tokens}", f"--save={out}", *extra]
     if load is not None:
         cmd.append(f"--load={load}")
     env = dict(__import__("os").environ, OMP_NUM_THREADS="1")
@@ -61,6 +63,20 @@ def test_interrupted_training_matches_uninterrupted(tmp_path):
     a, b = tmp_path / "continuous" / "step_00000002", tmp_path / "resumed" / "step_00000002"
     for d in (a, b):
         assert (d / "manifest.pt").is_file() and len(list(d.glob("rank_*.pt"))) == 4
+    for r in range(4):
+        name = f"rank_{r:05d}.pt"
+        _equal(torch.load(b / name, weights_only=False), torch.load(a / name, weights_only=False))
+
+
+def test_dp_buckets_match_one_average_after_backward(tmp_path):
+    """DP=2 x PP=2: gradients averaged bucket by bucket during the last backward
+    (tiny buckets, so many) give bit-identical shards to one average after it."""
+    tokens = tmp_path / "tokens.bin"
+    tokens.write_bytes(struct.pack("=4096H", *(i % 64 for i in range(4096))))
+    layout = ("--tp=1", "--pp=2", "--dp=2")
+    _run(tmp_path / "buckets", tokens, 2, layout=layout, extra=("--dp-bucket-mb=0.002",))
+    _run(tmp_path / "single", tokens, 2, layout=layout, extra=("--dp-bucket-mb=0",))
+    a, b = tmp_path / "single" / "step_00000002", tmp_path / "buckets" / "step_00000002"
     for r in range(4):
         name = f"rank_{r:05d}.pt"
         _equal(torch.load(b / name, weights_only=False), torch.load(a / name, weights_only=False))
