@@ -122,9 +122,9 @@ def build_reference(tp, pp, device, n_layer):
     500000 (its ``build_rope_cache`` base argument) and untied embeddings
     (``GPTConfig.tie_word_embeddings=False``). Parameters are created directly
     on the GPU (default-device context) instead of on the CPU and then moved."""
-    ref = os.path.join(HERE, "baseline", "_ref")
+    ref = os.environ.get("NMB_REFERENCE_PATH") or os.path.join(HERE, "baseline", "_ref")
     if not os.path.isdir(os.path.join(ref, "nano_megatron")):
-        raise ImportError("reference not installed under baseline/_ref")
+        raise ImportError(f"reference package not found under {ref}")
     sys.path.insert(0, ref)
     from nano_megatron.grads import clip_grad_norm, finalize_gradients, synchronize_model_parameters
     from nano_megatron.model import GPT, GPTConfig, build_rope_cache

@@ -1,7 +1,8 @@
 """Parity with the reference implementation itself (installed under
-``baseline/_ref``; skipped when it is absent): same seed -> identical initial
-weights, logits and loss, gradients to fp32 rounding, and the same parameters
-after three AdamW steps of 1F1B training."""
+``baseline/_ref``, or the directory named by ``NMB_REFERENCE_PATH``; skipped
+when neither holds the ``nano_megatron`` package): same seed -> identical
+initial weights, logits and loss, gradients to fp32 rounding, and the same
+parameters after three AdamW steps of 1F1B training."""
 
 import os
 import sys
@@ -9,13 +10,14 @@ import sys
 import pytest
 import torch
 
-REF = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "baseline", "_ref")
+REF = os.environ.get("NMB_REFERENCE_PATH") or os.path.join(
+    os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "baseline", "_ref")
 
 
 @pytest.fixture(scope="module")
 def ref():
     if not os.path.isdir(os.path.join(REF, "nano_megatron")):
-        pytest.skip("reference not installed under baseline/_ref")
+        pytest.skip(f"reference package not found under {REF}")
     sys.path.insert(0, REF)
     try:
         import nano_megatron.model as model
