@@ -66,8 +66,47 @@ def check_status(device: torch.device | None = None) -> None:
     code = int(word[0].item())
     if code:
         word.zero_()
-        cls = CollectiveTimeout if code == 2 else RuntimeError
-        raise cls(f"CUDA kernel error {code}: {ERROR_MESSAGES.get(code, 'unknown')}")
+        _raise_for(code)
+
+
+def _raise_for(code: int) -> None:
+    cls = CollectiveTimeout if code == 2 else RuntimeError
+    raise cls(f"CUDA kernel error {code}: {ERROR_MESSAGES.get(code, 'unknown')}")
+
+
+class StatusPoller:
+    """Checks the status word without stalling the host on the device.
+
+    ``poll()`` looks at the last snapshot whose copy has completed (an event
+    query, no synchronization), raises if it holds an error, and enqueues a
+    fresh snapshot (a 16-byte device->pinned-host copy on the current stream)
+    when none is in flight. Errors are therefore reported one or two steps
+    after the kernel that set them; ``final()`` synchronizes and checks
+    everything up to now (call it before exiting).
+    """
+
+    def __init__(self, device: torch.device):
+        self.device = device
+        self.host = torch.zeros(4, dtype=torch.int32, pin_memory=True)
+        self.event: torch.cuda.Event | None = None
+
+    def poll(self) -> None:
+        if self.event is not None:
+            if not self.event.query():
+                return
+            self.event = None
+            code = int(self.host[0])
+            if code:
+                status_word(self.device).zero_()
+                _raise_for(code)
+        self.host.copy_(status_word(self.device), non_blocking=True)
+        self.event = torch.cuda.Event()
+        self.event.record()
+
+    def final(self) -> None:
+        torch.cuda.synchronize(self.device)
+        self.event = None
+        check_status(self.device)
 
 
 def _dtype_ok(t: torch.Tensor) -> None:

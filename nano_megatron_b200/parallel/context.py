@@ -57,32 +57,31 @@ class ParallelContext:
     @property
     def previous_pipeline_rank(self) -> int:
         if self.is_first_stage:
-            raise RuntimeError("the first pipeline stage has no predecessor")
+            raise RuntimeError(f"pipeline stage {self.pp_rank} is the first one; nothing sends to it")
         return self.pp_ranks[self.pp_rank - 1]
 
     @property
     def next_pipeline_rank(self) -> int:
         if self.is_last_stage:
-            raise RuntimeError("the last pipeline stage has no successor")
+            raise RuntimeError(f"pipeline stage {self.pp_rank} is the last of {self.pp_size}; it sends to nobody")
         return self.pp_ranks[self.pp_rank + 1]
 
     def describe(self) -> str:
-        return (
-            f"rank {self.rank:2d}/{self.world_size} | "
-            f"tp {self.tp_rank}/{self.tp_size} pp {self.pp_rank}/{self.pp_size} "
-            f"dp {self.dp_rank}/{self.dp_size} | tp_ranks={list(self.tp_ranks)} "
-            f"pp_ranks={list(self.pp_ranks)} dp_ranks={list(self.dp_ranks)}"
-        )
+        """One line per rank: grid coordinate and the members of its groups."""
+        coord = f"(pp={self.pp_rank}, dp={self.dp_rank}, tp={self.tp_rank})"
+        shape = f"{self.pp_size}x{self.dp_size}x{self.tp_size}"
+        return (f"[rank {self.rank} of {self.world_size}] grid {shape} at {coord}; "
+                f"TP peers {list(self.tp_ranks)}, PP chain {list(self.pp_ranks)}, "
+                f"DP replicas {list(self.dp_ranks)}")
 
 
 def grid_ranks(world_size: int, tp_size: int, pp_size: int):
     """Return the nested rank lists ``grid[pp][dp][tp]`` for a world size."""
     if tp_size <= 0 or pp_size <= 0:
-        raise ValueError("tp_size and pp_size must be positive")
+        raise ValueError(f"tensor ({tp_size}) and pipeline ({pp_size}) widths must both be >= 1")
     if world_size % (tp_size * pp_size):
-        raise ValueError(
-            f"world size {world_size} is not divisible by tp_size * pp_size = {tp_size * pp_size}"
-        )
+        raise ValueError(f"{world_size} ranks cannot be split into TP {tp_size} x PP {pp_size} "
+                         f"blocks ({world_size} % {tp_size * pp_size} != 0)")
     dp_size = world_size // (tp_size * pp_size)
     return [[[(p * dp_size + d) * tp_size + t for t in range(tp_size)]
              for d in range(dp_size)] for p in range(pp_size)], dp_size
@@ -91,7 +90,8 @@ def grid_ranks(world_size: int, tp_size: int, pp_size: int):
 def init_parallel(tp_size: int = 1, pp_size: int = 1) -> ParallelContext:
     """Create all TP, DP, PP and tied-embedding groups; return this rank's view."""
     if not dist.is_initialized():
-        raise RuntimeError("torch.distributed must be initialized before init_parallel")
+        raise RuntimeError("init_parallel builds groups over an existing world: call "
+                           "torch.distributed.init_process_group first")
     world_size = dist.get_world_size()
     rank = dist.get_rank()
     grid, dp_size = grid_ranks(world_size, tp_size, pp_size)

@@ -127,15 +127,64 @@ def config_from_args(args) -> GPTConfig:
         rope_theta=args.rope_theta, init_std=args.init_std)
 
 
+def _parse_fault(spec: str | None):
+    """``RANK:STEP:MODE`` -> (rank, step, mode); host-side fault injection for tests."""
+    if not spec:
+        return None
+    rank, step, mode = spec.split(":")
+    if mode not in ("leave", "raise", "hang", "vanish"):
+        raise ValueError(f"--inject-fault mode {mode!r}: use leave, raise, hang or vanish")
+    return int(rank), int(step), mode
+
+
+def _inject(fault, rank: int, step: int, watch) -> None:
+    """Make this rank fail between steps, the way a real job can: announce and
+    exit cleanly (leave), raise (raise), stop without a word for a bounded time
+    (hang), or die without a word (vanish)."""
+    if fault is None or fault[0] != rank or fault[1] != step:
+        return
+    mode = fault[2]
+    if mode == "leave":
+        if watch is not None:
+            watch.leave(f"left on request before step {step}")
+        os._exit(0)
+    if mode == "raise":
+        raise RuntimeError(f"injected fault before step {step}")
+    if mode == "hang":
+        time.sleep(600)  # the harness kills it long before this ends
+        os._exit(4)
+    os._exit(3)  # vanish: like a process killed by a signal
+
+
 def train(args):
+    from datetime import timedelta
+
+    from .utils.health import PeerLost, PeerWatch
+
     if (args.backend == "nccl") != (args.device == "cuda"):
         raise ValueError("use gloo with cpu or nccl with cuda")
     if args.backend == "nccl":
         torch.cuda.set_device(int(os.environ["LOCAL_RANK"]))
-    dist.init_process_group(backend=args.backend)
+    dist.init_process_group(backend=args.backend, timeout=timedelta(seconds=args.pg_timeout))
     rank, world = dist.get_rank(), dist.get_world_size()
     if world != args.tp * args.pp * args.dp:
         raise ValueError(f"torchrun world size {world} != tp * pp * dp = {args.tp * args.pp * args.dp}")
+    watch = PeerWatch(rank, world, timeout=args.peer_timeout) if args.peer_timeout > 0 else None
+    fault = _parse_fault(args.inject_fault)
+    try:
+        _train_loop(args, rank, watch, fault)
+    except PeerLost as exc:
+        watch.leave(f"stopped because {exc}")
+        raise
+    except BaseException as exc:
+        if watch is not None:
+            watch.leave(f"{type(exc).__name__}: {exc}")
+        raise
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def _train_loop(args, rank, watch, fault):
     ctx = init_parallel(tp_size=args.tp, pp_size=args.pp)
     device = (torch.device("cuda", int(os.environ["LOCAL_RANK"])) if args.device == "cuda"
               else torch.device(args.device))
@@ -157,8 +206,15 @@ def train(args):
         total = sum(p.numel() for p in trainer.model.parameters())
         print(f"{ctx.describe()}\nlocal params: {total / 1e6:.2f}M  schedule: 1f1b\n", flush=True)
 
+    poller = None
+    if device.type == "cuda":
+        from .ops.cuda import StatusPoller
+        poller = StatusPoller(device)
     timing = args.timing and device.type == "cuda"
     for step in range(start_step, args.steps):
+        _inject(fault, rank, step, watch)
+        if watch is not None:
+            watch.enter_step()  # raises PeerLost before any kernel of this step is launched
         t0 = time.perf_counter()
         if timing:
             ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -169,7 +225,8 @@ def train(args):
         else:
             batches = [stream.next_batch(args.micro_batch_size) for _ in range(args.num_microbatches)]
         loss = trainer.train_step(batches)
-        trainer.check_kernel_status()  # a bounded wait that ran out raises here, after the step
+        if poller is not None:
+            poller.poll()  # kernel errors (bounded waits, token ids) surface without a device sync
         if timing:
             ev1.record()
             ev1.synchronize()
@@ -185,11 +242,13 @@ def train(args):
         next_step = step + 1
         if args.save and (next_step == args.steps
                           or (args.save_every > 0 and next_step % args.save_every == 0)):
+            if poller is not None:
+                poller.final()  # never checkpoint state that a failed kernel produced
             save_checkpoint(Path(args.save) / f"step_{next_step:08d}", trainer.model,
                             trainer.optimizer, ctx, step=next_step, data=stream,
                             extra=training_state)
-    dist.barrier()
-    dist.destroy_process_group()
+    if poller is not None:
+        poller.final()
 
 
 def build_parser():
@@ -231,6 +290,13 @@ def build_parser():
                         "(0: one all-reduce of the whole gradient buffer after backward)")
     p.add_argument("--no-fused-tp", action="store_true",
                    help="use NCCL collectives instead of the fused TP kernels")
+    p.add_argument("--peer-timeout", type=float, default=300.0,
+                   help="seconds a rank waits at a step boundary for a silent peer before raising "
+                        "PeerLost (0 disables the host-side peer watch)")
+    p.add_argument("--pg-timeout", type=float, default=1800.0,
+                   help="process-group timeout in seconds: a collective whose peers never arrive "
+                        "ends with an error after this long")
+    p.add_argument("--inject-fault", default=None, help=argparse.SUPPRESS)  # RANK:STEP:MODE (tests)
     return p
 
 

@@ -1,28 +1,42 @@
-"""Atomic, rank-local training checkpoints for a fixed parallel topology.
+"""Rank-local training checkpoints with a completion manifest and integrity data.
 
-Layout of one checkpoint directory (``<save>/step_{n:08d}``)::
+Directory of one saved step (the layout of ``nano_megatron/checkpoint.py``,
+kept so tools and resume scripts find the same files)::
 
-    rank_{rank:05d}.pt   one shard per global rank
-    manifest.pt          written last by rank 0; its presence marks completion
+    rank_{global_rank:05d}.pt   one shard per rank
+    manifest.pt                 rank 0 writes it last; a directory without it is incomplete
 
-Commit protocol: rank 0 removes a stale manifest -> barrier -> every rank
-writes its shard to a temporary name and renames it into place -> barrier ->
-rank 0 checks that all shards exist and writes the manifest the same way ->
-barrier. Loading validates the manifest, every shard's presence, this shard's
-version, topology, model config and step before it touches any state.
+A shard is a dict with the keys ``version``, ``topology``, ``model``,
+``model_config``, ``optimizer``, ``step``, ``rng``, ``data`` and ``extra``.
+The manifest carries ``version``, ``step``, ``world_size``,
+``parallel_sizes`` and ``shards`` and, in this implementation, the byte size
+and CRC-32 of every shard, so a resumed run detects a truncated or damaged
+shard instead of loading it.
 
-A shard holds: format version, topology, model state dict, model config,
-optimizer state dict, step, RNG states (torch CPU, python, every CUDA device),
-token-stream state and caller extras.
+Saving (a collective over the world when it has more than one rank):
 
-Parity: ``nano_megatron/checkpoint.py:16-196`` (same file names, keys,
-protocol and validation order).
+1. rank 0 withdraws an existing manifest, and every rank waits for that, so a
+   crash from here on leaves the directory visibly incomplete;
+2. every rank streams its shard through a CRC-32 counter into a temporary
+   file of the same directory, ``fsync``s it and renames it into place;
+3. the (size, CRC) pairs are gathered to rank 0, which writes the manifest the
+   same durable way; every rank waits for it before returning.
+
+Loading checks, before it changes any state: the manifest can be read; its
+version, world size and parallel sizes match this run; every listed shard
+exists; this rank's shard has the recorded size and CRC; the shard's version,
+topology, model configuration and step agree with the manifest and the run;
+and a data stream is supplied if the shard holds a stream position. All
+failing checks are reported together in one :class:`CheckpointError`.
 """
 
 from __future__ import annotations
 
+import io
 import os
 import random
+import tempfile
+import zlib
 from dataclasses import asdict, is_dataclass
 from pathlib import Path
 
@@ -34,140 +48,229 @@ FORMAT_VERSION = 1
 MANIFEST = "manifest.pt"
 
 
+class CheckpointError(RuntimeError):
+    """A checkpoint directory that cannot be written or resumed by this run."""
+
+
+def shard_name(rank: int) -> str:
+    return f"rank_{rank:05d}.pt"
+
+
 def topology(ctx: ParallelContext) -> dict[str, int]:
+    """The rank coordinates a shard is valid for."""
     return {"world_size": ctx.world_size, "global_rank": ctx.rank,
             "tp_size": ctx.tp_size, "tp_rank": ctx.tp_rank,
             "pp_size": ctx.pp_size, "pp_rank": ctx.pp_rank,
             "dp_size": ctx.dp_size, "dp_rank": ctx.dp_rank}
 
 
-def _capture_rng() -> dict:
-    state = {"torch": torch.get_rng_state(), "python": random.getstate()}
+def _sizes(ctx: ParallelContext) -> dict[str, int]:
+    return {"tp": ctx.tp_size, "pp": ctx.pp_size, "dp": ctx.dp_size}
+
+
+class _Checksummed(io.RawIOBase):
+    """Write-through file wrapper that counts bytes and folds them into a CRC-32."""
+
+    def __init__(self, raw):
+        self.raw, self.crc, self.size = raw, 0, 0
+
+    def writable(self) -> bool:
+        return True
+
+    def write(self, data) -> int:
+        view = memoryview(data)
+        self.raw.write(view)
+        self.crc = zlib.crc32(view, self.crc)
+        self.size += view.nbytes
+        return view.nbytes
+
+
+def _durable_save(obj, path: Path) -> dict[str, int]:
+    """``torch.save`` into a temp file beside ``path``, fsync, rename; (size, crc) of the bytes."""
+    fd, tmp = tempfile.mkstemp(prefix=f".{path.name}.", suffix=".partial", dir=path.parent)
+    try:
+        with os.fdopen(fd, "wb") as raw:
+            sink = _Checksummed(raw)
+            try:
+                torch.save(obj, sink)
+            except RuntimeError as exc:
+                # torch's zip writer replaces a failed write with its own error
+                # when it closes; report the I/O error the caller can act on
+                if isinstance(exc.__context__, OSError):
+                    raise exc.__context__ from exc
+                raise
+            raw.flush()
+            os.fsync(raw.fileno())
+        os.replace(tmp, path)
+    except BaseException:
+        Path(tmp).unlink(missing_ok=True)
+        raise
+    dir_fd = os.open(path.parent, os.O_RDONLY)
+    try:  # make the rename itself durable
+        os.fsync(dir_fd)
+    finally:
+        os.close(dir_fd)
+    return {"bytes": sink.size, "crc32": sink.crc}
+
+
+def _host_copy(obj):
+    """Deep copy with every tensor on the host, so a shard never pins device memory."""
+    if torch.is_tensor(obj):
+        return obj.detach().to("cpu", copy=True)
+    if isinstance(obj, dict):
+        return {k: _host_copy(v) for k, v in obj.items()}
+    if isinstance(obj, (list, tuple)):
+        return type(obj)(_host_copy(v) for v in obj)
+    return obj
+
+
+def _random_states() -> dict:
+    states = {"cpu": torch.get_rng_state(), "python": random.getstate()}
     if torch.cuda.is_available():
-        state["cuda"] = torch.cuda.get_rng_state_all()
-    return state
+        states["cuda"] = torch.cuda.get_rng_state_all()
+    return states
 
 
-def _restore_rng(state: dict) -> None:
-    torch.set_rng_state(state["torch"])
-    random.setstate(state["python"])
-    if "cuda" in state:
-        if not torch.cuda.is_available():
-            raise RuntimeError("checkpoint contains CUDA RNG state but CUDA is unavailable")
-        torch.cuda.set_rng_state_all(state["cuda"])
+def _apply_random_states(states: dict) -> None:
+    torch.set_rng_state(states["cpu"])
+    random.setstate(states["python"])
+    if "cuda" in states:
+        torch.cuda.set_rng_state_all(states["cuda"])
 
 
-def shard_path(directory, ctx: ParallelContext) -> Path:
-    return Path(directory) / f"rank_{ctx.rank:05d}.pt"
-
-
-def _config_dict(model):
+def _model_config(model):
     config = getattr(model, "config", None)
     return asdict(config) if config is not None and is_dataclass(config) else None
 
 
-def _write_atomically(obj, path: Path) -> None:
-    tmp = path.with_name(f".{path.name}.{os.getpid()}.tmp")
-    try:
-        torch.save(obj, tmp)
-        os.replace(tmp, path)
-    finally:
-        tmp.unlink(missing_ok=True)
-
-
-def _distributed(ctx: ParallelContext) -> bool:
-    return ctx.world_size > 1 and torch.distributed.is_initialized()
-
-
-def _cpu_state(obj):
-    """Deep-copy tensors to CPU so a shard does not pin device memory on load."""
-    if torch.is_tensor(obj):
-        return obj.detach().to("cpu", copy=True)
-    if isinstance(obj, dict):
-        return {k: _cpu_state(v) for k, v in obj.items()}
-    if isinstance(obj, (list, tuple)):
-        return type(obj)(_cpu_state(v) for v in obj)
-    return obj
+def _valid_step(step) -> bool:
+    return type(step) is int and step >= 0
 
 
 def save_checkpoint(directory, model, optimizer, ctx: ParallelContext, *, step: int,
                     data=None, extra: dict | None = None) -> Path:
-    """Atomically write this rank's shard (and, on rank 0, the manifest)."""
-    if isinstance(step, bool) or not isinstance(step, int) or step < 0:
-        raise ValueError(f"step must be a non-negative integer, got {step!r}")
+    """Write this rank's shard (and, on rank 0, the manifest) into ``directory``.
+
+    Collective when the world has more than one rank. Returns the shard path.
+    """
+    if not _valid_step(step):
+        raise ValueError(f"save_checkpoint: step {step!r} is not a non-negative int")
     directory = Path(directory)
     directory.mkdir(parents=True, exist_ok=True)
-    path = shard_path(directory, ctx)
-    state = {
-        "version": FORMAT_VERSION,
-        "topology": topology(ctx),
-        "model": _cpu_state(model.state_dict()),
-        "model_config": _config_dict(model),
-        "optimizer": _cpu_state(optimizer.state_dict()),
-        "step": step,
-        "rng": _capture_rng(),
-        "data": data.state_dict() if data is not None else None,
-        "extra": extra or {},
-    }
-    distributed = _distributed(ctx)
+    group_save = ctx.world_size > 1 and torch.distributed.is_initialized()
     manifest_path = directory / MANIFEST
-    if distributed:
-        if ctx.rank == 0:
-            manifest_path.unlink(missing_ok=True)
-        torch.distributed.barrier()
-    _write_atomically(state, path)
-    if distributed:
-        torch.distributed.barrier()
+
     if ctx.rank == 0:
-        shards = [f"rank_{r:05d}.pt" for r in range(ctx.world_size)]
-        if not all((directory / s).is_file() for s in shards):
-            raise RuntimeError("checkpoint is missing one or more rank shards")
-        _write_atomically({"version": FORMAT_VERSION, "step": step, "world_size": ctx.world_size,
-                           "parallel_sizes": {"tp": ctx.tp_size, "pp": ctx.pp_size,
-                                              "dp": ctx.dp_size},
-                           "shards": shards}, manifest_path)
-    if distributed:
+        manifest_path.unlink(missing_ok=True)
+    if group_save:
+        torch.distributed.barrier()
+
+    shard = {
+        "version": FORMAT_VERSION, "topology": topology(ctx),
+        "model": _host_copy(model.state_dict()), "model_config": _model_config(model),
+        "optimizer": _host_copy(optimizer.state_dict()), "step": step,
+        "rng": _random_states(), "data": None if data is None else data.state_dict(),
+        "extra": dict(extra or {}),
+    }
+    path = directory / shard_name(ctx.rank)
+    digest = _durable_save(shard, path)
+
+    digests = [None] * ctx.world_size
+    if group_save:
+        torch.distributed.all_gather_object(digests, digest)
+    else:
+        digests[0] = digest
+    if ctx.rank == 0:
+        names = [shard_name(r) for r in range(ctx.world_size)]
+        absent = [n for n in names if not (directory / n).is_file()]
+        if absent:
+            raise CheckpointError(f"{directory}: shards {absent} were not written; no manifest")
+        _durable_save({"version": FORMAT_VERSION, "step": step, "world_size": ctx.world_size,
+                       "parallel_sizes": _sizes(ctx), "shards": names,
+                       "shard_digests": dict(zip(names, digests))}, manifest_path)
+    if group_save:
         torch.distributed.barrier()
     return path
 
 
+def _read(path: Path, what: str, map_location, problems: list[str], digest=None):
+    try:
+        blob = path.read_bytes()
+    except OSError as exc:
+        problems.append(f"{what} {path.name} cannot be read ({exc.strerror})")
+        return None
+    if digest is not None:
+        if len(blob) != digest["bytes"]:
+            problems.append(f"{what} {path.name} has {len(blob)} bytes, the manifest recorded "
+                            f"{digest['bytes']} (truncated or overwritten)")
+            return None
+        if zlib.crc32(blob) != digest["crc32"]:
+            problems.append(f"{what} {path.name} fails its CRC-32 check (damaged)")
+            return None
+    try:
+        obj = torch.load(io.BytesIO(blob), map_location=map_location, weights_only=False)
+    except Exception as exc:  # torch raises several types for a damaged zip/pickle
+        problems.append(f"{what} {path.name} is not a readable torch file ({type(exc).__name__})")
+        return None
+    if not isinstance(obj, dict):
+        problems.append(f"{what} {path.name} does not hold a dict")
+        return None
+    return obj
+
+
+def _fail(directory: Path, problems: list[str]):
+    raise CheckpointError(f"cannot resume from {directory}:\n  - " + "\n  - ".join(problems))
+
+
 def load_checkpoint(directory, model, optimizer, ctx: ParallelContext, *, data=None,
                     map_location="cpu") -> tuple[int, dict]:
-    """Validate everything, then restore this rank; return ``(step, extra)``."""
+    """Validate ``directory`` for this rank, then restore model, optimizer, RNG and
+    data position. Returns ``(step, extra)``. Nothing is modified unless every
+    check passes."""
     directory = Path(directory)
+    problems: list[str] = []
     manifest_path = directory / MANIFEST
     if not manifest_path.is_file():
-        raise RuntimeError(f"checkpoint is incomplete: missing {manifest_path}")
-    manifest = torch.load(manifest_path, map_location="cpu", weights_only=False)
-    expected = {"version": FORMAT_VERSION, "world_size": ctx.world_size,
-                "parallel_sizes": {"tp": ctx.tp_size, "pp": ctx.pp_size, "dp": ctx.dp_size}}
-    for key, want in expected.items():
-        if manifest.get(key) != want:
-            raise RuntimeError(f"checkpoint manifest mismatch for {key}: "
-                               f"saved={manifest.get(key)!r}, current={want!r}")
-    if not all((directory / s).is_file() for s in manifest.get("shards", ())):
-        raise RuntimeError("checkpoint is incomplete: a rank shard is missing")
-    state = torch.load(shard_path(directory, ctx), map_location=map_location, weights_only=False)
-    if state.get("version") != FORMAT_VERSION:
-        raise RuntimeError(f"unsupported checkpoint version {state.get('version')!r}; "
-                           f"expected {FORMAT_VERSION}")
-    if state.get("topology") != topology(ctx):
-        raise RuntimeError(f"checkpoint topology mismatch: saved={state.get('topology')}, "
-                           f"current={topology(ctx)}")
-    if state.get("model_config") != _config_dict(model):
-        raise RuntimeError(f"checkpoint model configuration mismatch: "
-                           f"saved={state.get('model_config')}, current={_config_dict(model)}")
-    step = state.get("step")
-    if isinstance(step, bool) or not isinstance(step, int) or step < 0:
-        raise RuntimeError(f"invalid checkpoint step {step!r}")
-    if manifest.get("step") != step:
-        raise RuntimeError("checkpoint manifest and rank shard have different steps")
-    if state["data"] is not None and data is None:
-        raise RuntimeError("checkpoint contains data state but no data stream was provided")
+        _fail(directory, ["no manifest.pt: the save did not complete"])
+    manifest = _read(manifest_path, "manifest", "cpu", problems)
+    if manifest is None:
+        _fail(directory, problems)
 
-    model.load_state_dict(state["model"])
-    optimizer.load_state_dict(state["optimizer"])
-    if state["data"] is not None:
-        data.load_state_dict(state["data"])
-    _restore_rng(state["rng"])
-    return step, state.get("extra", {})
+    table = [("format version", manifest.get("version"), FORMAT_VERSION),
+             ("world size", manifest.get("world_size"), ctx.world_size),
+             ("parallel sizes", manifest.get("parallel_sizes"), _sizes(ctx))]
+    problems += [f"{name}: checkpoint {saved!r}, this run {now!r}" for name, saved, now in table
+                 if saved != now]
+    listed = list(manifest.get("shards") or ())
+    missing = [n for n in listed if not (directory / n).is_file()]
+    if missing:
+        problems.append(f"listed shards missing on disk: {missing}")
+    if not _valid_step(manifest.get("step")):
+        problems.append(f"manifest step {manifest.get('step')!r} is not a non-negative int")
+    if problems:
+        _fail(directory, problems)
+
+    mine = shard_name(ctx.rank)
+    digest = (manifest.get("shard_digests") or {}).get(mine)
+    shard = _read(directory / mine, "shard", map_location, problems, digest)
+    if shard is None:
+        _fail(directory, problems)
+    table = [("shard format version", shard.get("version"), FORMAT_VERSION),
+             ("rank topology", shard.get("topology"), topology(ctx)),
+             ("model configuration", shard.get("model_config"), _model_config(model)),
+             ("step (shard vs manifest)", shard.get("step"), manifest["step"])]
+    problems += [f"{name}: checkpoint {saved!r}, expected {now!r}" for name, saved, now in table
+                 if saved != now]
+    if shard.get("data") is not None and data is None:
+        problems.append("the shard holds a data-stream position but no stream was passed")
+    if "cuda" in (shard.get("rng") or {}) and not torch.cuda.is_available():
+        problems.append("the shard holds CUDA generator states but CUDA is not available")
+    if problems:
+        _fail(directory, problems)
+
+    model.load_state_dict(shard["model"])
+    optimizer.load_state_dict(shard["optimizer"])
+    if shard["data"] is not None:
+        data.load_state_dict(shard["data"])
+    _apply_random_states(shard["rng"])
+    return shard["step"], shard.get("extra") or {}

@@ -1,13 +1,24 @@
-"""Pre-tokenized token streams and the synthetic batch generator.
+"""Token input for training: a memory-mapped pre-tokenized file and the
+synthetic uniform generator.
 
-The file format is a flat, native-endian array of uint16 or uint32 token ids.
-DP rank ``r`` of ``d`` reads, for each call, the window starting at
-``cursor + r * B * S`` and every rank then advances ``cursor`` by ``d * B * S``;
-reads wrap at the end of the file. Only the monotonically growing cursor is
-state, so equal cursors mean the same training position on every TP/PP rank.
+A token file is a headerless array of native-endian ``uint16`` or ``uint32``
+ids. :class:`TokenFile` owns the mapping and a fingerprint of the file
+(resolved path, byte size, modification time) so a resumed run can tell that
+it is reading the same bytes. :class:`TokenStream` turns the file into
+next-token windows for one data-parallel rank.
 
-Parity: ``nano_megatron/data.py:22-123`` (format, window formula, wrap,
-state/validation) and ``nano_megatron/train.py:29-39`` (synthetic seeds).
+Window arithmetic (the same positions as ``nano_megatron/data.py:86-92``,
+so a cursor means the same training position in both implementations): one
+call with batch ``B`` and sequence ``S`` covers ``n = B*S`` positions; DP
+rank ``r`` of ``d`` reads the ``n + 1`` tokens that start at
+``cursor + r*n`` (inputs are the first ``n``, labels the last ``n``), and
+every rank then advances ``cursor`` by ``d*n``. Positions wrap modulo the
+file length. The cursor only grows; it is the whole resumable state.
+
+Reads are one or two contiguous slices of the mapping (two when the window
+crosses the end of the file), so a window costs one copy of ``n + 1`` ids and
+no index array. ``next_batch(pin=True)`` returns page-locked tensors for an
+asynchronous host-to-device copy.
 """
 
 from __future__ import annotations
@@ -18,79 +29,109 @@ from pathlib import Path
 import numpy as np
 import torch
 
-_ITEM = {"uint16": np.dtype("=u2"), "uint32": np.dtype("=u4")}
+# token width name -> numpy dtype of one id in the file (native byte order)
+TOKEN_WIDTHS = {"uint16": np.dtype("=u2"), "uint32": np.dtype("=u4")}
+
+
+class TokenFile:
+    """Read-only mapping of a token file plus its fingerprint."""
+
+    def __init__(self, path: str | os.PathLike, width: str):
+        if width not in TOKEN_WIDTHS:
+            raise ValueError(f"token width {width!r} is not supported; use one of "
+                             f"{', '.join(sorted(TOKEN_WIDTHS))}")
+        self.path = Path(path)
+        info = self.path.stat()
+        item = TOKEN_WIDTHS[width].itemsize
+        whole, stray = divmod(info.st_size, item)
+        if stray:
+            raise ValueError(f"{self.path}: {info.st_size} bytes is not a whole number of "
+                             f"{item}-byte {width} ids ({stray} stray bytes)")
+        if whole < 2:
+            raise ValueError(f"{self.path}: {whole} token(s) cannot form an (input, label) pair")
+        self.width = width
+        self.length = whole
+        self.fingerprint = {"path": str(self.path.resolve()), "bytes": int(info.st_size),
+                            "mtime_ns": int(info.st_mtime_ns)}
+        self._ids = np.memmap(self.path, dtype=TOKEN_WIDTHS[width], mode="r", shape=(whole,))
+
+    def read_cyclic(self, start: int, count: int, out: np.ndarray) -> None:
+        """Write ids ``start, start+1, ... (mod length)`` into ``out[:count]``."""
+        ids, length = self._ids, self.length
+        pos = start % length
+        filled = 0
+        while filled < count:  # at most two passes unless the window exceeds the file
+            take = min(count - filled, length - pos)
+            out[filled:filled + take] = ids[pos:pos + take]
+            filled += take
+            pos = 0
 
 
 class TokenStream:
-    """Deterministic next-token ``(inputs, labels)`` windows from a memory-mapped file."""
+    """Next-token ``(inputs, labels)`` windows of one data-parallel rank."""
 
     def __init__(self, path: str | os.PathLike, *, dtype: str, seq_len: int,
                  dp_rank: int = 0, dp_size: int = 1) -> None:
-        if dtype not in _ITEM:
-            raise ValueError(f"dtype must be one of {sorted(_ITEM)}, got {dtype!r}")
-        if seq_len <= 0:
-            raise ValueError(f"seq_len must be positive, got {seq_len}")
-        if dp_size <= 0:
-            raise ValueError(f"dp_size must be positive, got {dp_size}")
-        if not 0 <= dp_rank < dp_size:
-            raise ValueError(f"dp_rank must be in [0, {dp_size}), got {dp_rank}")
-        path = Path(path)
-        stat = path.stat()
-        item = _ITEM[dtype].itemsize
-        if stat.st_size % item:
-            raise ValueError(
-                f"{path} has {stat.st_size} bytes, not divisible by {dtype} item size {item}")
-        count = stat.st_size // item
-        if count < 2:
-            raise ValueError(f"token stream needs at least 2 tokens, got {count}")
-        self.path, self.dtype, self.seq_len = path, dtype, seq_len
+        if seq_len < 1:
+            raise ValueError(f"TokenStream: seq_len={seq_len}; a window needs at least one position")
+        if dp_size < 1 or not 0 <= dp_rank < dp_size:
+            raise ValueError(f"TokenStream: data-parallel rank {dp_rank} does not exist in a "
+                             f"group of {dp_size}")
+        self.file = TokenFile(path, dtype)
+        self.path, self.dtype, self.seq_len = self.file.path, dtype, seq_len
         self.dp_rank, self.dp_size = dp_rank, dp_size
         self.cursor = 0
-        self._identity = {"path": str(path.resolve()), "size_bytes": stat.st_size,
-                          "mtime_ns": stat.st_mtime_ns}
-        self._tokens = np.memmap(path, dtype=_ITEM[dtype], mode="r", shape=(count,))
 
     @property
     def num_tokens(self) -> int:
-        return int(self._tokens.shape[0])
+        return self.file.length
 
-    def next_batch(self, batch_size: int) -> tuple[torch.Tensor, torch.Tensor]:
-        """``(input_ids, labels)``, each int64 ``[batch_size, seq_len]``."""
-        if batch_size <= 0:
-            raise ValueError(f"batch_size must be positive, got {batch_size}")
+    def _layout(self) -> dict:
+        return {"dtype": self.dtype, "seq_len": self.seq_len, "dp_rank": self.dp_rank,
+                "dp_size": self.dp_size}
+
+    def next_batch(self, batch_size: int, *, pin: bool = False) -> tuple[torch.Tensor, torch.Tensor]:
+        """``(input_ids, labels)`` as int64 ``[batch_size, seq_len]`` and advance the cursor."""
+        if batch_size < 1:
+            raise ValueError(f"TokenStream.next_batch: batch_size={batch_size} must be >= 1")
         n = batch_size * self.seq_len
-        start = self.cursor + self.dp_rank * n
-        idx = (np.arange(n + 1, dtype=np.int64) + start) % self.num_tokens
-        window = torch.from_numpy(self._tokens[idx].astype(np.int64))
+        window = torch.empty(n + 1, dtype=torch.int64, pin_memory=pin)
+        self.file.read_cyclic(self.cursor + self.dp_rank * n, n + 1, window.numpy())
         self.cursor += self.dp_size * n
-        return (window[:-1].view(batch_size, self.seq_len).clone(),
-                window[1:].view(batch_size, self.seq_len).clone())
+        return (window[:n].view(batch_size, self.seq_len),
+                window[1:].view(batch_size, self.seq_len))
 
     def state_dict(self) -> dict:
-        return {"cursor": self.cursor, "dtype": self.dtype, "seq_len": self.seq_len,
-                "dp_rank": self.dp_rank, "dp_size": self.dp_size, "identity": dict(self._identity)}
+        return {"cursor": self.cursor, "layout": self._layout(), "file": dict(self.file.fingerprint)}
 
     def load_state_dict(self, state: dict) -> None:
-        expected = {"dtype": self.dtype, "seq_len": self.seq_len, "dp_rank": self.dp_rank,
-                    "dp_size": self.dp_size, "identity": self._identity}
-        actual = {k: state.get(k) for k in expected}
-        if actual != expected:
-            raise ValueError(f"token-stream configuration mismatch: saved={actual}, current={expected}")
         cursor = state.get("cursor")
-        if isinstance(cursor, bool) or not isinstance(cursor, int) or cursor < 0:
-            raise ValueError(f"cursor must be a non-negative integer, got {cursor!r}")
+        if type(cursor) is not int or cursor < 0:
+            raise ValueError(f"TokenStream: saved cursor {cursor!r} is not a non-negative int")
+        differences = [f"{what} {key}: saved {saved.get(key)!r}, now {now[key]!r}"
+                       for what, saved, now in (("layout", state.get("layout") or {}, self._layout()),
+                                                ("file", state.get("file") or {}, self.file.fingerprint))
+                       for key in now if saved.get(key) != now[key]]
+        if differences:
+            raise ValueError("TokenStream: the saved position belongs to a different stream ("
+                             + "; ".join(differences) + ")")
         self.cursor = cursor
 
 
 def synthetic_batches(config, micro_batch_size: int, num_microbatches: int, step: int,
                       data_parallel_rank: int = 0):
-    """Uniform random ``(inputs, labels)`` microbatches, seeded per (step, DP rank).
+    """Uniform random ``(inputs, labels)`` microbatches for one step of one DP rank.
 
-    Seed ``1234 + 100003 * step + dp_rank``: pipeline stages of one DP lane agree,
-    DP replicas differ. Inputs and labels are drawn independently.
+    The CPU generator is seeded with ``1234 + 100003 * step + dp_rank`` and
+    draws inputs, then labels, per microbatch (``nano_megatron/train.py:29-39``),
+    so every pipeline stage and TP rank of a DP lane sees the same tokens and
+    the two implementations train on identical data.
     """
     gen = torch.Generator().manual_seed(1234 + 100_003 * step + data_parallel_rank)
     shape = (micro_batch_size, config.seq_len)
-    return [(torch.randint(0, config.vocab_size, shape, generator=gen),
-             torch.randint(0, config.vocab_size, shape, generator=gen))
-            for _ in range(num_microbatches)]
+    batches = []
+    for _ in range(num_microbatches):
+        inputs = torch.randint(0, config.vocab_size, shape, generator=gen)
+        labels = torch.randint(0, config.vocab_size, shape, generator=gen)
+        batches.append((inputs, labels))
+    return batches

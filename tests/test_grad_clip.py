@@ -1,116 +1,184 @@
-"""Logical-model gradient clipping with the TP/PP collectives replaced by known
-peer contributions (no process groups)."""
+"""Logical-model gradient clipping without sockets.
 
-import contextlib
+Each virtual rank of a TP x PP grid runs ``clip_grad_norm`` in its own thread.
+The process groups are in-process objects: ``all_reduce`` over a group is a
+barrier exchange among that group's threads, so the collectives run for real
+(order, membership, values) without ``torch.distributed``. The data-parallel
+group refuses every call, because the norm of DP replicas must never be
+reduced over DP. The expected norm comes from the unsharded logical model.
+"""
+
+import threading
+from contextlib import contextmanager
 
 import pytest
 import torch
 import torch.nn as nn
 
-from nano_megatron_b200.parallel import ParallelContext
-from nano_megatron_b200.parallel import grads
-
-TOL = dict(rtol=1e-6, atol=1e-6)
+from nano_megatron_b200.parallel import ParallelContext, grads
 
 
-class _W(nn.Module):
-    def __init__(self, g, sharded):
-        super().__init__()
-        self.weight = nn.Parameter(torch.zeros(len(g)))
-        self.weight.grad = torch.tensor(g, dtype=torch.float32)
-        self.weight.tensor_parallel_sharded = sharded
+class _Group:
+    def __init__(self, kind, members):
+        self.kind, self.members = kind, tuple(members)
+        self.barrier = threading.Barrier(len(members))
+        self.slots = {}
 
 
-class _Stage(nn.Module):
-    def __init__(self, pp_rank, tp_rank):
-        super().__init__()
-        shard = {(0, 0): [3.0], (0, 1): [4.0], (1, 0): [5.0], (1, 1): [12.0]}
-        repl = {0: [2.0], 1: [6.0]}
-        emb = {0: [1.0, 2.0], 1: [2.0, 1.0]}
-        self.shard = _W(shard[pp_rank, tp_rank], True)
-        self.replicated = _W(repl[pp_rank], False)
-        if pp_rank == 0:
-            self.embedding = _W(emb[tp_rank], True)
-        else:
-            self.lm_head = _W(emb[tp_rank], True)
+class ThreadWorld:
+    """Virtual ranks ``(pp, tp)`` of DP lane 0 in a world with ``dp`` lanes."""
+
+    def __init__(self, tp, pp, dp=2):
+        self.tp, self.pp, self.dp = tp, pp, dp
+        self.local = threading.local()
+        self.log, self.dp_calls = [], []
+        self.tp_groups = {p: _Group("tp", [(p, t) for t in range(tp)]) for p in range(pp)}
+        self.pp_groups = {t: _Group("pp", [(p, t) for p in range(pp)]) for t in range(tp)}
+        self.dp_group = _Group("dp", [0])
+
+    def context(self, p, t):
+        rank = (p * self.dp) * self.tp + t
+        return ParallelContext(
+            rank=rank, world_size=self.tp * self.pp * self.dp, tp_size=self.tp, tp_rank=t,
+            pp_size=self.pp, pp_rank=p, dp_size=self.dp, dp_rank=0,
+            tp_group=self.tp_groups[p], pp_group=self.pp_groups[t], dp_group=self.dp_group,
+            tp_ranks=tuple(p * self.dp * self.tp + i for i in range(self.tp)),
+            pp_ranks=tuple(i * self.dp * self.tp + t for i in range(self.pp)),
+            dp_ranks=tuple(p * self.dp * self.tp + d * self.tp + t for d in range(self.dp)))
+
+    def all_reduce(self, tensor, op=None, group=None, **_):
+        me = self.local.coord
+        if group.kind == "dp":
+            self.dp_calls.append(me)
+            raise AssertionError("gradient-norm terms were reduced over data parallelism")
+        self.log.append((me, group.kind))
+        group.slots[me] = tensor.clone()
+        group.barrier.wait()
+        total = sum(group.slots[m] for m in group.members)
+        group.barrier.wait()
+        tensor.copy_(total)
+
+    def run(self, fn):
+        """``fn(p, t, ctx)`` on every virtual rank at once; results by coordinate."""
+        results, errors = {}, []
+
+        def body(p, t):
+            self.local.coord = (p, t)
+            try:
+                results[p, t] = fn(p, t, self.context(p, t))
+            except BaseException as exc:  # noqa: BLE001 - reported below
+                errors.append(exc)
+                for g in (self.tp_groups[p], self.pp_groups[t]):
+                    g.barrier.abort()
+
+        threads = [threading.Thread(target=body, args=(p, t))
+                   for p in range(self.pp) for t in range(self.tp)]
+        for th in threads:
+            th.start()
+        for th in threads:
+            th.join(timeout=30)
+        if errors:
+            raise errors[0]
+        return results
 
 
-@contextlib.contextmanager
-def fake_groups(*, tp_size, pp_size, pp_rank, tp_peer=0.0, pp_peer=0.0):
-    tp_group, pp_group, dp_group = object(), object(), object()
-    calls = []
-    ctx = ParallelContext(rank=pp_rank * tp_size, world_size=tp_size * pp_size * 2,
-                          tp_size=tp_size, tp_rank=0, pp_size=pp_size, pp_rank=pp_rank,
-                          dp_size=2, dp_rank=0, tp_group=tp_group, pp_group=pp_group,
-                          dp_group=dp_group, tp_ranks=tuple(range(tp_size)),
-                          pp_ranks=tuple(i * tp_size for i in range(pp_size)), dp_ranks=(0, tp_size))
+@contextmanager
+def simulated(world):
     original = grads.dist.all_reduce
-
-    def fake(tensor, group=None, **_):
-        if group is tp_group:
-            calls.append("tp")
-            tensor.add_(tp_peer)
-        elif group is pp_group:
-            calls.append("pp")
-            tensor.add_(pp_peer)
-        elif group is dp_group:
-            raise AssertionError("the gradient norm must never be reduced over DP")
-        else:
-            raise AssertionError("unexpected group")
-
-    grads.dist.all_reduce = fake
+    grads.dist.all_reduce = world.all_reduce
     try:
-        yield calls, ctx
+        yield world
     finally:
         grads.dist.all_reduce = original
 
 
-def test_tp_pp_dp_tied_norm_and_scaling():
-    local = {(0, 0): 16.0, (0, 1): 23.0, (1, 0): 43.0, (1, 1): 162.0}
-    stage = {0: 39.0, 1: 205.0}
-    expected = torch.tensor(244.0, dtype=torch.float64).sqrt()
-    max_norm = expected.item() / 2
-    scale = max_norm / (expected.item() + 1e-6)
-    for pp_rank in (0, 1):
-        for tp_rank in (0, 1):
-            model = _Stage(pp_rank, tp_rank)
-            before = {n: p.grad.clone() for n, p in model.named_parameters()}
-            with fake_groups(tp_size=2, pp_size=2, pp_rank=pp_rank,
-                             tp_peer=local[pp_rank, 1 - tp_rank], pp_peer=stage[1 - pp_rank]) as (calls, ctx):
-                norm = grads.clip_grad_norm(model, ctx, max_norm, tie_embeddings=True)
-            assert calls == ["tp", "pp"]
-            torch.testing.assert_close(norm, expected, **TOL)
-            for n, p in model.named_parameters():
-                torch.testing.assert_close(p.grad, before[n] * scale, **TOL)
+class _Param(nn.Module):
+    def __init__(self, grad, sharded):
+        super().__init__()
+        self.weight = nn.Parameter(torch.zeros_like(grad))
+        self.weight.grad = grad.clone()
+        self.weight.tensor_parallel_sharded = sharded
 
 
-def test_tied_lm_head_counted_only_when_tied():
-    model = nn.Module()
-    model.lm_head = _W([3.0], True)
-    with fake_groups(tp_size=1, pp_size=2, pp_rank=1, pp_peer=16.0) as (_, ctx):
-        n = grads.clip_grad_norm(model, ctx, 100.0, tie_embeddings=False)
-    torch.testing.assert_close(n, torch.tensor(5.0, dtype=torch.float64), **TOL)
-    model.lm_head.weight.grad.fill_(3.0)
-    with fake_groups(tp_size=1, pp_size=2, pp_rank=1, pp_peer=16.0) as (_, ctx):
-        n = grads.clip_grad_norm(model, ctx, 100.0, tie_embeddings=True)
-    torch.testing.assert_close(n, torch.tensor(4.0, dtype=torch.float64), **TOL)
+def _logical(pp, tp, seed=7):
+    """Unsharded logical gradients of a stage stack with tied embedding / LM head."""
+    g = torch.Generator().manual_seed(seed)
+    return {
+        "attn": [torch.randn(6, 4 * tp, generator=g) for _ in range(pp)],  # column-sharded per stage
+        "norm": [torch.randn(6, generator=g) for _ in range(pp)],          # replicated per stage
+        "embedding": torch.randn(8 * tp, 6, generator=g),                  # vocab-sharded, tied
+    }
 
 
-def test_limits_and_empty_gradients():
-    model = nn.Module()
-    model.weight = nn.Parameter(torch.zeros(2))
-    model.weight.grad = torch.tensor([3.0, 4.0])
-    with fake_groups(tp_size=1, pp_size=1, pp_rank=0) as (_, ctx):
-        assert grads.clip_grad_norm(model, ctx, 100.0).item() == 5.0
-    assert torch.equal(model.weight.grad, torch.tensor([3.0, 4.0]))
-    with fake_groups(tp_size=1, pp_size=1, pp_rank=0) as (_, ctx):
-        assert grads.clip_grad_norm(model, ctx, 0.0).item() == 5.0
-    assert torch.equal(model.weight.grad, torch.zeros(2))
-    model.weight.grad = None
-    with fake_groups(tp_size=1, pp_size=1, pp_rank=0) as (_, ctx):
-        assert grads.clip_grad_norm(model, ctx, 1.0).item() == 0.0
-    with pytest.raises(ValueError):
-        grads.clip_grad_norm(model, ParallelContext.single(), -1.0)
+def _stage(logical, p, t, tp, pp, tied):
+    m = nn.Module()
+    m.attn = _Param(logical["attn"][p][:, 4 * t: 4 * t + 4], True)
+    m.norm = _Param(logical["norm"][p], False)
+    shard = logical["embedding"][8 * t: 8 * t + 8]
+    if p == 0:
+        m.embedding = _Param(shard, True)
+    if p == pp - 1 and (pp > 1 or not tied):
+        m.lm_head = _Param(shard if tied else shard * 0.5, True)
+    return m
+
+
+def _expected_norm(logical, pp, tied):
+    sq = sum(a.double().pow(2).sum() for a in logical["attn"])
+    sq += sum(n.double().pow(2).sum() for n in logical["norm"])
+    sq += logical["embedding"].double().pow(2).sum()
+    if not tied:
+        sq += (logical["embedding"] * 0.5).double().pow(2).sum()
+    return sq.sqrt()
+
+
+@pytest.mark.parametrize("tp, pp, tied", [(2, 2, True), (4, 2, True), (2, 3, False), (1, 2, True)])
+def test_logical_norm_and_uniform_scaling(tp, pp, tied):
+    logical = _logical(pp, tp)
+    expected = _expected_norm(logical, pp, tied)
+    max_norm = float(expected) / 3
+
+    def rank_fn(p, t, ctx):
+        stage = _stage(logical, p, t, tp, pp, tied)
+        before = {n: q.grad.clone() for n, q in stage.named_parameters()}
+        norm = grads.clip_grad_norm(stage, ctx, max_norm, tie_embeddings=tied)
+        ratios = {n: q.grad / before[n] for n, q in stage.named_parameters()}
+        return norm, ratios
+
+    with simulated(ThreadWorld(tp, pp)) as world:
+        results = world.run(rank_fn)
+    coefficient = max_norm / (float(expected) + 1e-6)
+    for (norm, ratios) in results.values():
+        torch.testing.assert_close(norm, expected, rtol=1e-12, atol=0)
+        for r in ratios.values():
+            torch.testing.assert_close(r, torch.full_like(r, coefficient), rtol=1e-6, atol=0)
+    kinds = [k for _, k in world.log]
+    assert kinds.count("tp") == (tp * pp if tp > 1 else 0)
+    assert kinds.count("pp") == (tp * pp if pp > 1 else 0)
+    assert world.dp_calls == []
+
+
+def test_small_norm_leaves_gradients_alone_and_zero_limit_clears_them():
+    logical = _logical(1, 1, seed=3)
+    expected = _expected_norm(logical, 1, True)
+    for limit, factor in ((float(expected) * 10, 1.0), (0.0, 0.0)):
+        def rank_fn(p, t, ctx):
+            stage = _stage(logical, p, t, 1, 1, True)
+            before = [q.grad.clone() for q in stage.parameters()]
+            norm = grads.clip_grad_norm(stage, ctx, limit, tie_embeddings=True)
+            return norm, [(q.grad, b * factor) for q, b in zip(stage.parameters(), before)]
+        with simulated(ThreadWorld(1, 1)) as world:
+            (norm, pairs), = world.run(rank_fn).values()
+        torch.testing.assert_close(norm, expected)
+        for got, want in pairs:
+            assert torch.equal(got, want)
+
+
+def test_parameters_without_gradients_and_negative_limit():
+    m = nn.Module()
+    m.weight = nn.Parameter(torch.ones(3))
+    assert grads.clip_grad_norm(m, ParallelContext.single(), 1.0).item() == 0.0
+    with pytest.raises(ValueError, match="non-negative"):
+        grads.clip_grad_norm(m, ParallelContext.single(), -0.5)
 
 
 def test_flat_buffer_model_clip_matches_torch():
