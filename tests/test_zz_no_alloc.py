@@ -1,7 +1,9 @@
 """The allocation-free RMSNorm backward C entry point, called through its
 exported C symbol the way a caller that cannot allocate device memory would
-(ctypes, raw device pointers, a raw stream handle), checked against the
-framework's regular RMSNorm backward on two calls in a row.
+(ctypes, raw device pointers, a raw stream handle): checked against the
+framework's regular RMSNorm backward on two calls in a row, checked to leave
+the device's free memory and torch's allocator counters unchanged, and
+checked to refuse rows wider than its kernel or larger than its scratch array.
 
 This file is named so that pytest collects it last."""
 
@@ -29,6 +31,8 @@ def _lib():
     lib.nmb_noalloc_error_string.restype = ctypes.c_char_p
     lib.nmb_noalloc_error_string.argtypes = [ctypes.c_int]
     lib.nmb_rmsnorm_bwd_noalloc_scratch_floats.restype = ctypes.c_long
+    lib.nmb_rmsnorm_bwd_noalloc_max_cols.restype = ctypes.c_int
+    lib.nmb_noalloc_prepare.restype = ctypes.c_int
     return lib
 
 
@@ -40,6 +44,7 @@ def _rel(a, b):
 def test_noalloc_matches_regular_entry_point_twice(dtype, rows, cols):
     lib = _lib()
     torch.cuda.set_device(DEV)
+    assert lib.nmb_noalloc_prepare() == 0
     stream = torch.cuda.current_stream(DEV).cuda_stream
     tol = 1e-2 if dtype == torch.bfloat16 else 1e-5
     w = torch.rand(cols, device=DEV) + 0.5
@@ -75,3 +80,50 @@ def test_noalloc_rejects_sizes_beyond_the_scratch_array():
                                        torch.cuda.current_stream(DEV).cuda_stream)
     assert code == 1
     assert b"scratch" in lib.nmb_noalloc_error_string(code)
+
+
+def test_noalloc_call_allocates_nothing():
+    lib = _lib()
+    torch.cuda.set_device(DEV)
+    assert lib.nmb_noalloc_prepare() == 0
+    rows, cols = 2048, 4096
+    x = torch.randn(rows, cols, device=DEV).to(torch.bfloat16)
+    dy = torch.randn(rows, cols, device=DEV).to(torch.bfloat16)
+    w = torch.rand(cols, device=DEV) + 0.5
+    _, rstd = KC.rmsnorm(x, w, 1e-6)
+    dx = torch.empty_like(x)
+    dw = torch.zeros(cols, device=DEV)
+    stream = torch.cuda.current_stream(DEV).cuda_stream
+
+    def call():
+        return lib.nmb_rmsnorm_bwd_noalloc(dy.data_ptr(), x.data_ptr(), w.data_ptr(), rstd.data_ptr(),
+                                           dx.data_ptr(), dw.data_ptr(), rows, cols, 1, stream)
+
+    assert call() == 0  # warm-up: module and symbol already resolved by prepare
+    torch.cuda.synchronize(DEV)
+    free_before, _ = torch.cuda.mem_get_info(DEV)
+    stats_before = torch.cuda.memory_stats(DEV)
+    for _ in range(3):
+        assert call() == 0
+    torch.cuda.synchronize(DEV)
+    free_after, _ = torch.cuda.mem_get_info(DEV)
+    stats_after = torch.cuda.memory_stats(DEV)
+    assert free_after == free_before
+    for key in ("allocation.all.allocated", "segment.all.allocated", "reserved_bytes.all.current"):
+        assert stats_after.get(key, 0) == stats_before.get(key, 0), key
+
+
+def test_noalloc_rejects_rows_wider_than_its_kernel():
+    lib = _lib()
+    cols = lib.nmb_rmsnorm_bwd_noalloc_max_cols() + 8
+    rows = 16  # few rows: the scratch array alone would have room
+    assert _C.rmsnorm_bwd_blocks(rows) * cols <= lib.nmb_rmsnorm_bwd_noalloc_scratch_floats()
+    x = torch.zeros(rows, cols, device=DEV, dtype=torch.bfloat16)
+    w = torch.ones(cols, device=DEV)
+    rstd = torch.ones(rows, device=DEV)
+    dw = torch.zeros(cols, device=DEV)
+    code = lib.nmb_rmsnorm_bwd_noalloc(x.data_ptr(), x.data_ptr(), w.data_ptr(), rstd.data_ptr(),
+                                       x.data_ptr(), dw.data_ptr(), rows, cols, 1,
+                                       torch.cuda.current_stream(DEV).cuda_stream)
+    assert code == 2
+    assert b"8192" in lib.nmb_noalloc_error_string(code)
