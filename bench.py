@@ -53,6 +53,9 @@ def parse():
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--n-layer", type=int, default=None, help=argparse.SUPPRESS)  # debugging only
+    p.add_argument("--breakdown", default=None, metavar="FILE",
+                   help="after the timed runs, profile one more step per op class (CUDA events) "
+                        "and write the per-rank breakdown to FILE (JSON, rank 0 writes)")
     return p.parse_args()
 
 
@@ -234,6 +237,20 @@ def main():
                               f"{str(exc).splitlines()[0][:200]}"}), flush=True)
         dist.destroy_process_group()
         return
+
+    breakdown = None
+    if args.breakdown and args.impl == "ours":
+        from nano_megatron_b200.utils.op_profile import OpProfile
+        dist.barrier()
+        with OpProfile() as prof:
+            step(dev_batches[0])
+        breakdown = prof.report(step_ms=ms)
+        gathered = [None] * world
+        dist.all_gather_object(gathered, breakdown)
+        if rank == 0:
+            with open(args.breakdown, "w") as f:
+                json.dump({"step_ms_unprofiled": ms, "layout": f"tp{tp}pp{pp}",
+                           "per_rank": gathered}, f, indent=1)
 
     tokens = MICRO_BATCH * NUM_MICROBATCHES * seq * ctx.dp_size
     value = tokens / (ms / 1e3)

@@ -215,7 +215,8 @@ void dp_allreduce(const std::vector<int64_t>& bufs, const std::vector<int64_t>& 
   a.err = err.data_ptr<int>();
   a.timeout_ns = (uint64_t)(timeout_s * 1e9);
   const at::cuda::CUDAGuard guard(err.device());
-  check_ok(nmb::dp_allreduce(a, at::cuda::getCurrentCUDAStream()), "dp_allreduce");
+  const int sms = at::cuda::getCurrentDeviceProperties()->multiProcessorCount;
+  check_ok(nmb::dp_allreduce(a, sms, at::cuda::getCurrentCUDAStream()), "dp_allreduce");
 }
 
 int64_t dp_flag_bytes() { return nmb::kDpFlagInts * 4; }

@@ -8,11 +8,11 @@
 namespace nmb {
 
 constexpr int kDpMaxRanks = 8;
-constexpr int kDpMaxCtas = 64;
 // int32 offsets inside each rank's flag area
-constexpr int kDpReadyOff = 0;                                    // [kDpMaxRanks]
-constexpr int kDpDoneOff = kDpMaxRanks;                           // [kDpMaxRanks][kDpMaxCtas]
-constexpr int kDpFlagInts = kDpDoneOff + kDpMaxRanks * kDpMaxCtas;
+constexpr int kDpReadyOff = 0;                       // [kDpMaxRanks] epoch announced by each peer
+constexpr int kDpDoneOff = kDpMaxRanks;              // [kDpMaxRanks] CTAs of each peer that delivered
+constexpr int kDpFinishedOff = 2 * kDpMaxRanks;      // CTAs of this rank that finished
+constexpr int kDpFlagInts = 2 * kDpMaxRanks + 8;
 
 struct DpReduceArgs {
   float* buf[kDpMaxRanks];  // every rank's flat gradient buffer, mapped in this process
@@ -26,6 +26,8 @@ struct DpReduceArgs {
 };
 
 // buf[r][span] = scale * sum over ranks of buf[p][span], on every rank.
-cudaError_t dp_allreduce(const DpReduceArgs& args, cudaStream_t stream);
+// The grid depends only on (n, world, num_sms), so it is the same on every
+// rank of the group (the completion count relies on it).
+cudaError_t dp_allreduce(const DpReduceArgs& args, int num_sms, cudaStream_t stream);
 
 }  // namespace nmb

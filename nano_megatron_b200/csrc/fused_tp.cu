@@ -80,7 +80,7 @@ struct Cfg {
   static constexpr int STAGES = 4;
   // all-gather modes: two 4 KB output boxes (32 rows x 128 B) per epilogue warp
   static constexpr int STAGING = MODE == kReduceScatterGemm ? STAGING_BYTES : 4 * 2 * 4096;
-  static constexpr int SMEM = STAGES * STAGE_BYTES + STAGING + 1024 + 256;
+  static constexpr int SMEM = STAGES * STAGE_BYTES + STAGING + 1024 + 512;
 };
 constexpr int THREADS = 224;  // 7 warps: producer, MMA, 4 epilogue, comm
 constexpr float kLog2e = 1.4426950408889634f;
@@ -145,6 +145,24 @@ __device__ __forceinline__ int* flags_of(const FusedTpArgs& a, int rank) {
   return reinterpret_cast<int*>(a.ws[rank] + a.flags_off);
 }
 
+// Work claiming. With more than one rank, tiles and all-gather slices are
+// claimed from counters in this rank's flag area, in a fixed order, by
+// whichever CTAs are running: no rank ever waits for work that is bound to a
+// particular CTA of a peer, so the kernel finishes even when other kernels
+// (NCCL, the data-parallel reduction) hold some SMs and only part of the grid
+// is resident at a time. Each call uses the counters of its epoch's parity
+// and zeroes the other parity's, which the previous call (complete, by
+// stream order) used. A group of one assigns work statically.
+__device__ __forceinline__ int* claim_ctr(const FusedTpArgs& a, int* my_flags, int kind) {
+  return a.world > 1 ? my_flags + kClaimOff + kind + (a.epoch & 1u) : nullptr;
+}
+
+__device__ __forceinline__ int claim(int* ctr, int it) {
+  return ctr != nullptr ? atomicAdd(ctr, 1) : (int)blockIdx.x + it * (int)gridDim.x;
+}
+
+constexpr int kQueue = 4;  // tiles handed from the producer to the MMA warp and the epilogue
+
 struct TileInfo {
   int tm, tn, chunk, local;
 };
@@ -175,7 +193,11 @@ fused_tp_kernel(const __grid_constant__ CUtensorMap tmA_local, const __grid_cons
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
   uint64_t* mma_done = tempty + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
+  uint64_t* qfull = mma_done + 1;     // [kQueue] tile index published
+  uint64_t* qempty = qfull + kQueue;  // [kQueue] read by the MMA warp and the epilogue leader
+  int* tq = reinterpret_cast<int*>(qempty + kQueue);  // [kQueue] claimed tile, -1 = no more
+  volatile int* ep_tile = tq + kQueue;                // [2] tile broadcast to the epilogue warps
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(const_cast<int*>(ep_tile) + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
@@ -196,7 +218,17 @@ fused_tp_kernel(const __grid_constant__ CUtensorMap tmA_local, const __grid_cons
       mbar_init(&tempty[b], 128);
     }
     mbar_init(mma_done, 1);
+    for (int q = 0; q < kQueue; ++q) {
+      mbar_init(&qfull[q], 1);
+      mbar_init(&qempty[q], 2);
+    }
     *abort_flag = 0;
+    if (a.world > 1) {  // the previous call's counters, for the next call
+      const int other = (int)((a.epoch + 1) & 1u);
+      my_flags[kClaimOff + kClaimTiles + other] = 0;
+      my_flags[kClaimOff + kClaimPush + other] = 0;
+      my_flags[kClaimOff + kClaimSave + other] = 0;
+    }
     fence_barrier_init();
   }
   if (warp == 1) {
@@ -210,26 +242,38 @@ fused_tp_kernel(const __grid_constant__ CUtensorMap tmA_local, const __grid_cons
 
   if (warp == 6) {
     // ---------------------------------------------------------------- comm
-    if (lane == 0 && blockIdx.x == 0) {
-      for (int p = 0; p < a.world; ++p)
-        if (p != a.rank) st_release_sys(flags_of(a, p) + kReadyOff + a.rank, epoch);
-    }
+    // Every CTA announces the epoch (idempotent), so a peer never waits for a
+    // particular CTA of this rank to be scheduled.
+    if (lane < a.world && lane != a.rank) st_release_sys(flags_of(a, lane) + kReadyOff + a.rank, epoch);
     if (is_ag<MODE>()) {
-      // This CTA's slice of the local shard, in 16-byte units.
+      // The local shard is cut into S = gridDim.x slices (16-byte units). A
+      // job is one slice pushed to one destination; jobs are claimed from a
+      // counter by whichever comm warps are running, destination-major (the
+      // peer that needs chunk r soonest first, the own gather slot last), so
+      // every slice is delivered as long as one CTA of this rank is resident.
+      const int S = gridDim.x;
       const long total = (long)a.m_chunk * a.K / 8;
-      const long per = (total + gridDim.x - 1) / gridDim.x;
-      const long beg = per * blockIdx.x, end = min(total, beg + per);
+      const long per = (total + S - 1) / S;
       const uint4* src = reinterpret_cast<const uint4*>(a.a_local);
       const long chunk_off = a.gather_off + (long)a.rank * a.m_chunk * a.K * 2;
-      for (int j = 1; j <= a.world; ++j) {
-        const int p = (a.rank - j + a.world) % a.world;  // j == world -> own slot
-        if (p == a.rank && !a.copy_own) continue;
-        if (p != a.rank) {
+      const int dests = a.world - 1 + (a.copy_own ? 1 : 0);
+      int* push_ctr = claim_ctr(a, my_flags, kClaimPush);
+      uint32_t ready_seen = 0;
+      for (int it = 0;; ++it) {
+        int job = 0;
+        if (lane == 0) job = claim(push_ctr, it);
+        job = __shfl_sync(0xffffffffu, job, 0);
+        if (job >= dests * S || *abort_flag) break;
+        const int d = job / S, slice = job - d * S;
+        const int p = d < a.world - 1 ? (a.rank - 1 - d + a.world) % a.world : a.rank;
+        if (p != a.rank && !((ready_seen >> p) & 1u)) {
           bool ok = true;
           if (lane == 0) ok = wait_flag(my_flags + kReadyOff + p, epoch, a.err, a.timeout_ns, abort_flag);
           ok = __shfl_sync(0xffffffffu, ok, 0);
           if (!ok) break;
+          ready_seen |= 1u << p;
         }
+        const long beg = per * slice, end = min(total, beg + per);
         uint4* dst = reinterpret_cast<uint4*>(a.ws[p] + chunk_off);
         long i = beg + lane;
         for (; i + 31 * 8 < end; i += 32 * 8) {
@@ -243,17 +287,24 @@ fused_tp_kernel(const __grid_constant__ CUtensorMap tmA_local, const __grid_cons
         if (p != a.rank) {
           __threadfence_system();
           __syncwarp();
-          if (lane == 0) st_release_sys(flags_of(a, p) + kAgDoneOff + a.rank * kMaxCtas + blockIdx.x, epoch);
+          if (lane == 0) st_release_sys(flags_of(a, p) + kAgDoneOff + a.rank * kMaxCtas + slice, epoch);
         }
       }
       if (a.save_out != nullptr) {
+        // Private copy of the gathered input: job = (chunk in arrival order, slice).
         const long chunk_units = (long)a.m_chunk * a.K / 8;
-        for (int j = 0; j < a.world && !*abort_flag; ++j) {
+        int* save_ctr = claim_ctr(a, my_flags, kClaimSave);
+        for (int it = 0;; ++it) {
+          int job = 0;
+          if (lane == 0) job = claim(save_ctr, it);
+          job = __shfl_sync(0xffffffffu, job, 0);
+          if (job >= a.world * S || *abort_flag) break;
+          const int j = job / S, slice = job - j * S;
           const int c = (a.rank + j) % a.world;  // own chunk first, then in arrival order
           const uint4* from = src;
           if (c != a.rank) {
             bool ok = true;
-            if (lane == 0) ok = wait_flag(my_flags + kAgDoneOff + c * kMaxCtas + blockIdx.x, epoch, a.err,
+            if (lane == 0) ok = wait_flag(my_flags + kAgDoneOff + c * kMaxCtas + slice, epoch, a.err,
                                           a.timeout_ns, abort_flag);
             ok = __shfl_sync(0xffffffffu, ok, 0);
             __syncwarp();
@@ -261,6 +312,7 @@ fused_tp_kernel(const __grid_constant__ CUtensorMap tmA_local, const __grid_cons
             from = reinterpret_cast<const uint4*>(a.ws[a.rank] + a.gather_off) + c * chunk_units;
           }
           uint4* to = reinterpret_cast<uint4*>(a.save_out) + c * chunk_units;
+          const long beg = per * slice, end = min(total, beg + per);
           long i = beg + lane;
           for (; i + 31 * 8 < end; i += 32 * 8) {
             uint4 v[8];
@@ -283,7 +335,15 @@ fused_tp_kernel(const __grid_constant__ CUtensorMap tmA_local, const __grid_cons
     int issued[STAGES];  // parity of the last load issued into each stage, -1 if none
 #pragma unroll
     for (int s = 0; s < STAGES; ++s) issued[s] = -1;
-    for (int t = blockIdx.x; t < num_tiles && !*abort_flag; t += gridDim.x) {
+    int* tile_ctr = claim_ctr(a, my_flags, kClaimTiles);
+    for (int it = 0;; ++it) {
+      const int slot = it & (kQueue - 1);
+      if (!mbar_wait_abortable(&qempty[slot], ((uint32_t)(it / kQueue) & 1u) ^ 1u, a.err, abort_flag)) break;
+      int t = *abort_flag ? -1 : claim(tile_ctr, it);
+      if (t >= num_tiles) t = -1;
+      tq[slot] = t;
+      mbar_arrive(&qfull[slot]);
+      if (t < 0) break;
       const TileInfo ti = tile_of<MODE>(t, a, mt_chunk, num_n);
       const bool from_gather = is_ag<MODE>() && ti.chunk != a.rank;
       if (from_gather && !((ready_mask >> ti.chunk) & 1u)) {
@@ -322,7 +382,12 @@ fused_tp_kernel(const __grid_constant__ CUtensorMap tmA_local, const __grid_cons
     uint32_t phase = 0;
     int acc = 0;
     uint32_t acc_phase = 0;
-    for (int t = blockIdx.x; t < num_tiles && !*abort_flag; t += gridDim.x) {
+    for (int it = 0;; ++it) {
+      const int slot = it & (kQueue - 1);
+      if (!mbar_wait_abortable(&qfull[slot], (uint32_t)(it / kQueue) & 1u, a.err, abort_flag)) break;
+      const int t = tq[slot];
+      mbar_arrive(&qempty[slot]);
+      if (t < 0) break;
       if (!mbar_wait_abortable(&tempty[acc], acc_phase ^ 1, a.err, abort_flag)) break;
       tc_fence_after();
       const uint32_t d_tmem = tmem_base + acc * BN;
@@ -378,8 +443,19 @@ fused_tp_kernel(const __grid_constant__ CUtensorMap tmA_local, const __grid_cons
       __syncwarp();
     };
     // Control flow here is uniform over the 128 epilogue threads (named
-    // barriers): after an abort the loop still runs to the end, skipping waits.
-    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
+    // barriers): the leader takes the next tile from the queue and hands it to
+    // all four warps; after an abort it hands out -1 and everyone leaves.
+    for (int it = 0;; ++it) {
+      if (leader) {
+        const int slot = it & (kQueue - 1);
+        int next = -1;
+        if (mbar_wait_abortable(&qfull[slot], (uint32_t)(it / kQueue) & 1u, a.err, abort_flag)) next = tq[slot];
+        mbar_arrive(&qempty[slot]);
+        ep_tile[it & 1] = next;
+      }
+      epilogue_bar();
+      const int t = ep_tile[it & 1];
+      if (t < 0) break;
       const TileInfo ti = tile_of<MODE>(t, a, mt_chunk, num_n);
       mbar_wait_abortable(&tfull[acc], acc_phase, a.err, abort_flag);
       tc_fence_after();

@@ -21,7 +21,11 @@ constexpr int kAgDoneOff = kMaxRanks;                          // [kMaxRanks][kM
 constexpr int kRsDoneOff = kAgDoneOff + kMaxRanks * kMaxCtas;  // [kMaxTiles][kMaxRanks]
 constexpr int kMaxCeBlocks = 1024;
 constexpr long kCeFlagOff = kRsDoneOff + (long)kMaxTiles * kMaxRanks;  // [kMaxRanks][kMaxCeBlocks]
-constexpr long kFlagInts = kCeFlagOff + (long)kMaxRanks * kMaxCeBlocks;
+// work-claim counters of the fused GEMM kernels, [kind][call parity]: tiles,
+// all-gather push slices, gathered-input copy slices (local atomics only)
+constexpr long kClaimOff = kCeFlagOff + (long)kMaxRanks * kMaxCeBlocks;
+constexpr int kClaimTiles = 0, kClaimPush = 2, kClaimSave = 4;
+constexpr long kFlagInts = kClaimOff + 8;
 
 struct FusedTpArgs {
   int M, N, K;          // M = rows of the full (gathered) sequence

@@ -105,11 +105,9 @@ class GradBucketer:
     stream wait for all of it.
 
     ``overlap=False`` issues each bucket on the compute stream instead (still
-    bucket by bucket, still started during backward). That is the mode for
-    models whose fused tensor-parallel kernels run during backward: those
-    kernels keep one CTA per SM resident and wait for their TP peers, and an
-    NCCL kernel running beside them on another stream could leave one of
-    their CTAs without an SM on one rank while its peers wait for it.
+    bucket by bucket, still started during backward). ``last_step`` records,
+    after :meth:`finish`, how many buckets started during the last backward
+    and how many only in :meth:`finish`.
 
     Parity: replaces ``nano_megatron/grads.py:35-54`` (one flat all-reduce
     after the whole backward, then a division by ``dp``).
@@ -151,6 +149,7 @@ class GradBucketer:
         self.overlap = overlap and self.grad.is_cuda
         self.stream = torch.cuda.Stream(device=self.grad.device) if self.overlap else None
         self.per_microbatch: list[int] | None = None
+        self.last_step = {"during_backward": 0, "in_finish": 0, "on_comm_stream": self.overlap}
         self._reset()
 
     def _reset(self) -> None:
@@ -216,6 +215,9 @@ class GradBucketer:
 
     def finish(self) -> None:
         """Start the remaining buckets (in bucket order) and wait for every bucket."""
+        early = sum(self.started)
+        self.last_step = {"during_backward": early, "in_finish": len(self.buckets) - early,
+                          "on_comm_stream": self.overlap}
         for b in range(len(self.buckets)):
             self._start(b)
         for work in self.works:

@@ -54,13 +54,12 @@ class Trainer:
             self.model = GPT(config, ctx).to(self.device)
         synchronize_model_parameters(self.model, ctx, tie_embeddings=config.tie_word_embeddings)
         self.optimizer = FusedAdamW(self.model, lr=lr)
-        # Data-parallel averaging bucket by bucket during the last backward.
-        # NCCL runs beside the compute stream only when no fused TP kernel
-        # (one resident CTA per SM, waiting for TP peers) runs in backward.
+        # Data-parallel averaging bucket by bucket during the last backward, on
+        # a communication stream beside the compute stream. The fused TP
+        # kernels and the averaging kernel claim their work dynamically, so
+        # neither needs its whole grid resident to finish.
         self.bucketer = None
         if ctx.dp_size > 1 and dp_bucket_mb > 0 and getattr(self.model, "flat_buffers", None) is not None:
-            fused_in_backward = (self.device.type == "cuda" and fused_tp and ctx.tp_size > 1
-                                 and config.activation_dtype == torch.bfloat16)
             reducer = None
             if self.device.type == "cuda":
                 # our NVLink averaging kernel over a symmetric gradient buffer
@@ -68,7 +67,7 @@ class Trainer:
                 self.dp_workspace = DPWorkspace(ctx, self.model.flat_buffers)
                 reducer = self.dp_workspace.all_reduce_avg
             self.bucketer = GradBucketer(self.model, ctx, bucket_bytes=int(dp_bucket_mb * (1 << 20)),
-                                         overlap=not fused_in_backward, reducer=reducer)
+                                         overlap=True, reducer=reducer)
             set_grad_observer(self.bucketer.observe)
 
     def to_device(self, batches):

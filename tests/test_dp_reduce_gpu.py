@@ -1,6 +1,9 @@
-"""Data-parallel averaging kernel (NVLink peer memory) on 2 GPUs against the
-plain average, span by span, and the averaged gradients of a DP=2 training
-step with it against the NCCL path. Needs at least 2 GPUs (skipped otherwise)."""
+"""Data-parallel averaging kernel (NVLink peer memory) on 2, 4 or 8 GPUs (every
+size the box has) against the plain average, span by span, bitwise repeatable;
+the averaged gradients of a data-parallel training step with it against the
+NCCL path; and, with 4 or more GPUs, a TP=2 sequence-parallel x DP step whose
+buckets run on the communication stream beside the fused TP kernels of the
+backward. Needs at least 2 GPUs (skipped otherwise)."""
 
 import os
 import socket
@@ -14,6 +17,8 @@ pytestmark = pytest.mark.gpu
 
 if not torch.cuda.is_available() or torch.cuda.device_count() < 2:  # pragma: no cover
     pytest.skip("needs 2 CUDA GPUs", allow_module_level=True)
+
+WORLDS = [w for w in (2, 4, 8) if w <= torch.cuda.device_count()]
 
 
 def _port():
@@ -46,7 +51,7 @@ def _worker(rank, world, port, q):
                 g.copy_(self.grad)
                 self.grad = g
 
-        n = 1 << 20
+        n = (1 << 22) + 64
         flat = _Flat(n)
         ws = dp_reduce.DPWorkspace(ctx, flat)
         for it in range(3):
@@ -55,12 +60,22 @@ def _worker(rank, world, port, q):
             parts = [torch.empty_like(flat.grad) for _ in range(world)]
             dist.all_gather(parts, flat.grad)
             want = sum(parts) / world
-            for start, end in [(0, 4096), (4096, 4096 + 262144), (4096 + 262144, n)]:
+            before = flat.grad.clone()
+            spans = [(0, 4096), (4096, 4096 + 262144), (4096 + 262144, n - 64), (n - 64, n)]
+            for start, end in spans:
                 ws.all_reduce_avg(start, end)
             torch.cuda.synchronize()
             err = (flat.grad - want).abs().max().item()
             if err > 1e-6:
                 failures.append(f"iteration {it}: max error {err}")
+            first = flat.grad.clone()
+            flat.grad.copy_(before)
+            dist.barrier()
+            for start, end in spans:
+                ws.all_reduce_avg(start, end)
+            torch.cuda.synchronize()
+            if not torch.equal(flat.grad, first):
+                failures.append(f"iteration {it}: not bitwise repeatable")
         KC.check_status(dev)
 
         # DP=2 training step: bucketed NVLink averaging vs one NCCL average after backward
@@ -83,20 +98,47 @@ def _worker(rank, world, port, q):
         if diff > 1e-5:
             failures.append(f"trainer step: bucketed NVLink vs NCCL gradient difference {diff}")
         KC.check_status(dev)
+
+        if world >= 4:
+            # TP=2 (fused kernels in backward) x DP: buckets on the comm stream
+            from nano_megatron_b200.ops import fused_tp
+            fused_tp.TIMEOUT_S = 10.0
+            tctx = init_parallel(tp_size=2, pp_size=1)
+            cfg = GPTConfig(vocab_size=1024, n_layer=2, n_head=4, n_embd=512, seq_len=512,
+                            ffn_hidden_size=1024, compute_dtype="bfloat16", tie_word_embeddings=False,
+                            sequence_parallel=True, init_std=0.05)
+            gen = torch.Generator().manual_seed(70 + tctx.dp_rank)
+            batches = [(torch.randint(0, 1024, (1, 512), generator=gen),
+                        torch.randint(0, 1024, (1, 512), generator=gen)) for _ in range(3)]
+            grads = {}
+            for mb in (0.0, 0.25):
+                trainer = Trainer(cfg, tctx, dev, lr=1e-3, seed=3, init_device=dev, dp_bucket_mb=mb)
+                trainer.train_step(batches)
+                torch.cuda.synchronize()
+                grads[mb] = trainer.model.flat_buffers.grad.clone()
+                if mb > 0:
+                    stats = trainer.bucketer.last_step
+                    if not stats["on_comm_stream"] or stats["during_backward"] < 2:
+                        failures.append(f"TPxDP buckets did not overlap backward: {stats}")
+            diff = ((grads[0.0] - grads[0.25]).norm() / grads[0.0].norm()).item()
+            if diff > 1e-5:
+                failures.append(f"TPxDP step: bucketed vs one average gradient difference {diff}")
+            KC.check_status(dev)
     except Exception as exc:  # report instead of hanging the peer
         failures.append(f"exception: {exc!r}")
     q.put((rank, failures))
     dist.destroy_process_group()
 
 
-def test_dp_allreduce_two_gpus():
+@pytest.mark.parametrize("world", WORLDS)
+def test_dp_allreduce(world):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
     for p in procs:
         p.start()
-    results = dict(q.get(timeout=300) for _ in procs)
+    results = dict(q.get(timeout=600) for _ in procs)
     for p in procs:
         p.join(timeout=60)
-    assert results[0] == [] and results[1] == [], results
+    assert all(results[r] == [] for r in range(world)), results

@@ -1,8 +1,19 @@
-"""Fused all-gather->GEMM, GEMM->reduce-scatter and LM-head cross-entropy kernels on 2 GPUs, against
-fp32 torch references and against the NCCL path; plus a TP=2 sequence-parallel
-GPT step with and without the fused kernels. Needs at least 2 GPUs (skipped
-otherwise). Every cross-GPU wait in the kernels is bounded; the test lowers the
-bound to 10 s so a protocol bug fails fast instead of waiting."""
+"""Fused all-gather->GEMM, GEMM->reduce-scatter and LM-head cross-entropy kernels
+on a TP group of 2, 4 or 8 GPUs (every size the box has), against fp32 torch
+and against the NCCL path:
+
+* shapes of the benchmark configurations, including the ragged widths of the
+  1.3B shape at TP 8 (SwiGLU width 5632 / 8 = 704, vocabulary 32000 / 8 = 4000);
+* two identical calls give bitwise-identical results (the reductions have a
+  fixed order, whatever CTA claims which tile);
+* the kernels finish while NCCL kernels hold SMs beside them and wait for work
+  queued behind a peer's fused kernel (each rank's grid is only partly
+  resident, so work bound to a particular peer CTA would stall until the
+  bound);
+* a TP sequence-parallel GPT step with and without the fused kernels.
+
+Every cross-GPU wait in the kernels is bounded; the tests lower the bound to
+5 s, so a protocol bug fails fast with an error instead of waiting."""
 
 import os
 import socket
@@ -17,6 +28,8 @@ pytestmark = pytest.mark.gpu
 if not torch.cuda.is_available() or torch.cuda.device_count() < 2:  # pragma: no cover
     pytest.skip("needs 2 CUDA GPUs", allow_module_level=True)
 
+WORLDS = [w for w in (2, 4, 8) if w <= torch.cuda.device_count()]
+
 
 def _rel(a, b):
     return ((a.float() - b.float()).norm() / b.float().norm().clamp_min(1e-12)).item()
@@ -28,6 +41,138 @@ def _port():
         return s.getsockname()[1]
 
 
+def _check_gemms(rank, world, pctx, fused_tp, full, failures):
+    shapes = [(256, 512, 768), (128, 256, 392), (128, 2048, 2 * 704), (128, 704, 2048)]
+    for it in range(2):
+        for (mc, k, n) in shapes:
+            rows = mc * world
+            x = full(1 + it, rows, k)
+            w = full(2 + it, k, n)
+            wt = w.t().contiguous()
+            shard = x[rank * mc:(rank + 1) * mc]
+            y = fused_tp.all_gather_matmul(shard, w, pctx)
+            ref = x.float() @ w.float()
+            if _rel(y, ref) > 5e-3:
+                failures.append(f"ag_gemm {mc},{k},{n}: {_rel(y, ref)}")
+            g, y2 = fused_tp.all_gather_matmul(shard, wt, pctx, transpose_b=True, return_gathered=True)
+            if not torch.equal(g, x):
+                failures.append(f"gathered copy differs {mc},{k},{n}")
+            if not torch.equal(y2, y) and _rel(y2, ref) > 5e-3:
+                failures.append(f"ag_gemm^T {_rel(y2, ref)}")
+            a_parts = [full(100 + r + it, rows, k) for r in range(world)]
+            out = fused_tp.matmul_reduce_scatter(a_parts[rank], w, pctx)
+            ref = sum(p.float() @ w.float() for p in a_parts)[rank * mc:(rank + 1) * mc]
+            if _rel(out, ref) > 1e-2:
+                failures.append(f"gemm_rs {mc},{k},{n}: {_rel(out, ref)}")
+            out2 = fused_tp.matmul_reduce_scatter(a_parts[rank], wt, pctx, transpose_b=True)
+            if _rel(out2, ref) > 1e-2:
+                failures.append(f"gemm_rs^T {_rel(out2, ref)}")
+            xs, y3 = fused_tp.all_gather_matmul(shard, w, pctx, save_gathered=True)
+            if not torch.equal(xs, x):
+                failures.append(f"saved gathered copy differs {mc},{k},{n}")
+            # bitwise repeatability: same inputs, same bits
+            if not torch.equal(y3, y):
+                failures.append(f"ag_gemm not repeatable {mc},{k},{n}")
+            again = fused_tp.matmul_reduce_scatter(a_parts[rank], w, pctx)
+            if not torch.equal(again, out):
+                failures.append(f"gemm_rs not repeatable {mc},{k},{n}")
+
+
+def _check_ce(rank, world, pctx, fused_tp, full, dev, failures):
+    for it, (rows, hidden, vocab_local) in enumerate([(512, 256, 1040), (1024, 256, 4000)]):
+        vocab = vocab_local * world
+        xf = full(300 + it, rows, hidden)
+        wf = (full(400 + it, vocab, hidden).float() * 0.1).bfloat16()
+        gen = torch.Generator(device=dev).manual_seed(500 + it)
+        labels = torch.randint(0, vocab, (rows,), generator=gen, device=dev)
+        lf = xf.float() @ wf.float().t()
+        ref = torch.logsumexp(lf, dim=1) - lf.gather(1, labels[:, None])[:, 0]
+        wl = wf[rank * vocab_local:(rank + 1) * vocab_local]
+        for gather in (True, False):
+            xin = xf[rank * (rows // world):(rank + 1) * (rows // world)] if gather else xf
+            results = [fused_tp.lm_head_cross_entropy(xin, wl, labels, rank * vocab_local,
+                                                      (rank + 1) * vocab_local, pctx, gather=gather)
+                       for _ in range(2)]
+            loss, logits, gm, gs, X = results[0]
+            if (loss - ref).abs().max().item() > 3e-2:
+                failures.append(f"fused ce V/t={vocab_local} gather={gather}: {(loss - ref).abs().max().item()}")
+            if not torch.equal(X, xf):
+                failures.append(f"fused ce gathered input gather={gather}")
+            lse = torch.logsumexp(lf, dim=1)
+            if (gm + gs.log() - lse).abs().max().item() > 3e-2:
+                failures.append("fused ce global lse")
+            if not all(torch.equal(u, v) for u, v in zip(results[0][:4], results[1][:4])):
+                failures.append(f"fused ce not repeatable V/t={vocab_local}")
+
+
+def _check_beside_waiting_nccl(rank, world, pctx, fused_tp, full, dev, failures):
+    """Rank parity decides which of two NCCL groups runs on a side stream before
+    the fused kernel and which runs on the compute stream after it: every side
+    kernel waits for peers whose matching call is queued behind their fused
+    kernel, holding SMs meanwhile."""
+    g1 = dist.new_group(list(range(world)))
+    g2 = dist.new_group(list(range(world)))
+    warm = torch.ones(1024, device=dev)
+    dist.all_reduce(warm, group=g1)
+    dist.all_reduce(warm, group=g2)
+    torch.cuda.synchronize()
+    side_group, later_group = (g1, g2) if rank % 2 == 0 else (g2, g1)
+    side = torch.cuda.Stream(device=dev)
+    mc, k, n = 1024, 4096, 4096
+    rows = mc * world
+    x = full(7, rows, k)
+    w = full(8, k, n)
+    a_parts = [full(900 + r, rows, k) for r in range(world)]
+    want_ag = x.float() @ w.float()
+    want_rs = sum(p.float() @ w.float() for p in a_parts)[rank * mc:(rank + 1) * mc]
+    for trial in range(3):
+        big_side = torch.ones(64 << 20, device=dev)
+        big_later = torch.ones(64 << 20, device=dev)
+        torch.cuda.synchronize()
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            dist.all_reduce(big_side, group=side_group)
+        if trial % 2 == 0:
+            out = fused_tp.matmul_reduce_scatter(a_parts[rank], w, pctx)
+            xs, y = fused_tp.all_gather_matmul(x[rank * mc:(rank + 1) * mc], w, pctx, save_gathered=True)
+        else:
+            xs, y = fused_tp.all_gather_matmul(x[rank * mc:(rank + 1) * mc], w, pctx, save_gathered=True)
+            out = fused_tp.matmul_reduce_scatter(a_parts[rank], w, pctx)
+        dist.all_reduce(big_later, group=later_group)
+        torch.cuda.synchronize()
+        if _rel(y, want_ag) > 5e-3 or not torch.equal(xs, x):
+            failures.append(f"ag beside waiting NCCL, trial {trial}: {_rel(y, want_ag)}")
+        if _rel(out, want_rs) > 1e-2:
+            failures.append(f"rs beside waiting NCCL, trial {trial}: {_rel(out, want_rs)}")
+        if big_side[0].item() != world or big_later[0].item() != world:
+            failures.append("NCCL results wrong")
+
+
+def _check_model_step(rank, world, pctx, dev, failures):
+    from nano_megatron_b200 import GPT, GPTConfig
+    seq = 256 * world  # 256 rows per rank: the fused path
+    cfg = GPTConfig(vocab_size=128 * world, n_layer=2, n_head=world, n_embd=128 * world, seq_len=seq,
+                    ffn_hidden_size=256 * world, compute_dtype="bfloat16", sequence_parallel=True,
+                    tie_word_embeddings=False, init_std=0.05)
+    torch.manual_seed(rank)
+    model = GPT(cfg, pctx, device=dev)
+    x = torch.randint(0, cfg.vocab_size, (1, seq), generator=torch.Generator().manual_seed(5)).to(dev)
+    t = torch.randint(0, cfg.vocab_size, (1, seq), generator=torch.Generator().manual_seed(6)).to(dev)
+    grads, losses = {}, {}
+    for fused in (False, True):
+        pctx.resources["fused_tp"] = fused
+        model.zero_grad()
+        loss = model(x, t)
+        loss.backward()
+        losses[fused] = loss.item()
+        grads[fused] = [p.grad.clone() for p in model.parameters()]
+    if abs(losses[True] - losses[False]) > 1e-2 * abs(losses[False]):
+        failures.append(f"model loss fused {losses[True]} vs nccl {losses[False]}")
+    for (name, _), gf, gn in zip(model.named_parameters(), grads[True], grads[False]):
+        if _rel(gf, gn) > 3e-2:
+            failures.append(f"model grad {name}: {_rel(gf, gn)}")
+
+
 def _worker(rank, world, port, q):
     os.environ["NCCL_NVLS_ENABLE"] = "0"
     torch.cuda.set_device(rank)
@@ -36,116 +181,41 @@ def _worker(rank, world, port, q):
     dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
                             timeout=timedelta(seconds=60), device_id=dev)
     failures = []
+    stage = "setup"
     try:
         from nano_megatron_b200.ops import cuda as KC
         from nano_megatron_b200.ops import fused_tp
         from nano_megatron_b200.parallel import init_parallel
-        fused_tp.TIMEOUT_S = 10.0
+        fused_tp.TIMEOUT_S = 5.0
         pctx = init_parallel(tp_size=world)
 
         def full(seed, *shape):
             g = torch.Generator(device=dev).manual_seed(seed)
             return torch.randn(*shape, generator=g, device=dev).bfloat16()
 
-        for it in range(3):
-            for (mc, k, n) in [(256, 512, 768), (128, 256, 392)]:
-                rows = mc * world
-                x = full(1 + it, rows, k)
-                w = full(2 + it, k, n)
-                wt = w.t().contiguous()
-                # all-gather -> GEMM, both B layouts, with the gathered copy
-                y = fused_tp.all_gather_matmul(x[rank * mc:(rank + 1) * mc], w, pctx)
-                ref = x.float() @ w.float()
-                if _rel(y, ref) > 5e-3:
-                    failures.append(f"ag_gemm {mc},{k},{n}: {_rel(y, ref)}")
-                g, y2 = fused_tp.all_gather_matmul(x[rank * mc:(rank + 1) * mc], wt, pctx, transpose_b=True,
-                                                   return_gathered=True)
-                if not torch.equal(g, x):
-                    failures.append("gathered copy differs")
-                if _rel(y2, ref) > 5e-3:
-                    failures.append(f"ag_gemm^T {_rel(y2, ref)}")
-                # GEMM -> reduce-scatter: every rank has its own partial A
-                a_parts = [full(100 + r + it, rows, k) for r in range(world)]
-                out = fused_tp.matmul_reduce_scatter(a_parts[rank], w, pctx)
-                ref = sum(p.float() @ w.float() for p in a_parts)[rank * mc:(rank + 1) * mc]
-                if _rel(out, ref) > 1e-2:
-                    failures.append(f"gemm_rs {mc},{k},{n}: {_rel(out, ref)}")
-                out2 = fused_tp.matmul_reduce_scatter(a_parts[rank], wt, pctx, transpose_b=True)
-                if _rel(out2, ref) > 1e-2:
-                    failures.append(f"gemm_rs^T {_rel(out2, ref)}")
-                # all-gather -> GEMM with the private gathered copy
-                xs, y3 = fused_tp.all_gather_matmul(x[rank * mc:(rank + 1) * mc], w, pctx, save_gathered=True)
-                if not torch.equal(xs, x):
-                    failures.append("saved gathered copy differs")
-                if _rel(y3, x.float() @ w.float()) > 5e-3:
-                    failures.append("ag_gemm with save")
-        torch.cuda.synchronize()
-        KC.check_status(dev)
-
-        # fused vocab-parallel LM head + cross entropy (sequence-sharded input,
-        # and full input with the merge only), against torch on the full vocab
-        for it in range(3):
-            rows, hidden, vocab = 512, 256, 2 * 1040
-            vl = vocab // world
-            xf = full(300 + it, rows, hidden)
-            wf = (full(400 + it, vocab, hidden).float() * 0.1).bfloat16()
-            gen = torch.Generator(device=dev).manual_seed(500 + it)
-            labels = torch.randint(0, vocab, (rows,), generator=gen, device=dev)
-            lf = xf.float() @ wf.float().t()
-            ref = torch.logsumexp(lf, dim=1) - lf.gather(1, labels[:, None])[:, 0]
-            wl = wf[rank * vl:(rank + 1) * vl]
-            for gather in (True, False):
-                xin = xf[rank * (rows // world):(rank + 1) * (rows // world)] if gather else xf
-                loss, logits, gm, gs, X = fused_tp.lm_head_cross_entropy(
-                    xin, wl, labels, rank * vl, (rank + 1) * vl, pctx, gather=gather)
-                if (loss - ref).abs().max().item() > 3e-2:
-                    failures.append(f"fused ce gather={gather}: {(loss - ref).abs().max().item()}")
-                if not torch.equal(X, xf):
-                    failures.append(f"fused ce gathered input gather={gather}")
-                lse = torch.logsumexp(lf, dim=1)
-                if (gm + gs.log() - lse).abs().max().item() > 3e-2:
-                    failures.append("fused ce global lse")
-        torch.cuda.synchronize()
-        KC.check_status(dev)
-
-        # a TP=2 SP model step: fused kernels vs NCCL collectives, same weights
-        from nano_megatron_b200 import GPT, GPTConfig
-        cfg = GPTConfig(vocab_size=1024, n_layer=2, n_head=4, n_embd=512, seq_len=512, ffn_hidden_size=1024,
-                        compute_dtype="bfloat16", sequence_parallel=True, tie_word_embeddings=False,
-                        init_std=0.05)
-        torch.manual_seed(rank)
-        model = GPT(cfg, pctx, device=dev)
-        x = torch.randint(0, 1024, (1, 512), generator=torch.Generator().manual_seed(5)).to(dev)
-        t = torch.randint(0, 1024, (1, 512), generator=torch.Generator().manual_seed(6)).to(dev)
-        grads = {}
-        losses = {}
-        for fused in (False, True):
-            pctx.resources["fused_tp"] = fused
-            model.zero_grad()
-            loss = model(x, t)
-            loss.backward()
-            losses[fused] = loss.item()
-            grads[fused] = [p.grad.clone() for p in model.parameters()]
-        if abs(losses[True] - losses[False]) > 1e-2 * abs(losses[False]):
-            failures.append(f"model loss fused {losses[True]} vs nccl {losses[False]}")
-        for (name, _), gf, gn in zip(model.named_parameters(), grads[True], grads[False]):
-            if _rel(gf, gn) > 3e-2:
-                failures.append(f"model grad {name}: {_rel(gf, gn)}")
-        KC.check_status(dev)
+        for stage, check in [("gemms", lambda: _check_gemms(rank, world, pctx, fused_tp, full, failures)),
+                             ("ce", lambda: _check_ce(rank, world, pctx, fused_tp, full, dev, failures)),
+                             ("nccl", lambda: _check_beside_waiting_nccl(rank, world, pctx, fused_tp, full, dev,
+                                                                         failures)),
+                             ("model", lambda: _check_model_step(rank, world, pctx, dev, failures))]:
+            check()
+            torch.cuda.synchronize()
+            KC.check_status(dev)
     except Exception as exc:  # report instead of hanging the peer
-        failures.append(f"exception: {exc!r}")
+        failures.append(f"exception in {stage}: {exc!r}")
     q.put((rank, failures))
     dist.destroy_process_group()
 
 
-def test_fused_tp_two_gpus():
+@pytest.mark.parametrize("world", WORLDS)
+def test_fused_tp(world):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
     for p in procs:
         p.start()
-    results = dict(q.get(timeout=300) for _ in procs)
+    results = dict(q.get(timeout=600) for _ in procs)
     for p in procs:
         p.join(timeout=60)
-    assert results[0] == [] and results[1] == [], results
+    assert all(results[r] == [] for r in range(world)), results
