@@ -1,18 +1,29 @@
-"""Headline benchmark: Llama-3-8B-shape GPT training throughput (tokens/s per box).
+"""Training-throughput benchmark of the named configurations (tokens/s per box).
 
     python bench.py --gpus 1 --steps K --warmup W                  # this framework
     torchrun --nproc-per-node 8 bench.py --gpus 8 --steps K --warmup W
     python bench.py --impl reference ...                           # the reference, same config
+    python bench.py --config 3 ...                                 # another named configuration
 
-Model and data (the named headline configuration): vocab 128256, hidden 4096, 32 layers,
-32 heads (head_dim 128), SwiGLU ffn 14336, RoPE theta 500000, untied
-embeddings, seq 8192, micro-batch 1, 16 microbatches of 1F1B, whole-block
-recompute, sequence parallelism, bf16 compute with fp32 master weights,
-AdamW with clip 1.0; synthetic uniform tokens, random N(0, 0.02) weights.
+``--config 5`` (the default, the headline): Llama-3-8B shape -- vocab 128256,
+hidden 4096, 32 layers, 32 heads (head_dim 128), SwiGLU ffn 14336, RoPE theta
+500000, untied embeddings, seq 8192, micro-batch 1, 16 microbatches of 1F1B,
+whole-block recompute. The model and the global batch (16 x 8192 tokens) are
+fixed for every GPU count (strong scaling); the layout grows with N:
+N=1 tp1, N=2 tp2, N=4 tp4, N=8 tp4 x pp2 (the named TP4 x PP2 + SP layout).
 
-The model and the global batch (16 x 8192 tokens) are fixed for every GPU
-count (strong scaling); the parallel layout grows with N:
-N=1 tp1, N=2 tp2, N=4 tp4, N=8 tp4 x pp2 (the named TP4 x PP2 + SP config).
+``--config 3``: 1.3B shape -- vocab 32000, hidden 2048, 24 layers, 16 heads,
+SwiGLU ffn 5632, seq 4096, micro-batch 2, 8 microbatches, tied embeddings;
+N GPUs run tp N (the named layout is tp8).
+
+``--config 4``: 3B shape -- vocab 50304, hidden 2560, 32 layers, 20 heads,
+SwiGLU ffn 6912, seq 2048, micro-batch 4, 16 microbatches per data-parallel
+replica, tied embeddings; N=1 tp1, N=2 tp2, N=4 tp2 x pp2, N=8 tp2 x pp2 x dp2
+(the named layout; the batch grows with the data-parallel width).
+
+All: sequence parallelism, bf16 compute with fp32 master weights, AdamW with
+clip 1.0; synthetic uniform tokens (a different seeded window per DP rank),
+random N(0, 0.02) weights.
 
 Timing: W untimed steps; then K steps bracketed by a barrier and
 ``torch.cuda.synchronize()`` and timed with CUDA events on the compute stream,
@@ -39,11 +50,27 @@ import torch.distributed as dist
 HERE = os.path.dirname(os.path.abspath(__file__))
 if HERE not in sys.path:
     sys.path.insert(0, HERE)
-METRIC = "tokens/sec/box (device-timed, max over ranks) @8B-shape TP4×PP2+SP; MFU"
-MODEL = dict(vocab_size=128256, n_layer=32, n_head=32, n_embd=4096, seq_len=8192,
-             ffn_hidden_size=14336, rope_theta=500000.0)
-MICRO_BATCH, NUM_MICROBATCHES = 1, 16
-LAYOUT = {1: (1, 1), 2: (2, 1), 4: (4, 1), 8: (4, 2)}  # N -> (tp, pp)
+CONFIGS = {
+    5: dict(metric="tokens/sec/box (device-timed, max over ranks) @8B-shape TP4\u00d7PP2+SP; MFU",
+            label="llama3-8b-shape (V128256 H4096 L{L} A32 F14336 theta5e5 untied)",
+            model=dict(vocab_size=128256, n_layer=32, n_head=32, n_embd=4096, seq_len=8192,
+                       ffn_hidden_size=14336, rope_theta=500000.0),
+            tied=False, recompute=True, micro_batch=1, num_microbatches=16, scaling="strong",
+            layout={1: (1, 1), 2: (2, 1), 4: (4, 1), 8: (4, 2)}),
+    3: dict(metric="tokens/sec/box (device-timed, max over ranks) @1.3B-shape TP8+SP; MFU",
+            label="1.3b-shape (V32000 H2048 L{L} A16 F5632 tied)",
+            model=dict(vocab_size=32000, n_layer=24, n_head=16, n_embd=2048, seq_len=4096,
+                       ffn_hidden_size=5632, rope_theta=10000.0),
+            tied=True, recompute=False, micro_batch=2, num_microbatches=8, scaling="strong",
+            layout={1: (1, 1), 2: (2, 1), 4: (4, 1), 8: (8, 1)}),
+    4: dict(metric="tokens/sec/box (device-timed, max over ranks) @3B-shape TP2\u00d7PP2\u00d7DP2+SP tied; MFU",
+            label="3b-shape (V50304 H2560 L{L} A20 F6912 tied)",
+            model=dict(vocab_size=50304, n_layer=32, n_head=20, n_embd=2560, seq_len=2048,
+                       ffn_hidden_size=6912, rope_theta=10000.0),
+            tied=True, recompute=False, micro_batch=4, num_microbatches=16, scaling="weak in data parallel",
+            layout={1: (1, 1), 2: (2, 1), 4: (2, 2), 8: (2, 2)}),
+}
+CFG = CONFIGS[5]
 
 
 def parse():
@@ -52,6 +79,8 @@ def parse():
     p.add_argument("--steps", type=int, default=3)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--config", type=int, choices=sorted(CONFIGS), default=5,
+                   help="named configuration (5: the headline)")
     p.add_argument("--n-layer", type=int, default=None, help=argparse.SUPPRESS)  # debugging only
     p.add_argument("--breakdown", default=None, metavar="FILE",
                    help="after the timed runs, profile one more step per op class (CUDA events) "
@@ -92,9 +121,9 @@ def max_over_ranks(x: float, device) -> float:
 def make_batches(vocab, seq, step, dp_rank, pin=False):
     gen = torch.Generator().manual_seed(1234 + 100_003 * step + dp_rank)
     out = []
-    for _ in range(NUM_MICROBATCHES):
-        x = torch.randint(0, vocab, (MICRO_BATCH, seq), generator=gen)
-        y = torch.randint(0, vocab, (MICRO_BATCH, seq), generator=gen)
+    for _ in range(CFG["num_microbatches"]):
+        x = torch.randint(0, vocab, (CFG["micro_batch"], seq), generator=gen)
+        y = torch.randint(0, vocab, (CFG["micro_batch"], seq), generator=gen)
         out.append((x.pin_memory(), y.pin_memory()) if pin else (x, y))
     return out
 
@@ -105,8 +134,8 @@ def build_ours(tp, pp, device, n_layer):
     from nano_megatron_b200.parallel import init_parallel
     from nano_megatron_b200.train import Trainer
     ctx = init_parallel(tp_size=tp, pp_size=pp)
-    cfg = GPTConfig(**{**MODEL, "n_layer": n_layer}, tie_word_embeddings=False,
-                    sequence_parallel=True, recompute=True, compute_dtype="bfloat16")
+    cfg = GPTConfig(**{**CFG["model"], "n_layer": n_layer}, tie_word_embeddings=CFG["tied"],
+                    sequence_parallel=True, recompute=CFG["recompute"], compute_dtype="bfloat16")
     trainer = Trainer(cfg, ctx, device, lr=3e-4, clip=1.0, seed=0, init_device=device)
 
     def launches():
@@ -119,12 +148,14 @@ def build_ours(tp, pp, device, n_layer):
 # ------------------------------------------------------------ reference arm
 def build_reference(tp, pp, device, n_layer):
     """The unmodified reference package (baseline/_ref) driven by its own public
-    functions in the order of its ``train.py`` step loop. The benchmark shape
-    needs three settings its CLI cannot express; they are applied with its own
-    classes: SwiGLU width 14336 (its ``ParallelMLP`` hard-codes 4*H), RoPE theta
-    500000 (its ``build_rope_cache`` base argument) and untied embeddings
-    (``GPTConfig.tie_word_embeddings=False``). Parameters are created directly
-    on the GPU (default-device context) instead of on the CPU and then moved."""
+    functions in the order of its ``train.py`` step loop. The benchmark shapes
+    need settings its CLI cannot express; they are applied with its own
+    classes: the SwiGLU width (its ``ParallelMLP`` hard-codes 4*H; the MLP's
+    ``gate``/``up``/``down`` are replaced by its own ``ColumnParallelLinear`` /
+    ``RowParallelLinear`` of the configured width), RoPE theta (its
+    ``build_rope_cache`` base argument) and untied embeddings
+    (``GPTConfig.tie_word_embeddings``). Parameters are created directly on the
+    GPU (default-device context) instead of on the CPU and then moved."""
     ref = os.environ.get("NMB_REFERENCE_PATH") or os.path.join(HERE, "baseline", "_ref")
     if not os.path.isdir(os.path.join(ref, "nano_megatron")):
         raise ImportError(f"reference package not found under {ref}")
@@ -135,32 +166,39 @@ def build_reference(tp, pp, device, n_layer):
     from nano_megatron.pipeline import forward_backward_1f1b
     from nano_megatron.tp_layers import ColumnParallelLinear, RowParallelLinear
 
+    m, tied = CFG["model"], CFG["tied"]
     ctx = init_parallel(tp_size=tp, pp_size=pp)
-    cfg = GPTConfig(vocab_size=MODEL["vocab_size"], n_layer=n_layer, n_head=MODEL["n_head"],
-                    n_embd=MODEL["n_embd"], seq_len=MODEL["seq_len"], tie_word_embeddings=False,
-                    sequence_parallel=True, recompute=True, compute_dtype="bfloat16")
+    cfg = GPTConfig(vocab_size=m["vocab_size"], n_layer=n_layer, n_head=m["n_head"],
+                    n_embd=m["n_embd"], seq_len=m["seq_len"], tie_word_embeddings=tied,
+                    sequence_parallel=True, recompute=CFG["recompute"], compute_dtype="bfloat16")
     torch.manual_seed(tp * ctx.pp_rank + ctx.tp_rank)
     with torch.device(device):
         model = GPT(cfg, ctx)
-        for layer in model.layers:
-            mlp = layer.mlp
-            mlp.gate = ColumnParallelLinear(cfg.n_embd, MODEL["ffn_hidden_size"], ctx, bias=False)
-            mlp.up = ColumnParallelLinear(cfg.n_embd, MODEL["ffn_hidden_size"], ctx, bias=False)
-            mlp.down = RowParallelLinear(MODEL["ffn_hidden_size"], cfg.n_embd, ctx, bias=False)
-        cos, sin = build_rope_cache(cfg.seq_len, cfg.head_dim, device, base=MODEL["rope_theta"])
-        model.rope_cos, model.rope_sin = cos, sin
-    synchronize_model_parameters(model, ctx, tie_embeddings=False)
+        if m["ffn_hidden_size"] != 4 * m["n_embd"]:
+            for layer in model.layers:
+                mlp = layer.mlp
+                mlp.gate = ColumnParallelLinear(cfg.n_embd, m["ffn_hidden_size"], ctx, bias=False)
+                mlp.up = ColumnParallelLinear(cfg.n_embd, m["ffn_hidden_size"], ctx, bias=False)
+                mlp.down = RowParallelLinear(m["ffn_hidden_size"], cfg.n_embd, ctx, bias=False)
+        if m["rope_theta"] != 10000.0:
+            cos, sin = build_rope_cache(cfg.seq_len, cfg.head_dim, device, base=m["rope_theta"])
+            model.rope_cos, model.rope_sin = cos, sin
+    synchronize_model_parameters(model, ctx, tie_embeddings=tied)
     opt = torch.optim.AdamW(model.parameters(), lr=3e-4)
 
     def step(batches):
         opt.zero_grad(set_to_none=True)
         batches = [(x.to(device, non_blocking=True), y.to(device, non_blocking=True)) for x, y in batches]
         losses = forward_backward_1f1b(model, batches, cfg, device, ctx)
-        finalize_gradients(model, ctx, tie_embeddings=False, sequence_parallel=True)
-        clip_grad_norm(model, ctx, 1.0, tie_embeddings=False)
+        finalize_gradients(model, ctx, tie_embeddings=tied, sequence_parallel=True)
+        clip_grad_norm(model, ctx, 1.0, tie_embeddings=tied)
         opt.step()
         if ctx.is_last_stage and ctx.tp_rank == 0:
-            return torch.stack(losses).sum()
+            loss = torch.stack(losses).sum()
+            if ctx.dp_size > 1:
+                dist.all_reduce(loss, group=ctx.dp_group)
+                loss /= ctx.dp_size
+            return loss
         return None
 
     return ctx, step, lambda: 0
@@ -168,15 +206,17 @@ def build_reference(tp, pp, device, n_layer):
 
 # ------------------------------------------------------------------- driver
 def main():
+    global CFG
     args = parse()
+    CFG = CONFIGS[args.config]
     n = args.gpus
-    if n not in LAYOUT:
-        raise SystemExit(f"--gpus must be one of {sorted(LAYOUT)}")
-    tp, pp = LAYOUT[n]
+    if n not in CFG["layout"]:
+        raise SystemExit(f"--gpus must be one of {sorted(CFG['layout'])}")
+    tp, pp = CFG["layout"][n]
     rank, world, device = setup_dist(n)
     if world != n:
         raise SystemExit(f"world size {world} != --gpus {n}")
-    n_layer = args.n_layer or MODEL["n_layer"]
+    n_layer = args.n_layer or CFG["model"]["n_layer"]
     local0 = int(os.environ.get("LOCAL_RANK", 0)) == 0
     try:
         build = build_ours if args.impl == "ours" else build_reference
@@ -187,7 +227,7 @@ def main():
         dist.destroy_process_group()
         return
 
-    vocab, seq = MODEL["vocab_size"], MODEL["seq_len"]
+    vocab, seq = CFG["model"]["vocab_size"], CFG["model"]["seq_len"]
     dev_batches = [[(x.to(device), y.to(device)) for x, y in make_batches(vocab, seq, s, ctx.dp_rank)]
                    for s in range(2)]
     from nano_megatron_b200.utils.timing import ClockSampler
@@ -252,23 +292,27 @@ def main():
                 json.dump({"step_ms_unprofiled": ms, "layout": f"tp{tp}pp{pp}",
                            "per_rank": gathered}, f, indent=1)
 
-    tokens = MICRO_BATCH * NUM_MICROBATCHES * seq * ctx.dp_size
+    tokens = CFG["micro_batch"] * CFG["num_microbatches"] * seq * ctx.dp_size
     value = tokens / (ms / 1e3)
     peaks = measured_peaks()
     from nano_megatron_b200.models import GPTConfig
-    flops_tok = GPTConfig(**{**MODEL, "n_layer": n_layer}, tie_word_embeddings=False).flops_per_token()
+    flops_tok = GPTConfig(**{**CFG["model"], "n_layer": n_layer},
+                          tie_word_embeddings=CFG["tied"]).flops_per_token()
     mfu = value * flops_tok / (n * peaks.get("bf16_tflops_sustained", 1400.0) * 1e12)
     if rank == 0:
         clocks = sampler.summary() if sampler else {}
         line = {
-            "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": n,
+            "metric": CFG["metric"], "value": round(value, 1), "unit": "tokens/s", "n_gpus": n,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 2),
-            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-            "dtype": "bf16", "data": "synthetic uniform tokens in [0,128256), random-init N(0,0.02) weights",
-            "config": {"model": "llama3-8b-shape (V128256 H4096 L%d A32 F14336 theta5e5 untied)" % n_layer,
-                       "global_batch": MICRO_BATCH * NUM_MICROBATCHES * ctx.dp_size, "seq_len": seq,
-                       "micro_batch": MICRO_BATCH, "num_microbatches": NUM_MICROBATCHES,
-                       "parallelism": f"tp{tp}pp{pp}dp{ctx.dp_size}+sp+recompute",
+            "higher_is_better": True, "scaling": CFG["scaling"], "vs_baseline": None,
+            "dtype": "bf16",
+            "data": f"synthetic uniform tokens in [0,{vocab}), random-init N(0,0.02) weights",
+            "config": {"name": f"config {args.config}", "model": CFG["label"].format(L=n_layer),
+                       "global_batch": CFG["micro_batch"] * CFG["num_microbatches"] * ctx.dp_size,
+                       "seq_len": seq, "micro_batch": CFG["micro_batch"],
+                       "num_microbatches": CFG["num_microbatches"],
+                       "parallelism": f"tp{tp}pp{pp}dp{ctx.dp_size}+sp"
+                                      + ("+recompute" if CFG["recompute"] else ""),
                        "l2": "no flush: per-step working set (weights, activations) >> 126 MB L2"},
             "mfu": round(mfu, 4),
             "mfu_denominator": ("bf16_tflops_sustained of measured" if not peaks.get("fallback")

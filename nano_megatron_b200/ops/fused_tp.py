@@ -67,14 +67,17 @@ class TPWorkspace:
         recv_bytes = max(_round(recv_bytes), self.recv_bytes)
         ce_bytes = max(_round(ce_bytes), self.ce_bytes)
         if self.buf is not None:
-            # Every rank's kernels on the old buffer must be finished before it goes.
-            torch.cuda.synchronize(self.device)
+            # Every rank's kernels on the old buffer must be finished before it
+            # goes. They all ran on this stream; a device-wide synchronize would
+            # also wait for other streams' work (e.g. an NCCL kernel waiting for
+            # a peer that is itself here), so only this stream is drained.
+            torch.cuda.current_stream(self.device).synchronize()
             dist.barrier(group=self.pctx.tp_group)
         total = self.flag_bytes + gather_bytes + recv_bytes + ce_bytes
         buf = symm.empty(total, dtype=torch.uint8, device=self.device)
         buf.zero_()
         handle = symm.rendezvous(buf, self.pctx.tp_group)
-        torch.cuda.synchronize(self.device)
+        torch.cuda.current_stream(self.device).synchronize()
         dist.barrier(group=self.pctx.tp_group)
         self.buf, self.handle = buf, handle
         self.ptrs = [int(p) for p in handle.buffer_ptrs]

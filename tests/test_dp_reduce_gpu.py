@@ -132,13 +132,6 @@ def _worker(rank, world, port, q):
 
 @pytest.mark.parametrize("world", WORLDS)
 def test_dp_allreduce(world):
-    ctx = mp.get_context("spawn")
-    q = ctx.Queue()
-    port = _port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
-    for p in procs:
-        p.start()
-    results = dict(q.get(timeout=600) for _ in procs)
-    for p in procs:
-        p.join(timeout=60)
-    assert all(results[r] == [] for r in range(world)), results
+    from tests.test_fused_tp_gpu import run_ranks
+    results = run_ranks(_worker, world)
+    assert all(results.get(r) == [] for r in range(world)), results

@@ -125,6 +125,12 @@ def _check_beside_waiting_nccl(rank, world, pctx, fused_tp, full, dev, failures)
     a_parts = [full(900 + r, rows, k) for r in range(world)]
     want_ag = x.float() @ w.float()
     want_rs = sum(p.float() @ w.float() for p in a_parts)[rank * mc:(rank + 1) * mc]
+    # size the workspace for these shapes first: growing it drains the stream
+    # and meets the peers at a barrier, which must not happen while this
+    # test keeps NCCL kernels waiting on purpose
+    fused_tp.matmul_reduce_scatter(a_parts[rank], w, pctx)
+    fused_tp.all_gather_matmul(x[rank * mc:(rank + 1) * mc], w, pctx, save_gathered=True)
+    torch.cuda.synchronize()
     for trial in range(3):
         big_side = torch.ones(64 << 20, device=dev)
         big_later = torch.ones(64 << 20, device=dev)
@@ -198,24 +204,57 @@ def _worker(rank, world, port, q):
                              ("nccl", lambda: _check_beside_waiting_nccl(rank, world, pctx, fused_tp, full, dev,
                                                                          failures)),
                              ("model", lambda: _check_model_step(rank, world, pctx, dev, failures))]:
+            print(f"[rank {rank}] {stage} ...", flush=True)
             check()
             torch.cuda.synchronize()
             KC.check_status(dev)
+            print(f"[rank {rank}] {stage} done, failures so far {len(failures)}", flush=True)
     except Exception as exc:  # report instead of hanging the peer
         failures.append(f"exception in {stage}: {exc!r}")
     q.put((rank, failures))
     dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world", WORLDS)
-def test_fused_tp(world):
+def run_ranks(worker, world, deadline_s=420.0):
+    """Start ``world`` workers; collect ``{rank: failures}``. A worker that dies
+    without reporting, or is still silent at the deadline, is reported as such
+    (and killed) instead of leaving the harness waiting."""
+    import queue
+    import time
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    procs = [ctx.Process(target=worker, args=(r, world, port, q)) for r in range(world)]
     for p in procs:
         p.start()
-    results = dict(q.get(timeout=600) for _ in procs)
-    for p in procs:
-        p.join(timeout=60)
-    assert all(results[r] == [] for r in range(world)), results
+    results, deadline = {}, time.monotonic() + deadline_s
+    while len(results) < world and time.monotonic() < deadline:
+        try:
+            rank, failures = q.get(timeout=1.0)
+            results[rank] = failures
+        except queue.Empty:
+            dead = [r for r, p in enumerate(procs) if r not in results and p.exitcode is not None]
+            if dead:
+                time.sleep(2.0)  # a last report may still be in the pipe
+                while True:
+                    try:
+                        rank, failures = q.get(timeout=0.5)
+                        results[rank] = failures
+                    except queue.Empty:
+                        break
+                for r in dead:
+                    results.setdefault(r, [f"worker exited with code {procs[r].exitcode} without a report"])
+                break
+    for r, p in enumerate(procs):
+        p.join(timeout=30)
+        if p.is_alive():
+            p.kill()
+            p.join()
+            results.setdefault(r, ["worker still running at the deadline (killed)"])
+    return results
+
+
+@pytest.mark.parametrize("world", WORLDS)
+def test_fused_tp(world):
+    results = run_ranks(_worker, world)
+    assert all(results.get(r) == [] for r in range(world)), results
