@@ -336,14 +336,15 @@ fused_tp_kernel(const __grid_constant__ CUtensorMap tmA_local, const __grid_cons
 #pragma unroll
     for (int s = 0; s < STAGES; ++s) issued[s] = -1;
     int* tile_ctr = claim_ctr(a, my_flags, kClaimTiles);
+    int next = claim(tile_ctr, 0);  // claimed one tile ahead: the atomic's latency hides behind a tile
     for (int it = 0;; ++it) {
       const int slot = it & (kQueue - 1);
       if (!mbar_wait_abortable(&qempty[slot], ((uint32_t)(it / kQueue) & 1u) ^ 1u, a.err, abort_flag)) break;
-      int t = *abort_flag ? -1 : claim(tile_ctr, it);
-      if (t >= num_tiles) t = -1;
+      const int t = (*abort_flag || next >= num_tiles) ? -1 : next;
       tq[slot] = t;
       mbar_arrive(&qfull[slot]);
       if (t < 0) break;
+      next = claim(tile_ctr, it + 1);
       const TileInfo ti = tile_of<MODE>(t, a, mt_chunk, num_n);
       const bool from_gather = is_ag<MODE>() && ti.chunk != a.rank;
       if (from_gather && !((ready_mask >> ti.chunk) & 1u)) {
