@@ -86,6 +86,51 @@ void gemm(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, bool a_mn, bo
   check_ok(nmb::gemm_bf16(g, at::cuda::getCurrentCUDAStream()), "gemm_bf16");
 }
 
+// Fused gate|up projection with the SwiGLU epilogue (gemm.cu, OutMode::kSwiGLU):
+// a[M,F] = silu(X W_gate) * (X W_up) for X [M,K] and W_gu [K,2F] (gate | up
+// column halves); `gu` [M,2F] receives the bf16 pre-activation when given.
+void gemm_swiglu(const at::Tensor& X, const at::Tensor& W, at::Tensor& a, const c10::optional<at::Tensor>& gu,
+                 const c10::optional<at::Tensor>& err) {
+  check_cuda(X, "X");
+  check_cuda(W, "W");
+  check_cuda(a, "a");
+  TORCH_CHECK(X.scalar_type() == at::kBFloat16 && W.scalar_type() == at::kBFloat16 &&
+                  a.scalar_type() == at::kBFloat16,
+              "X, W and a must be bf16");
+  const int M = X.size(0), K = X.size(1), N = W.size(1);
+  TORCH_CHECK(W.size(0) == K, "inner dimensions differ");
+  TORCH_CHECK(N % 16 == 0, "2F must be a multiple of 16");
+  TORCH_CHECK(a.size(0) == M && a.size(1) == N / 2, "a has the wrong shape");
+  nmb::GemmArgs g{};
+  g.A = X.data_ptr();
+  g.B = W.data_ptr();
+  g.C = a.data_ptr();
+  g.lda = row_stride(X);
+  g.ldb = row_stride(W);
+  g.ldc = row_stride(a);
+  TORCH_CHECK(g.lda % 8 == 0 && g.ldb % 8 == 0 && g.ldc % 8 == 0, "row strides must be multiples of 8");
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(g.A) % 16 == 0 && reinterpret_cast<uintptr_t>(g.B) % 16 == 0 &&
+                  reinterpret_cast<uintptr_t>(g.C) % 16 == 0,
+              "operands must be 16-byte aligned");
+  if (gu.has_value()) {
+    check_cuda(*gu, "gu");
+    TORCH_CHECK(gu->scalar_type() == at::kBFloat16 && gu->size(0) == M && gu->size(1) == N, "gu must be bf16 [M, 2F]");
+    g.gu = gu->data_ptr();
+    g.ldgu = row_stride(*gu);
+    TORCH_CHECK(g.ldgu % 8 == 0 && reinterpret_cast<uintptr_t>(g.gu) % 16 == 0, "gu must be 16-byte aligned");
+  }
+  g.M = M;
+  g.N = N;
+  g.K = K;
+  g.a_mn = false;
+  g.b_mn = true;
+  g.out = nmb::OutMode::kSwiGLU;
+  g.err = err_ptr(err);
+  g.num_sms = num_sms();
+  const at::cuda::CUDAGuard guard(X.device());
+  check_ok(nmb::gemm_bf16(g, at::cuda::getCurrentCUDAStream()), "gemm_swiglu");
+}
+
 // One fused tensor-parallel GEMM + collective (see fused_tp.cu). `ws` holds every
 // rank's workspace pointer (mapped in this process); offsets are in bytes.
 void fused_tp_gemm(int64_t mode, const at::Tensor& a_local, const at::Tensor& B, bool b_mn, at::Tensor& out,
@@ -229,6 +274,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "nano_megatron_b200 sm_100a kernels";
   m.def("gemm", &gemm, "tcgen05 bf16 GEMM", pybind11::arg("A"), pybind11::arg("B"), pybind11::arg("C"),
         pybind11::arg("a_mn"), pybind11::arg("b_mn"), pybind11::arg("out_mode"), pybind11::arg("err") = pybind11::none());
+  m.def("gemm_swiglu", &gemm_swiglu, "tcgen05 gate|up GEMM with the SwiGLU epilogue", pybind11::arg("X"),
+        pybind11::arg("W"), pybind11::arg("a"), pybind11::arg("gu") = c10::nullopt,
+        pybind11::arg("err") = c10::nullopt);
   m.def("fused_tp_gemm", &fused_tp_gemm, pybind11::arg("mode"), pybind11::arg("a_local"), pybind11::arg("B"),
         pybind11::arg("b_mn"), pybind11::arg("out"), pybind11::arg("ws"), pybind11::arg("rank"), pybind11::arg("M"),
         pybind11::arg("gather_off"), pybind11::arg("recv_off"), pybind11::arg("flags_off"), pybind11::arg("epoch"),

@@ -24,10 +24,19 @@
 // masked in the epilogue. Requirements: 16-byte aligned bases and row strides
 // (every dim multiple of 8 bf16 elements), N % 8 == 0.
 //
+// SwiGLU mode (OUT == 3, forward of the fused gate|up projection): B is the
+// gate|up weight [K][2F]. A tile's four 64-column B boxes come from columns
+// n0, n0+64 of the gate half and F+n0, F+n0+64 of the up half, so the 256
+// accumulator columns of a row hold gate and up of the same 128 features.
+// The epilogue rounds both to bf16 (the values the unfused path stores),
+// writes a = bf16(bf16(silu(g)) * u) -- the arithmetic of swiglu_fwd_kernel --
+// and, when the backward needs them, g and u through two [M][F] views of gu.
+//
 // Every mbarrier wait is bounded; a timeout records an error code in `err`
 // and the kernel drains and returns instead of spinning forever.
 
 #include <cuda.h>
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
 #include "gemm.cuh"
@@ -60,7 +69,8 @@ __device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int& tm
 template <bool A_MN, bool B_MN, int OUT>
 __global__ void __launch_bounds__(THREADS, 1)
 gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                 const __grid_constant__ CUtensorMap tmC, int M, int N, int K, int* err) {
+                 const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmG,
+                 const __grid_constant__ CUtensorMap tmU, int M, int N, int K, bool save_gu, int* err) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* staging = smem + STAGES * STAGE_BYTES;
@@ -73,8 +83,10 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
 
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
+  constexpr bool SWIGLU = OUT == 3;
+  const int F = N / 2;  // SwiGLU: features per half
   const int num_m = (M + BM - 1) / BM;
-  const int num_n = (N + BN - 1) / BN;
+  const int num_n = SWIGLU ? (F + BN / 2 - 1) / (BN / 2) : (N + BN - 1) / BN;
   const int num_tiles = num_m * num_n;
   const int num_k = (K + BK - 1) / BK;
 
@@ -121,7 +133,12 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
         } else {
           tma_load_2d(a_dst, &tmA, &full[stage], k0, tm * BM);
         }
-        if (B_MN) {
+        if (SWIGLU) {
+          // gate columns [n0, n0+128) then up columns [F+n0, F+n0+128)
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            tma_load_2d(b_dst + j * 8192, &tmB, &full[stage], (j >> 1) * F + tn * (BN / 2) + 64 * (j & 1), k0);
+        } else if (B_MN) {
 #pragma unroll
           for (int j = 0; j < 4; ++j) tma_load_2d(b_dst + j * 8192, &tmB, &full[stage], tn * BN + 64 * j, k0);
         } else {
@@ -178,6 +195,65 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
       tc_fence_after();
       const int row0 = tm * BM + quarter * 32;
       const uint32_t t_row = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN;
+      if (SWIGLU) {
+        // One box of a row = 64 bf16 (128 B) in the 128-byte swizzle: stage it
+        // and TMA-store it to `map` at (col, row0) unless the box is past F.
+        auto store_box = [&](const CUtensorMap* map, const float* v, int col) {
+          uint8_t* buf = stg + (nbox & 1) * STG_BUF;
+          if (lane == 0) bulk_wait_group_read<1>();
+          __syncwarp();
+          uint8_t* row = buf + lane * 128;
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            uint4 u;
+            u.x = pack_bf16x2(v[8 * j + 0], v[8 * j + 1]);
+            u.y = pack_bf16x2(v[8 * j + 2], v[8 * j + 3]);
+            u.z = pack_bf16x2(v[8 * j + 4], v[8 * j + 5]);
+            u.w = pack_bf16x2(v[8 * j + 6], v[8 * j + 7]);
+            *reinterpret_cast<uint4*>(row + ((j ^ (lane & 7)) << 4)) = u;
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            if (col < F && row0 < M) tma_store_2d(map, buf, col, row0);
+            bulk_commit_group();
+          }
+          ++nbox;
+        };
+#pragma unroll 1
+        for (int c = 0; c < BN / 2; c += 64) {
+          uint32_t gr[64], ur[64];
+          tmem_ld_32x32b_x32(t_row + c, *reinterpret_cast<uint32_t(*)[32]>(&gr[0]));
+          tmem_ld_32x32b_x32(t_row + c + 32, *reinterpret_cast<uint32_t(*)[32]>(&gr[32]));
+          tmem_ld_32x32b_x32(t_row + BN / 2 + c, *reinterpret_cast<uint32_t(*)[32]>(&ur[0]));
+          tmem_ld_32x32b_x32(t_row + BN / 2 + c + 32, *reinterpret_cast<uint32_t(*)[32]>(&ur[32]));
+          tmem_wait_ld_regs(*reinterpret_cast<uint32_t(*)[32]>(&gr[0]));
+          tmem_wait_ld_regs(*reinterpret_cast<uint32_t(*)[32]>(&gr[32]));
+          tmem_wait_ld_regs(*reinterpret_cast<uint32_t(*)[32]>(&ur[0]));
+          tmem_wait_ld_regs(*reinterpret_cast<uint32_t(*)[32]>(&ur[32]));
+          float g[64], u[64];
+#pragma unroll
+          for (int j = 0; j < 64; ++j) {
+            g[j] = __bfloat162float(__float2bfloat16_rn(__uint_as_float(gr[j])));
+            u[j] = __bfloat162float(__float2bfloat16_rn(__uint_as_float(ur[j])));
+          }
+          const int col = tn * (BN / 2) + c;
+          if (save_gu) {
+            store_box(&tmG, g, col);
+            store_box(&tmU, u, col);
+          }
+#pragma unroll
+          for (int j = 0; j < 64; ++j) {
+            const float sl = g[j] / (1.f + __expf(-g[j]));
+            g[j] = __bfloat162float(__float2bfloat16_rn(sl)) * u[j];
+          }
+          store_box(&tmC, g, col);
+        }
+        tc_fence_before();
+        mbar_arrive(&tempty[acc]);
+        if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+        continue;
+      }
 #pragma unroll 1
       for (int c = 0; c < BN; c += CW) {
         uint32_t r[CW];
@@ -260,11 +336,23 @@ cudaError_t launch(const GemmArgs& g, cudaStream_t stream) {
   // A: K-major stored [M][K] (lda = row stride), or M-major stored [K][M].
   if (!make_tmap_bf16_2d(&ta, g.A, A_MN ? g.M : g.K, A_MN ? g.K : g.M, g.lda, 64, A_MN ? 64 : BM)) return cudaErrorInvalidValue;
   if (!make_tmap_bf16_2d(&tb, g.B, B_MN ? g.N : g.K, B_MN ? g.K : g.N, g.ldb, 64, B_MN ? 64 : BN)) return cudaErrorInvalidValue;
-  const int tiles = ((g.M + BM - 1) / BM) * ((g.N + BN - 1) / BN);
+  constexpr bool fp32_out = OUT == 1 || OUT == 2;
+  const int out_cols = OUT == 3 ? g.N / 2 : g.N;
+  const int tiles = ((g.M + BM - 1) / BM) * (OUT == 3 ? (out_cols + BN / 2 - 1) / (BN / 2) : (g.N + BN - 1) / BN);
   const int grid = tiles < g.num_sms ? tiles : g.num_sms;
-  CUtensorMap tc;
-  if (!make_tmap_out_2d(&tc, g.C, OUT != 0, g.N, g.M, g.ldc * (OUT != 0 ? 4 : 2), 32)) return cudaErrorInvalidValue;
-  kernel<<<grid, THREADS, SMEM_BYTES, stream>>>(ta, tb, tc, g.M, g.N, g.K, g.err);
+  CUtensorMap tc, tg, tu;
+  if (!make_tmap_out_2d(&tc, g.C, fp32_out, out_cols, g.M, g.ldc * (fp32_out ? 4 : 2), 32))
+    return cudaErrorInvalidValue;
+  tg = tu = tc;
+  const bool save_gu = OUT == 3 && g.gu != nullptr;
+  if (save_gu) {
+    // gate and up halves of gu as two [M][F] views with row stride ldgu
+    const __nv_bfloat16* gu = static_cast<const __nv_bfloat16*>(g.gu);
+    if (!make_tmap_out_2d(&tg, gu, false, out_cols, g.M, g.ldgu * 2, 32) ||
+        !make_tmap_out_2d(&tu, gu + out_cols, false, out_cols, g.M, g.ldgu * 2, 32))
+      return cudaErrorInvalidValue;
+  }
+  kernel<<<grid, THREADS, SMEM_BYTES, stream>>>(ta, tb, tc, tg, tu, g.M, g.N, g.K, save_gu, g.err);
   return cudaGetLastError();
 }
 
@@ -322,6 +410,10 @@ cudaError_t gemm_bf16(const GemmArgs& g, cudaStream_t stream) {
   if (g.a_mn && g.b_mn && g.out == OutMode::kF32) return launch<true, true, 1>(g, stream);
   if (!g.a_mn && !g.b_mn && g.out == OutMode::kF32Accumulate) return launch<false, false, 2>(g, stream);
   if (!g.a_mn && g.b_mn && g.out == OutMode::kF32Accumulate) return launch<false, true, 2>(g, stream);
+  if (!g.a_mn && g.b_mn && g.out == OutMode::kSwiGLU) {
+    if (g.N % 16 != 0) return cudaErrorInvalidValue;  // F % 8 == 0: 16-byte aligned up half
+    return launch<false, true, 3>(g, stream);
+  }
   return cudaErrorInvalidValue;
 }
 

@@ -8,7 +8,10 @@
 
 namespace nmb {
 
-enum class OutMode : int { kBf16 = 0, kF32 = 1, kF32Accumulate = 2 };
+// kSwiGLU: B is the fused gate|up weight [K][2F] (N-major, N = 2F); C = a =
+// silu(X W_gate) * (X W_up) as bf16 [M][F]; optionally also the bf16
+// pre-activation gu [M][2F] (gate | up halves) for the backward.
+enum class OutMode : int { kBf16 = 0, kF32 = 1, kF32Accumulate = 2, kSwiGLU = 3 };
 
 struct GemmArgs {
   const void* A;   // bf16; [M][lda] if !a_mn (K-major), [K][lda] if a_mn (M-major)
@@ -20,6 +23,8 @@ struct GemmArgs {
   OutMode out;
   int* err;        // device error word (may be null)
   int num_sms;
+  void* gu = nullptr;  // kSwiGLU only: [M][ldgu] bf16 pre-activation output, or null
+  long ldgu = 0;
 };
 
 cudaError_t gemm_bf16(const GemmArgs& args, cudaStream_t stream);

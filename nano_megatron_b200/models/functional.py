@@ -53,6 +53,30 @@ def _grad_written(tensor) -> None:
         _grad_observer(tensor)
 
 
+# True while a checkpointed layer runs its first forward: torch.utils.checkpoint
+# drops what that forward saves and recomputes the layer before its backward,
+# so an op may skip materializing tensors that exist only to be saved.
+_discarded_forward = [False]
+
+
+class discarded_forward:
+    """Context manager marking (or not) the first forward of a recomputed layer."""
+
+    def __init__(self, active: bool):
+        self.active = active
+
+    def __enter__(self):
+        self.previous, _discarded_forward[0] = _discarded_forward[0], self.active
+
+    def __exit__(self, *exc):
+        _discarded_forward[0] = self.previous
+
+
+def _placeholder(shape, like: torch.Tensor) -> torch.Tensor:
+    """A tensor with the metadata checkpointing compares (shape, dtype, device) and no storage of that size."""
+    return torch.empty((1,) * len(shape), dtype=like.dtype, device=like.device).expand(*shape)
+
+
 class WeightRef:
     """A weight as the kernels see it: master data, compute copy, grad buffer.
 
@@ -169,6 +193,54 @@ class _ColumnLinear(torch.autograd.Function):
 
 def column_linear(x, wref: WeightRef, pctx: ParallelContext, mode: str, dtype: torch.dtype):
     return _ColumnLinear.apply(x, wref, pctx, mode, dtype, *wref.params)
+
+
+# ------------------------------------------------- gate|up linear + SwiGLU
+class _GateUpSwiGLU(torch.autograd.Function):
+    """``a = silu(X W_gate) * (X W_up)`` in one GEMM whose epilogue applies the
+    SwiGLU (``X = x``, or ``AG(x)`` in mode ``"ag"``): the pre-activation is
+    written only when a backward will read it, and no separate element-wise
+    pass reads it back. Backward: SwiGLU backward, then the column-parallel
+    backward of the gate|up projection (``nano_megatron/model.py:151-152``)."""
+
+    @staticmethod
+    def forward(ctx, x, wref, pctx, mode, dtype, *params):
+        x = x if x.dtype == dtype else x.to(dtype)
+        w = wref.for_compute(dtype)
+        X = _ag(x, pctx) if mode == "ag" else x
+        a, gu = ops.cuda_ops().mm_swiglu(X, w, save_gu=not _discarded_forward[0])
+        if gu is None:
+            gu = _placeholder((a.shape[0], 2 * a.shape[1]), a)
+        ctx.save_for_backward(x, w, gu)
+        ctx.wref, ctx.pctx, ctx.mode = wref, pctx, mode
+        return a
+
+    @staticmethod
+    def backward(ctx, da):
+        x, w, gu = ctx.saved_tensors
+        pctx, mode, wref = ctx.pctx, ctx.mode, ctx.wref
+        dgu = ops.swiglu_bwd(da.contiguous(), gu)
+        dX = ops.mm_nt(dgu, w)
+        dx = _rs(dX, pctx) if mode == "ag" else (_ar(dX, pctx) if mode == "f" else dX)
+        X = _ag(x, pctx) if mode == "ag" else x
+        grads = wref.accumulate(ops.mm_tn_acc, X, dgu)
+        return (dx, None, None, None, None, *grads)
+
+
+def gate_up_swiglu_supported(x: torch.Tensor, ffn_local: int, pctx: ParallelContext, mode: str) -> bool:
+    """The one-GEMM SwiGLU path (bf16 compute): CUDA, 8-aligned width, and not a
+    layer whose gate|up GEMM runs as the fused all-gather kernel."""
+    if not (x.is_cuda and ffn_local % 8 == 0):
+        return False
+    if mode == "ag" and pctx.tp_size > 1 and pctx.resources.get("fused_tp", False):
+        from ..ops import fused_tp
+        if fused_tp.supported(x.shape[0], pctx):
+            return False
+    return True
+
+
+def gate_up_swiglu(x, wref: WeightRef, pctx: ParallelContext, mode: str, dtype: torch.dtype):
+    return _GateUpSwiGLU.apply(x, wref, pctx, mode, dtype, *wref.params)
 
 
 # --------------------------------------------------------------- row linear

@@ -28,8 +28,9 @@ from ..parallel.context import ParallelContext
 from .. import ops
 from .buffers import FlatBuffers
 from .config import GPTConfig, divide
-from .functional import (WeightRef, causal_attention, column_linear,
-                         lm_head_cross_entropy, lm_head_logits, row_linear, swiglu)
+from .functional import (WeightRef, causal_attention, column_linear, discarded_forward,
+                         gate_up_swiglu, gate_up_swiglu_supported, lm_head_cross_entropy,
+                         lm_head_logits, row_linear, swiglu)
 from .layers import (ColumnParallelLinear, RMSNorm, RowParallelLinear,
                      VocabParallelEmbedding)
 
@@ -99,10 +100,13 @@ class ParallelMLP(nn.Module):
 
     def forward(self, x, dtype):
         sp = self.sequence_parallel and self.ctx.tp_size > 1
+        mode = "ag" if sp else "f"
         gu_ref = _fused_ref(self.flat_buffers, (self.gate.weight, self.up.weight))
-        gu = column_linear(x, gu_ref, self.ctx, "ag" if sp else "f", dtype)
-        return row_linear(swiglu(gu), WeightRef.of(self.down.weight), self.ctx,
-                          "rs" if sp else "g", dtype)
+        if dtype == torch.bfloat16 and gate_up_swiglu_supported(x, self.gate.weight.shape[1], self.ctx, mode):
+            a = gate_up_swiglu(x, gu_ref, self.ctx, mode, dtype)
+        else:
+            a = swiglu(column_linear(x, gu_ref, self.ctx, mode, dtype))
+        return row_linear(a, WeightRef.of(self.down.weight), self.ctx, "rs" if sp else "g", dtype)
 
 
 class TransformerLayer(nn.Module):
@@ -220,7 +224,16 @@ class GPT(nn.Module):
     def _layer_call(self, layer, h, batch, dtype):
         cos, sin = self.rope_cos, self.rope_sin
         if self.config.recompute and self.training:
-            return checkpoint(layer, h, batch, cos, sin, dtype, use_reentrant=False)
+            calls = [0]
+
+            def run(h, batch, cos, sin, dtype):
+                # the first call is the forward whose saved tensors checkpoint
+                # drops; the second is the recomputation before backward
+                calls[0] += 1
+                with discarded_forward(calls[0] == 1):
+                    return layer(h, batch, cos, sin, dtype)
+
+            return checkpoint(run, h, batch, cos, sin, dtype, use_reentrant=False)
         return layer(h, batch, cos, sin, dtype)
 
     def forward(self, x, labels=None):

@@ -149,6 +149,18 @@ def mm_nt(a, b):
     return out
 
 
+def mm_swiglu(x, w_gu, save_gu: bool):
+    """``silu(x @ w_gate) * (x @ w_up)`` for the fused ``w_gu = [w_gate | w_up]``
+    ``[K, 2F]`` in one GEMM (SwiGLU epilogue); also the pre-activation
+    ``gu [M, 2F]`` when ``save_gu`` (the backward needs it), else None."""
+    m, f = x.shape[0], w_gu.shape[1] // 2
+    a = torch.empty((m, f), dtype=x.dtype, device=x.device)
+    gu = torch.empty((m, 2 * f), dtype=x.dtype, device=x.device) if save_gu else None
+    C.gemm_swiglu(x, w_gu, a, gu, status_word(x.device))
+    _count()
+    return a, gu
+
+
 def mm_tn_acc(a, b, out):
     """``out[K,N] += a[M,K]^T @ b[M,N]`` (fp32 ``out``)."""
     if a.dtype == torch.float32:

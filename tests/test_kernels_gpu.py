@@ -103,6 +103,27 @@ def test_swiglu(dtype):
     assert _rel(d, R.swiglu_bwd(da.float(), gu.float())) < (1e-2 if dtype == torch.bfloat16 else 1e-5)
 
 
+@pytest.mark.parametrize("M,K,F,save", [(1024, 512, 1024, True), (384, 256, 704, True),
+                                         (256, 128, 344, False), (2048, 1024, 3584, False)])
+def test_swiglu_gemm_epilogue(M, K, F, save):
+    """One GEMM with the SwiGLU epilogue against the GEMM + SwiGLU kernels
+    (same rounding points) and against fp32 torch; ragged feature counts
+    exercise the partial last tile of each half."""
+    torch.manual_seed(M + F)
+    x = (torch.randn(M, K, device=DEV) * 0.5).bfloat16()
+    w = (torch.randn(K, 2 * F, device=DEV) / K ** 0.5).bfloat16()
+    a, gu = KC.mm_swiglu(x, w, save_gu=save)
+    gu_ref = KC.mm_nn(x, w)
+    a_ref = KC.swiglu(gu_ref)
+    assert (gu is None) == (not save)
+    if save:
+        assert _rel(gu, gu_ref) < 1e-4, _rel(gu, gu_ref)
+    assert _rel(a, a_ref) < 1e-4, _rel(a, a_ref)
+    g32 = x.float() @ w.float()
+    want = torch.nn.functional.silu(g32[:, :F]) * g32[:, F:]
+    assert _rel(a, want) < 1e-2
+
+
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
 def test_rope_roundtrip(dtype):
     from nano_megatron_b200 import _C

@@ -1,6 +1,9 @@
 """The whole GPT stage on the GPU (bf16, our kernels) against the same model
 on the CPU in fp32 (plain torch math) from identical weights: loss, logits and
-every gradient within bf16 tolerance; and AdamW steps through the fused kernel."""
+every gradient within bf16 tolerance; recomputation reproduces the gradients
+of the plain forward bit for bit (the first forward of a recomputed layer
+skips the tensors only a backward reads); and AdamW steps through the fused
+kernel."""
 
 import dataclasses
 
@@ -44,6 +47,24 @@ def test_gpt_cuda_matches_cpu(recompute, tie):
         assert _rel(pg.grad.cpu(), pc.grad) < 6e-2, (n, _rel(pg.grad.cpu(), pc.grad))
     with torch.no_grad():
         assert _rel(gpu(x.to(DEV)).cpu(), cpu(x)) < 2e-2
+
+
+def test_recompute_gives_identical_gradients():
+    cfg = GPTConfig(vocab_size=512, n_layer=3, n_head=2, n_embd=256, seq_len=256, ffn_hidden_size=704,
+                    compute_dtype="bfloat16", tie_word_embeddings=False, init_std=0.05)
+    x = torch.randint(0, 512, (2, 256), device=DEV)
+    y = torch.randint(0, 512, (2, 256), device=DEV)
+    grads, losses = {}, {}
+    for recompute in (False, True):
+        torch.manual_seed(0)
+        model = GPT(dataclasses.replace(cfg, recompute=recompute), device=DEV)
+        loss = model(x, y)
+        loss.backward()
+        losses[recompute] = loss.item()
+        grads[recompute] = [p.grad.clone() for p in model.parameters()]
+    assert losses[True] == losses[False]
+    for g0, g1 in zip(grads[False], grads[True]):
+        assert torch.equal(g0, g1)
 
 
 def test_training_step_on_gpu_decreases_loss():
