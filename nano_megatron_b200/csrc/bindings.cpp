@@ -138,7 +138,7 @@ void fused_tp_gemm(int64_t mode, const at::Tensor& a_local, const at::Tensor& B,
                    int64_t flags_off, int64_t epoch, bool copy_own, const at::Tensor& err, double timeout_s,
                    const c10::optional<at::Tensor>& save_out, const c10::optional<at::Tensor>& labels,
                    int64_t vocab_start, const c10::optional<at::Tensor>& ce_part,
-                   const c10::optional<at::Tensor>& ce_target) {
+                   const c10::optional<at::Tensor>& ce_target, const c10::optional<at::Tensor>& gu) {
   check_cuda(a_local, "a_local");
   check_cuda(B, "B");
   check_cuda(out, "out");
@@ -159,7 +159,8 @@ void fused_tp_gemm(int64_t mode, const at::Tensor& a_local, const at::Tensor& B,
   TORCH_CHECK(M % world == 0 && a.m_chunk % 128 == 0, "rows per rank must be a multiple of 128");
   const bool ag = mode != nmb::kReduceScatterGemm;
   TORCH_CHECK(ag ? a_local.size(0) == a.m_chunk : a_local.size(0) == M, "A rows");
-  TORCH_CHECK(out.size(0) == (ag ? M : a.m_chunk) && out.size(1) == a.N, "out shape");
+  const bool swiglu = mode == nmb::kAllGatherGemmSwiGLU;
+  TORCH_CHECK(out.size(0) == (ag ? M : a.m_chunk) && out.size(1) == (swiglu ? a.N / 2 : a.N), "out shape");
   a.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
   a.ldo = out.stride(0);
   for (int r = 0; r < world; ++r) a.ws[r] = reinterpret_cast<uint8_t*>(ws[r]);
@@ -191,6 +192,13 @@ void fused_tp_gemm(int64_t mode, const at::Tensor& a_local, const at::Tensor& B,
     a.vocab_start = vocab_start;
     a.ce_part = reinterpret_cast<float2*>(ce_part->data_ptr<float>());
     a.ce_target = ce_target->data_ptr<float>();
+  }
+  if (swiglu && gu.has_value()) {
+    TORCH_CHECK(gu->is_cuda() && gu->scalar_type() == at::kBFloat16 && gu->stride(1) == 1 && gu->size(0) == M &&
+                    gu->size(1) == a.N && gu->stride(0) % 8 == 0 && reinterpret_cast<uintptr_t>(gu->data_ptr()) % 16 == 0,
+                "gu must be a 16-byte aligned bf16 [M, 2F] tensor");
+    a.gu = reinterpret_cast<__nv_bfloat16*>(gu->data_ptr());
+    a.ldgu = gu->stride(0);
   }
   const at::cuda::CUDAGuard guard(a_local.device());
   check_ok(nmb::fused_tp_gemm((int)mode, a, B.data_ptr(), row_stride(B), b_mn, num_sms(),
@@ -283,7 +291,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         pybind11::arg("copy_own"), pybind11::arg("err"), pybind11::arg("timeout_s"),
         pybind11::arg("save_out") = pybind11::none(), pybind11::arg("labels") = pybind11::none(),
         pybind11::arg("vocab_start") = 0, pybind11::arg("ce_part") = pybind11::none(),
-        pybind11::arg("ce_target") = pybind11::none());
+        pybind11::arg("ce_target") = pybind11::none(), pybind11::arg("gu") = pybind11::none());
   m.def("ce_merge", &ce_merge);
   m.def("dp_allreduce", &dp_allreduce);
   m.def("dp_flag_bytes", &dp_flag_bytes);

@@ -149,12 +149,16 @@ cudaError_t dp_allreduce(const DpReduceArgs& a, int num_sms, cudaStream_t stream
   if (a.world < 1 || a.world > kDpMaxRanks || a.rank < 0 || a.rank >= a.world || a.n % 4 != 0 ||
       a.offset % 4 != 0 || a.epoch <= 0 || num_sms < 1)
     return cudaErrorInvalidValue;
-  // one CTA per SM at most (leaves room for a GEMM CTA beside it), fewer for
-  // small spans: about 8 float4 of the slice per thread
+  // at most one CTA on every other SM: the averaging runs beside the
+  // backward's GEMMs, whose CTAs do not fit next to one of ours on an SM, so
+  // half the SMs stay free for them; fewer CTAs for small spans (about 8
+  // float4 of the slice per thread). 74 CTAs x 512 threads x 8 loads of 16 B
+  // keep about 5 MB in flight, far above what the NVLink latency needs.
   const long per4 = (a.n / 4 + a.world - 1) / a.world;
   long blocks = (per4 + 8L * kDpThreads - 1) / (8L * kDpThreads);
   if (blocks < 1) blocks = 1;
-  if (blocks > num_sms) blocks = num_sms;
+  const int cap = num_sms > 1 ? num_sms / 2 : 1;
+  if (blocks > cap) blocks = cap;
   switch (a.world) {
 #define NMB_DP(W) \
   case W: dp_allreduce_kernel<W><<<(int)blocks, kDpThreads, 0, stream>>>(a); break;

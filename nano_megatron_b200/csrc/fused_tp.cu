@@ -40,6 +40,12 @@
 //     epilogue thread, so no cross-thread reduction) plus the target logit.
 //     ce_merge (below) then combines tiles and ranks; fp32 logits are never
 //     materialized.
+// all-gather -> gate|up GEMM -> SwiGLU (kAllGatherGemmSwiGLU): B is the gate|up
+//   weight [K][2F]; a tile's four 64-column B boxes are gate columns n0, n0+64
+//   and up columns F+n0, F+n0+64, so an accumulator row holds gate and up of
+//   the same 128 features. The epilogue writes a = bf16(bf16(silu(g)) * u)
+//   with g, u rounded to bf16 first (the unfused arithmetic) and, if asked,
+//   the pre-activation halves through two [M][F] views of gu.
 // Optional copy of the gathered input (all-gather modes, `save_out`): after
 // its pushes the comm warp of CTA b copies slice b of every chunk (its own
 // from x, chunk c once peer c's CTA b flagged it) into save_out, overlapping
@@ -183,7 +189,9 @@ template <int MODE, bool B_MN>
 __global__ void __launch_bounds__(THREADS, 1)
 fused_tp_kernel(const __grid_constant__ CUtensorMap tmA_local, const __grid_constant__ CUtensorMap tmA_gather,
                 const __grid_constant__ CUtensorMap tmB, const __grid_constant__ CUtensorMap tmOut,
+                const __grid_constant__ CUtensorMap tmG, const __grid_constant__ CUtensorMap tmU,
                 const FusedTpArgs a) {
+  constexpr bool SWIGLU = MODE == kAllGatherGemmSwiGLU;
   constexpr int STAGES = Cfg<MODE>::STAGES;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -202,7 +210,8 @@ fused_tp_kernel(const __grid_constant__ CUtensorMap tmA_local, const __grid_cons
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int mt_chunk = a.m_chunk / BM;
-  const int num_n = (a.N + BN - 1) / BN;
+  const int F = a.N / 2;  // SwiGLU: features per half
+  const int num_n = SWIGLU ? (F + BN / 2 - 1) / (BN / 2) : (a.N + BN - 1) / BN;
   const int num_tiles = a.world * mt_chunk * num_n;
   const int num_k = (a.K + BK - 1) / BK;
   const int epoch = (int)a.epoch;
@@ -364,7 +373,11 @@ fused_tp_kernel(const __grid_constant__ CUtensorMap tmA_local, const __grid_cons
         issued[stage] = (int)phase;
         const int k0 = kb * BK;
         tma_load_2d(a_dst, amap, &full[stage], k0, arow);
-        if (B_MN) {
+        if (SWIGLU) {
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            tma_load_2d(b_dst + j * 8192, &tmB, &full[stage], (j >> 1) * F + ti.tn * (BN / 2) + 64 * (j & 1), k0);
+        } else if (B_MN) {
 #pragma unroll
           for (int j = 0; j < 4; ++j) tma_load_2d(b_dst + j * 8192, &tmB, &full[stage], ti.tn * BN + 64 * j, k0);
         } else {
@@ -463,6 +476,61 @@ fused_tp_kernel(const __grid_constant__ CUtensorMap tmA_local, const __grid_cons
       const int row = ti.tm * BM + quarter * 32 + lane;
       const int row_local = row - ti.chunk * a.m_chunk;
       const uint32_t t_row = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN;
+      if (SWIGLU) {
+        const int row0 = ti.tm * BM + quarter * 32;
+        auto store_box = [&](const CUtensorMap* map, const float* v, int col) {
+          uint8_t* buf = box_stg + (nbox & 1) * 4096;
+          if (lane == 0) bulk_wait_group_read<1>();
+          __syncwarp();
+          uint8_t* brow = buf + lane * 128;
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            uint4 u;
+            u.x = pack_bf16x2(v[8 * j + 0], v[8 * j + 1]);
+            u.y = pack_bf16x2(v[8 * j + 2], v[8 * j + 3]);
+            u.z = pack_bf16x2(v[8 * j + 4], v[8 * j + 5]);
+            u.w = pack_bf16x2(v[8 * j + 6], v[8 * j + 7]);
+            *reinterpret_cast<uint4*>(brow + ((j ^ (lane & 7)) << 4)) = u;
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            if (col < F) tma_store_2d(map, buf, col, row0);
+            bulk_commit_group();
+          }
+          ++nbox;
+        };
+#pragma unroll 1
+        for (int c = 0; c < BN / 2; c += 64) {
+          uint32_t gr[64], ur[64];
+          tmem_ld_32x32b_x32(t_row + c, *reinterpret_cast<uint32_t(*)[32]>(&gr[0]));
+          tmem_ld_32x32b_x32(t_row + c + 32, *reinterpret_cast<uint32_t(*)[32]>(&gr[32]));
+          tmem_ld_32x32b_x32(t_row + BN / 2 + c, *reinterpret_cast<uint32_t(*)[32]>(&ur[0]));
+          tmem_ld_32x32b_x32(t_row + BN / 2 + c + 32, *reinterpret_cast<uint32_t(*)[32]>(&ur[32]));
+          tmem_wait_ld();
+          float g[64], u[64];
+#pragma unroll
+          for (int j = 0; j < 64; ++j) {
+            g[j] = __bfloat162float(__float2bfloat16_rn(__uint_as_float(gr[j])));
+            u[j] = __bfloat162float(__float2bfloat16_rn(__uint_as_float(ur[j])));
+          }
+          const int col = ti.tn * (BN / 2) + c;
+          if (a.gu != nullptr) {
+            store_box(&tmG, g, col);
+            store_box(&tmU, u, col);
+          }
+#pragma unroll
+          for (int j = 0; j < 64; ++j) {
+            const float sl = g[j] / (1.f + __expf(-g[j]));
+            g[j] = __bfloat162float(__float2bfloat16_rn(sl)) * u[j];
+          }
+          store_box(&tmOut, g, col);
+        }
+        tc_fence_before();
+        mbar_arrive(&tempty[acc]);
+        if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+        continue;
+      }
       // cross-entropy statistics of this row over the tile's columns
       float ce_m = -INFINITY, ce_s = 0.f;
       long ce_col = -1;  // target column relative to the tile, if inside
@@ -642,13 +710,21 @@ cudaError_t launch(const FusedTpArgs& a, const void* B, long ldb, int num_sms, c
   }
   if (!make_tmap_bf16_2d(&tb, B, B_MN ? a.N : a.K, B_MN ? a.K : a.N, ldb, 64, B_MN ? 64 : BN))
     return cudaErrorInvalidValue;
+  constexpr bool swiglu = MODE == kAllGatherGemmSwiGLU;
+  const int out_cols = swiglu ? a.N / 2 : a.N;
   CUtensorMap tout = tb;  // reduce-scatter writes its rows itself
-  if (is_ag<MODE>() && !make_tmap_out_2d(&tout, a.out, false, a.N, a.M, (uint64_t)a.ldo * 2, 32))
+  if (is_ag<MODE>() && !make_tmap_out_2d(&tout, a.out, false, out_cols, a.M, (uint64_t)a.ldo * 2, 32))
     return cudaErrorInvalidValue;
-  const int tiles = a.world * (a.m_chunk / BM) * ((a.N + BN - 1) / BN);
+  CUtensorMap tg = tout, tu = tout;
+  if (swiglu && a.gu != nullptr &&
+      (!make_tmap_out_2d(&tg, a.gu, false, out_cols, a.M, (uint64_t)a.ldgu * 2, 32) ||
+       !make_tmap_out_2d(&tu, a.gu + out_cols, false, out_cols, a.M, (uint64_t)a.ldgu * 2, 32)))
+    return cudaErrorInvalidValue;
+  const int num_n = swiglu ? (out_cols + BN / 2 - 1) / (BN / 2) : (a.N + BN - 1) / BN;
+  const int tiles = a.world * (a.m_chunk / BM) * num_n;
   int grid = tiles < num_sms ? tiles : num_sms;
   if (grid > kMaxCtas) grid = kMaxCtas;
-  kernel<<<grid, THREADS, Cfg<MODE>::SMEM, stream>>>(ta_local, ta_gather, tb, tout, a);
+  kernel<<<grid, THREADS, Cfg<MODE>::SMEM, stream>>>(ta_local, ta_gather, tb, tout, tg, tu, a);
   return cudaGetLastError();
 }
 
@@ -738,6 +814,10 @@ cudaError_t fused_tp_gemm(int mode, const FusedTpArgs& a, const void* B, long ld
   if (mode == kAllGatherGemm) {
     return b_mn ? launch<kAllGatherGemm, true>(a, B, ldb, num_sms, stream)
                 : launch<kAllGatherGemm, false>(a, B, ldb, num_sms, stream);
+  }
+  if (mode == kAllGatherGemmSwiGLU) {
+    if (!b_mn || a.N % 16 != 0) return cudaErrorInvalidValue;  // F % 8 == 0: aligned up half
+    return launch<kAllGatherGemmSwiGLU, true>(a, B, ldb, num_sms, stream);
   }
   if (mode == kAllGatherGemmCE) {
     if (a.labels == nullptr || a.ce_part == nullptr || a.ce_target == nullptr || b_mn) return cudaErrorInvalidValue;

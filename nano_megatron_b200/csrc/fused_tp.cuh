@@ -12,6 +12,9 @@ constexpr int kAllGatherGemm = 0;
 constexpr int kReduceScatterGemm = 1;
 // all-gather -> LM-head GEMM with the cross-entropy statistics in the epilogue
 constexpr int kAllGatherGemmCE = 2;
+// all-gather -> gate|up GEMM with the SwiGLU epilogue: B is [K][2F] (gate |
+// up halves), out = silu(X W_gate) * (X W_up) [M][F], gu (optional) [M][2F]
+constexpr int kAllGatherGemmSwiGLU = 3;
 constexpr int kMaxRanks = 8;
 constexpr int kMaxCtas = 160;
 constexpr int kMaxTiles = 16384;
@@ -51,6 +54,9 @@ struct FusedTpArgs {
   long vocab_start;
   float2* ce_part;
   float* ce_target;
+  // kAllGatherGemmSwiGLU: bf16 pre-activation output [M][ldgu] (null = not written)
+  __nv_bfloat16* gu;
+  long ldgu;
 };
 
 cudaError_t fused_tp_gemm(int mode, const FusedTpArgs& args, const void* B, long ldb, bool b_mn, int num_sms,

@@ -160,9 +160,14 @@ class _ColumnLinear(torch.autograd.Function):
         ctx.gathered = mode == "ag" and _use_fused(pctx, x, x.shape[0])
         if ctx.gathered:
             # The kernel also leaves a private copy of AG(x) for the weight
-            # gradient, so the backward needs no second all-gather.
+            # gradient, so the backward needs no second all-gather (not in the
+            # first forward of a recomputed layer, whose saves are dropped).
             from ..ops import fused_tp
-            X, y = fused_tp.all_gather_matmul(x, w, pctx, save_gathered=True)
+            if _discarded_forward[0]:
+                y = fused_tp.all_gather_matmul(x, w, pctx)
+                X = _placeholder((y.shape[0], x.shape[1]), x)
+            else:
+                X, y = fused_tp.all_gather_matmul(x, w, pctx, save_gathered=True)
             ctx.save_for_backward(X, w)
         else:
             X = _ag(x, pctx) if mode == "ag" else x
@@ -207,11 +212,21 @@ class _GateUpSwiGLU(torch.autograd.Function):
     def forward(ctx, x, wref, pctx, mode, dtype, *params):
         x = x if x.dtype == dtype else x.to(dtype)
         w = wref.for_compute(dtype)
-        X = _ag(x, pctx) if mode == "ag" else x
-        a, gu = ops.cuda_ops().mm_swiglu(X, w, save_gu=not _discarded_forward[0])
+        keep = not _discarded_forward[0]
+        ctx.gathered = mode == "ag" and _use_fused(pctx, x, x.shape[0])
+        if ctx.gathered:
+            from ..ops import fused_tp
+            X, a, gu = fused_tp.all_gather_matmul_swiglu(x, w, pctx, save_gu=keep, save_gathered=keep)
+            if X is None:
+                X = _placeholder((a.shape[0], x.shape[1]), x)
+            saved_x = X
+        else:
+            X = _ag(x, pctx) if mode == "ag" else x
+            a, gu = ops.cuda_ops().mm_swiglu(X, w, save_gu=keep)
+            saved_x = x
         if gu is None:
             gu = _placeholder((a.shape[0], 2 * a.shape[1]), a)
-        ctx.save_for_backward(x, w, gu)
+        ctx.save_for_backward(saved_x, w, gu)
         ctx.wref, ctx.pctx, ctx.mode = wref, pctx, mode
         return a
 
@@ -220,23 +235,26 @@ class _GateUpSwiGLU(torch.autograd.Function):
         x, w, gu = ctx.saved_tensors
         pctx, mode, wref = ctx.pctx, ctx.mode, ctx.wref
         dgu = ops.swiglu_bwd(da.contiguous(), gu)
-        dX = ops.mm_nt(dgu, w)
-        dx = _rs(dX, pctx) if mode == "ag" else (_ar(dX, pctx) if mode == "f" else dX)
-        X = _ag(x, pctx) if mode == "ag" else x
+        if ctx.gathered and _use_fused(pctx, dgu, x.shape[0] // pctx.tp_size):
+            from ..ops import fused_tp
+            dx = fused_tp.matmul_reduce_scatter(dgu, w, pctx, transpose_b=True)
+            X = x  # the gathered input the forward kernel saved
+        elif ctx.gathered:
+            dx = _rs(ops.mm_nt(dgu, w), pctx)
+            X = x
+        else:
+            dX = ops.mm_nt(dgu, w)
+            dx = _rs(dX, pctx) if mode == "ag" else (_ar(dX, pctx) if mode == "f" else dX)
+            X = _ag(x, pctx) if mode == "ag" else x
         grads = wref.accumulate(ops.mm_tn_acc, X, dgu)
         return (dx, None, None, None, None, *grads)
 
 
 def gate_up_swiglu_supported(x: torch.Tensor, ffn_local: int, pctx: ParallelContext, mode: str) -> bool:
-    """The one-GEMM SwiGLU path (bf16 compute): CUDA, 8-aligned width, and not a
-    layer whose gate|up GEMM runs as the fused all-gather kernel."""
-    if not (x.is_cuda and ffn_local % 8 == 0):
-        return False
-    if mode == "ag" and pctx.tp_size > 1 and pctx.resources.get("fused_tp", False):
-        from ..ops import fused_tp
-        if fused_tp.supported(x.shape[0], pctx):
-            return False
-    return True
+    """The one-GEMM SwiGLU path (bf16 compute, CUDA, 8-aligned width); with
+    sequence parallelism over more than one GPU it is the fused all-gather
+    kernel's SwiGLU mode."""
+    return x.is_cuda and ffn_local % 8 == 0
 
 
 def gate_up_swiglu(x, wref: WeightRef, pctx: ParallelContext, mode: str, dtype: torch.dtype):

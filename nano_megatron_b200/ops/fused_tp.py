@@ -141,6 +141,29 @@ def all_gather_matmul(x_local, w, pctx: ParallelContext, transpose_b: bool = Fal
     return out
 
 
+def all_gather_matmul_swiglu(x_local, w_gu, pctx: ParallelContext, save_gu: bool = True,
+                             save_gathered: bool = True):
+    """``silu(AG(x) @ w_gate) * (AG(x) @ w_up)`` for ``w_gu = [w_gate | w_up]``
+    ``[K, 2F]`` in one kernel (all-gather, GEMM, SwiGLU epilogue). Returns
+    ``(X, a, gu)``: the private gathered input (None unless ``save_gathered``),
+    the activation ``[M, F]`` and the pre-activation ``[M, 2F]`` (None unless
+    ``save_gu``)."""
+    x_local = x_local.contiguous()
+    m_chunk, k = x_local.shape
+    rows = m_chunk * pctx.tp_size
+    f = w_gu.shape[1] // 2
+    ws = workspace(pctx, x_local.device)
+    ws.ensure(rows * k * 2, 0)
+    a = torch.empty((rows, f), dtype=x_local.dtype, device=x_local.device)
+    gu = torch.empty((rows, 2 * f), dtype=x_local.dtype, device=x_local.device) if save_gu else None
+    saved = torch.empty((rows, k), dtype=x_local.dtype, device=x_local.device) if save_gathered else None
+    K.C.fused_tp_gemm(3, x_local, w_gu, True, a, ws.ptrs, pctx.tp_rank, rows, ws.gather_off, ws.recv_off,
+                      ws.flags_off, ws.next_epoch(), False, K.status_word(x_local.device), TIMEOUT_S,
+                      save_out=saved, gu=gu)
+    K._count()
+    return saved, a, gu
+
+
 def matmul_reduce_scatter(x, w, pctx: ParallelContext, transpose_b: bool = False):
     """``RS(x @ op(w))`` over the sequence (row) dim: returns this rank's rows."""
     x = x.contiguous()

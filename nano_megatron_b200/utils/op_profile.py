@@ -28,6 +28,7 @@ import torch
 # op-layer function -> class in the report
 _CUDA_OPS = {
     "mm_nn": "gemm", "mm_nt": "gemm", "mm_tn_acc": "gemm (weight gradient)",
+    "mm_swiglu": "gemm + swiglu epilogue",
     "rmsnorm": "rmsnorm", "rmsnorm_bwd": "rmsnorm backward",
     "attention": "attention forward", "attention_bwd": "attention backward",
     "swiglu": "swiglu", "swiglu_bwd": "swiglu backward",

@@ -10,6 +10,8 @@ and against the NCCL path:
   queued behind a peer's fused kernel (each rank's grid is only partly
   resident, so work bound to a particular peer CTA would stall until the
   bound);
+* the all-gather -> gate|up GEMM with the SwiGLU epilogue against the plain
+  fused all-gather GEMM followed by the SwiGLU kernel;
 * a TP sequence-parallel GPT step with and without the fused kernels.
 
 Every cross-GPU wait in the kernels is bounded; the tests lower the bound to
@@ -76,6 +78,17 @@ def _check_gemms(rank, world, pctx, fused_tp, full, failures):
             again = fused_tp.matmul_reduce_scatter(a_parts[rank], w, pctx)
             if not torch.equal(again, out):
                 failures.append(f"gemm_rs not repeatable {mc},{k},{n}")
+            if n % 16 == 0:  # w as a gate|up weight: SwiGLU epilogue vs GEMM then SwiGLU
+                from nano_megatron_b200.ops import cuda as KC
+                for save in (True, False):
+                    Xs, a, gu = fused_tp.all_gather_matmul_swiglu(shard, w, pctx, save_gu=save,
+                                                                  save_gathered=save)
+                    if save and (not torch.equal(Xs, x) or _rel(gu, y) > 1e-4):
+                        failures.append(f"ag_swiglu pre-activation {mc},{k},{n}: {_rel(gu, y)}")
+                    if (Xs is None) == save or (gu is None) == save:
+                        failures.append("ag_swiglu optional outputs")
+                    if _rel(a, KC.swiglu(y)) > 1e-4:
+                        failures.append(f"ag_swiglu {mc},{k},{n}: {_rel(a, KC.swiglu(y))}")
 
 
 def _check_ce(rank, world, pctx, fused_tp, full, dev, failures):
