@@ -92,7 +92,8 @@ def _check_gemms(rank, world, pctx, fused_tp, full, failures):
 
 
 def _check_ce(rank, world, pctx, fused_tp, full, dev, failures):
-    for it, (rows, hidden, vocab_local) in enumerate([(512, 256, 1040), (1024, 256, 4000)]):
+    for it, (rows, hidden, vocab_local) in enumerate([(max(512, 128 * world), 256, 1040),
+                                                      (max(1024, 256 * world), 256, 4000)]):
         vocab = vocab_local * world
         xf = full(300 + it, rows, hidden)
         wf = (full(400 + it, vocab, hidden).float() * 0.1).bfloat16()
