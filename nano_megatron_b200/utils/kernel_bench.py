@@ -2,11 +2,18 @@
 
     python -m nano_megatron_b200.utils.kernel_bench attention --seq 8192 --heads 32 [--sdpa]
     python -m nano_megatron_b200.utils.kernel_bench gemm --shapes 8192x12288x4096 [--cublas]
+    python -m nano_megatron_b200.utils.kernel_bench memory [--rows 8192 --hidden 4096 --ffn 14336]
 
 Times each op with CUDA events on the current stream after warm-up and prints
 one JSON line per case. ``--iters 1 --warmup 1`` gives a capture-sized run.
 Attention FLOPs count causal attention as ``4 * S^2 * d * heads / 2`` forward
-and 2.5x that backward.
+and 2.5x that backward. ``memory`` times the memory-bound kernels at the
+headline shapes (one microbatch of 8192 tokens at tp1) and reports the
+algorithmic bytes each must move (every input read once, every output
+written once) over its time, against the measured copy bandwidth of
+``MEASURED_PEAKS.json``; every input is larger than the 126 MB L2, and the L2
+is flushed between iterations by writing a 256 MB buffer (outside the timed
+span).
 """
 
 from __future__ import annotations
@@ -83,6 +90,75 @@ def bench_gemm(args):
         print(json.dumps(line), flush=True)
 
 
+def _time_flushed(fn, iters, warmup):
+    """Mean time of ``fn`` with a 256 MB write between calls (outside the timing)."""
+    scrub = torch.empty(64 << 20, dtype=torch.float32, device="cuda")
+    for _ in range(warmup):
+        fn()
+    total = 0.0
+    for _ in range(iters):
+        scrub.fill_(1.0)
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        fn()
+        end.record()
+        end.synchronize()
+        total += start.elapsed_time(end)
+    return total / iters
+
+
+def bench_memory(args):
+    import os
+    from ..ops import cuda as K
+    from ..ops import reference as R
+    dev = torch.device("cuda")
+    try:
+        with open(os.path.join(os.path.dirname(__file__), "..", "..", "MEASURED_PEAKS.json")) as f:
+            peak, src = json.load(f)["hbm_gbs"], "hbm_gbs of measured"
+    except (OSError, ValueError, KeyError):
+        peak, src = 6650.0, "6.65 TB/s of fallback"
+    T, H, F, heads = args.rows, args.hidden, args.ffn, args.hidden // 128
+    bf = torch.bfloat16
+    x = torch.randn(T, H, device=dev).to(bf)
+    w = torch.rand(H, device=dev) + 0.5
+    _, rstd = K.rmsnorm(x, w, 1e-6)
+    dy = torch.randn_like(x)
+    dw = torch.zeros(H, device=dev)
+    gu = torch.randn(T, 2 * F, device=dev).to(bf)
+    da = torch.randn(T, F, device=dev).to(bf)
+    qkv = torch.randn(T, 3 * H, device=dev).to(bf)
+    cos, sin = R.rope_cache(T, 128, 500000.0, dev)
+    n = args.params
+    p32, g32 = torch.randn(n, device=dev), torch.randn(n, device=dev)
+    m32, v32 = torch.zeros(n, device=dev), torch.zeros(n, device=dev)
+    comp = torch.empty(n, device=dev, dtype=bf)
+    one = torch.ones(1, device=dev)
+    V = args.vocab
+    logits = torch.randn(T, V, device=dev).to(bf)
+    labels = torch.randint(0, V, (T,), device=dev)
+    mx, se, _, _ = K.ce_local_stats(logits, labels, 0, V)
+    B2, B4 = 2, 4
+    cases = [
+        ("rmsnorm fwd", lambda: K.rmsnorm(x, w, 1e-6), T * H * B2 * 2 + T * B4),
+        ("rmsnorm bwd", lambda: K.rmsnorm_bwd(dy, x, w, rstd, dw), T * H * B2 * 3 + T * B4),
+        ("swiglu fwd", lambda: K.swiglu(gu), T * F * B2 * 3),
+        ("swiglu bwd", lambda: K.swiglu_bwd(da, gu), T * F * B2 * 5),
+        ("rope (q and k, in place)", lambda: K.C.rope_inplace(qkv, cos, sin, 1, heads, 128, 1.0),
+         T * 2 * H * B2 * 2 + T * 64 * B4 * 2),
+        ("adamw (fp32 master, moments, bf16 copy)",
+         lambda: K.adamw_flat(p32, g32, m32, v32, comp, one, lr=1e-4, beta1=0.9, beta2=0.999, eps=1e-8,
+                              weight_decay=0.01, step=1), n * (B4 * 4 + B4 * 3 + B2)),
+        ("cross-entropy grad (softmax - onehot, bf16 logits)",
+         lambda: K.ce_grad(logits, labels, 0, mx, se, one, bf), T * V * B2 * 2),
+    ]
+    for name, fn, nbytes in cases:
+        ms = _time_flushed(fn, args.iters, args.warmup)
+        gbs = nbytes / ms / 1e6
+        print(json.dumps({"op": name, "ms": round(ms, 4), "bytes": int(nbytes), "GB/s": round(gbs, 1),
+                          "frac_of_peak": round(gbs / peak, 3), "peak": src}), flush=True)
+    K.check_status(dev)
+
+
 def main(argv=None):
     p = argparse.ArgumentParser()
     sub = p.add_subparsers(dest="what", required=True)
@@ -94,11 +170,17 @@ def main(argv=None):
     pg = sub.add_parser("gemm")
     pg.add_argument("--shapes", nargs="+", default=["8192x12288x4096", "8192x4096x14336"])
     pg.add_argument("--cublas", action="store_true", help="also time torch.matmul (cuBLAS)")
-    for sp in (pa, pg):
+    pm = sub.add_parser("memory")
+    pm.add_argument("--rows", type=int, default=8192)
+    pm.add_argument("--hidden", type=int, default=4096)
+    pm.add_argument("--ffn", type=int, default=14336)
+    pm.add_argument("--vocab", type=int, default=32064, help="LM-head shard width for the CE gradient")
+    pm.add_argument("--params", type=int, default=1 << 28, help="parameters in the AdamW buffer")
+    for sp in (pa, pg, pm):
         sp.add_argument("--iters", type=int, default=5)
         sp.add_argument("--warmup", type=int, default=2)
     args = p.parse_args(argv)
-    {"attention": bench_attention, "gemm": bench_gemm}[args.what](args)
+    {"attention": bench_attention, "gemm": bench_gemm, "memory": bench_memory}[args.what](args)
 
 
 if __name__ == "__main__":
