@@ -24,6 +24,12 @@
 // masked in the epilogue. Requirements: 16-byte aligned bases and row strides
 // (every dim multiple of 8 bf16 elements), N % 8 == 0.
 //
+// Split-K (accumulate mode only): when the output has too few tiles to fill
+// the last wave of CTAs, each tile's K range is cut into `splits` pieces and
+// every (piece, tile) pair is its own work unit; the fp32 reduce-add of the
+// epilogue sums the pieces in L2. The weight gradients of a tensor-parallel
+// rank are such outputs (at tp4 the attention-output gradient is 64 tiles).
+//
 // SwiGLU mode (OUT == 3, forward of the fused gate|up projection): B is the
 // gate|up weight [K][2F]. A tile's four 64-column B boxes come from columns
 // n0, n0+64 of the gate half and F+n0, F+n0+64 of the up half, so the 256
@@ -70,7 +76,8 @@ template <bool A_MN, bool B_MN, int OUT>
 __global__ void __launch_bounds__(THREADS, 1)
 gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                  const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmG,
-                 const __grid_constant__ CUtensorMap tmU, int M, int N, int K, bool save_gu, int* err) {
+                 const __grid_constant__ CUtensorMap tmU, int M, int N, int K, bool save_gu, int splits,
+                 int* err) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* staging = smem + STAGES * STAGE_BYTES;
@@ -89,6 +96,13 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
   const int num_n = SWIGLU ? (F + BN / 2 - 1) / (BN / 2) : (N + BN - 1) / BN;
   const int num_tiles = num_m * num_n;
   const int num_k = (K + BK - 1) / BK;
+  // work unit u: tile u % num_tiles, K piece u / num_tiles (one piece unless split)
+  const int num_units = num_tiles * splits;
+  auto k_range = [&](int u, int& kb0, int& kb1) {
+    const int piece = u / num_tiles;
+    kb0 = (int)((long)num_k * piece / splits);
+    kb1 = (int)((long)num_k * (piece + 1) / splits);
+  };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -117,10 +131,11 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
     tma_prefetch_desc(&tmB);
     int stage = 0;
     uint32_t phase = 0;
-    for (int t = blockIdx.x; t < num_tiles && !*abort_flag; t += gridDim.x) {
-      int tm, tn;
-      tile_coords(t, num_m, num_n, tm, tn);
-      for (int kb = 0; kb < num_k; ++kb) {
+    for (int u = blockIdx.x; u < num_units && !*abort_flag; u += gridDim.x) {
+      int tm, tn, kb0, kb1;
+      tile_coords(u % num_tiles, num_m, num_n, tm, tn);
+      k_range(u, kb0, kb1);
+      for (int kb = kb0; kb < kb1; ++kb) {
         if (!mbar_wait(&empty[stage], phase ^ 1, err)) { *abort_flag = 1; break; }
         uint8_t* a_dst = smem + stage * STAGE_BYTES;
         uint8_t* b_dst = a_dst + A_TILE_BYTES;
@@ -154,11 +169,13 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
     uint32_t phase = 0;
     int acc = 0;
     uint32_t acc_phase = 0;
-    for (int t = blockIdx.x; t < num_tiles && !*abort_flag; t += gridDim.x) {
+    for (int u = blockIdx.x; u < num_units && !*abort_flag; u += gridDim.x) {
       if (!mbar_wait(&tempty[acc], acc_phase ^ 1, err)) { *abort_flag = 1; break; }
       tc_fence_after();
       const uint32_t d_tmem = tmem_base + acc * BN;
-      for (int kb = 0; kb < num_k; ++kb) {
+      int kb0, kb1;
+      k_range(u, kb0, kb1);
+      for (int kb = kb0; kb < kb1; ++kb) {
         if (!mbar_wait(&full[stage], phase, err)) { *abort_flag = 1; break; }
         tc_fence_after();
         const uint32_t a_base = smem_u32(smem + stage * STAGE_BYTES);
@@ -171,7 +188,7 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
                                        : smem_desc_sw128(a_base + kk * 32, 0, 1024);
           const uint64_t b_desc = B_MN ? smem_desc_sw128(b_base + kk * 2048, 8192, 1024)
                                        : smem_desc_sw128(b_base + kk * 32, 0, 1024);
-          mma_bf16_ss(d_tmem, a_desc, b_desc, idesc, (kb | kk) != 0);
+          mma_bf16_ss(d_tmem, a_desc, b_desc, idesc, (kb > kb0) || kk != 0);
         }
         mma_commit(&empty[stage]);
         if (++stage == STAGES) { stage = 0; phase ^= 1; }
@@ -187,10 +204,10 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
     int nbox = 0;
     int acc = 0;
     uint32_t acc_phase = 0;
-    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
+    for (int u = blockIdx.x; u < num_units; u += gridDim.x) {
       if (*abort_flag) break;
       int tm, tn;
-      tile_coords(t, num_m, num_n, tm, tn);
+      tile_coords(u % num_tiles, num_m, num_n, tm, tn);
       if (!mbar_wait(&tfull[acc], acc_phase, err)) { *abort_flag = 1; break; }
       tc_fence_after();
       const int row0 = tm * BM + quarter * 32;
@@ -323,6 +340,25 @@ EncodeTiledFn encode_fn() {
   return fn;
 }
 
+// Pieces per tile for the accumulate mode: the smallest count (up to 8, at
+// least 8 k-blocks per piece) whose last wave of work units is at least 90 %
+// full, else the count with the fullest last wave.
+int split_count(int tiles, int num_k, int sms) {
+  int best = 1;
+  double best_fill = 0.0;
+  for (int s = 1; s <= 8 && (s == 1 || num_k / s >= 8); ++s) {
+    const long units = (long)tiles * s;
+    const long waves = (units + sms - 1) / sms;
+    const double fill = (double)units / (double)(waves * sms);
+    if (fill >= 0.9) return s;
+    if (fill > best_fill + 1e-9) {
+      best_fill = fill;
+      best = s;
+    }
+  }
+  return best;
+}
+
 template <bool A_MN, bool B_MN, int OUT>
 cudaError_t launch(const GemmArgs& g, cudaStream_t stream) {
   auto kernel = gemm_bf16_kernel<A_MN, B_MN, OUT>;
@@ -339,7 +375,9 @@ cudaError_t launch(const GemmArgs& g, cudaStream_t stream) {
   constexpr bool fp32_out = OUT == 1 || OUT == 2;
   const int out_cols = OUT == 3 ? g.N / 2 : g.N;
   const int tiles = ((g.M + BM - 1) / BM) * (OUT == 3 ? (out_cols + BN / 2 - 1) / (BN / 2) : (g.N + BN - 1) / BN);
-  const int grid = tiles < g.num_sms ? tiles : g.num_sms;
+  const int splits = OUT == 2 ? split_count(tiles, (g.K + BK - 1) / BK, g.num_sms) : 1;
+  const int units = tiles * splits;
+  const int grid = units < g.num_sms ? units : g.num_sms;
   CUtensorMap tc, tg, tu;
   if (!make_tmap_out_2d(&tc, g.C, fp32_out, out_cols, g.M, g.ldc * (fp32_out ? 4 : 2), 32))
     return cudaErrorInvalidValue;
@@ -352,7 +390,7 @@ cudaError_t launch(const GemmArgs& g, cudaStream_t stream) {
         !make_tmap_out_2d(&tu, gu + out_cols, false, out_cols, g.M, g.ldgu * 2, 32))
       return cudaErrorInvalidValue;
   }
-  kernel<<<grid, THREADS, SMEM_BYTES, stream>>>(ta, tb, tc, tg, tu, g.M, g.N, g.K, save_gu, g.err);
+  kernel<<<grid, THREADS, SMEM_BYTES, stream>>>(ta, tb, tc, tg, tu, g.M, g.N, g.K, save_gu, splits, g.err);
   return cudaGetLastError();
 }
 

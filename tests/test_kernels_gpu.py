@@ -47,9 +47,12 @@ def test_gemm_nt(M, N, K):
     assert _rel(got, ref) < 5e-3
 
 
-@pytest.mark.parametrize("M,N,K", [(128, 256, 64), (512, 768, 1024), (264, 392, 200), (4096, 1024, 2048)])
+@pytest.mark.parametrize("M,N,K", [(128, 256, 64), (512, 768, 1024), (264, 392, 200), (4096, 1024, 2048),
+                                   (8192, 1024, 1024), (8192, 4096, 1024), (6000, 392, 264)])
 def test_gemm_tn_accumulate(M, N, K):
-    """out[K,N] += a[M,K]^T b[M,N] in fp32 (weight-gradient accumulation)."""
+    """out[K,N] += a[M,K]^T b[M,N] in fp32 (weight-gradient accumulation). The
+    last three shapes have few output tiles and a long reduction, so the kernel
+    splits K into pieces whose partial tiles are summed by the reduce-add."""
     torch.manual_seed(2)
     a = torch.randn(M, K, device=DEV).bfloat16()
     b = torch.randn(M, N, device=DEV).bfloat16()
