@@ -37,16 +37,39 @@ void rmsnorm_fwd(const at::Tensor& x, const at::Tensor& w, at::Tensor& y, at::Te
      "rmsnorm_fwd");
 }
 
-int64_t rmsnorm_bwd_blocks(int64_t rows) { return nmb::rmsnorm_bwd_blocks((int)rows); }
+// s = x + a, y = rmsnorm(s) * w in one pass (s, y, x, a of one dtype; w, rstd fp32)
+void add_rmsnorm_fwd(const at::Tensor& x, const at::Tensor& a, at::Tensor& s_out, const at::Tensor& w, at::Tensor& y,
+                     at::Tensor& rstd, double eps) {
+  need(x, "x"); need(a, "a"); need(s_out, "s"); need(w, "w"); need(y, "y"); need(rstd, "rstd");
+  TORCH_CHECK(w.scalar_type() == at::kFloat && rstd.scalar_type() == at::kFloat, "w, rstd must be fp32");
+  TORCH_CHECK(a.scalar_type() == x.scalar_type() && s_out.scalar_type() == x.scalar_type() &&
+                  y.scalar_type() == x.scalar_type() && a.sizes() == x.sizes() && s_out.sizes() == x.sizes(),
+              "x, a, s and y must match");
+  const at::cuda::CUDAGuard g(x.device());
+  ok(nmb::add_rmsnorm_fwd(x.data_ptr(), a.data_ptr(), s_out.data_ptr(), w.data_ptr<float>(), y.data_ptr(),
+                          rstd.data_ptr<float>(), x.size(0), x.size(1), (float)eps, dtype_tag(x), stream()),
+     "add_rmsnorm_fwd");
+}
 
+int64_t rmsnorm_bwd_blocks(int64_t rows, int64_t max_blocks) {
+  return nmb::rmsnorm_bwd_blocks((int)rows, (int)max_blocks);
+}
+
+// dx = rmsnorm backward of dy (+ dres when given); weight-gradient partials per block
 void rmsnorm_bwd(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& w, const at::Tensor& rstd, at::Tensor& dx,
-                 at::Tensor& partial) {
+                 at::Tensor& partial, const c10::optional<at::Tensor>& dres) {
   need(dy, "dy"); need(x, "x"); need(w, "w"); need(rstd, "rstd"); need(dx, "dx"); need(partial, "partial");
   TORCH_CHECK(partial.size(0) >= nmb::rmsnorm_bwd_blocks(x.size(0)) && partial.size(1) == x.size(1),
               "partial buffer too small");
+  const void* res = nullptr;
+  if (dres.has_value()) {
+    need(*dres, "dres");
+    TORCH_CHECK(dres->scalar_type() == x.scalar_type() && dres->sizes() == x.sizes(), "dres must match x");
+    res = dres->data_ptr();
+  }
   const at::cuda::CUDAGuard g(x.device());
   ok(nmb::rmsnorm_bwd(dy.data_ptr(), x.data_ptr(), w.data_ptr<float>(), rstd.data_ptr<float>(), dx.data_ptr(),
-                      partial.data_ptr<float>(), x.size(0), x.size(1), dtype_tag(x), stream()),
+                      partial.data_ptr<float>(), x.size(0), x.size(1), dtype_tag(x), stream(), res),
      "rmsnorm_bwd");
 }
 
@@ -245,8 +268,11 @@ void softmax_bwd_f32(const at::Tensor& P, const at::Tensor& dP, at::Tensor& dS, 
 
 void register_elementwise(pybind11::module& m) {
   m.def("rmsnorm_fwd", &rmsnorm_fwd);
-  m.def("rmsnorm_bwd", &rmsnorm_bwd);
-  m.def("rmsnorm_bwd_blocks", &rmsnorm_bwd_blocks);
+  m.def("rmsnorm_bwd", &rmsnorm_bwd, pybind11::arg("dy"), pybind11::arg("x"), pybind11::arg("w"),
+        pybind11::arg("rstd"), pybind11::arg("dx"), pybind11::arg("partial"), pybind11::arg("dres") = pybind11::none());
+  m.def("add_rmsnorm_fwd", &add_rmsnorm_fwd);
+  m.def("rmsnorm_bwd_blocks", &rmsnorm_bwd_blocks, pybind11::arg("rows"),
+        pybind11::arg("max_blocks") = nmb::kNormBwdMaxBlocks);
   m.def("reduce_rows_add", &reduce_rows_add);
   m.def("swiglu_fwd", &swiglu_fwd);
   m.def("swiglu_bwd", &swiglu_bwd);

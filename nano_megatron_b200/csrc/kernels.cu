@@ -103,6 +103,66 @@ __global__ void rmsnorm_fwd_kernel(const T* __restrict__ x, const float* __restr
   }
 }
 
+// One block per row (rows in a grid-stride loop): thread t holds columns
+// (t + 256 j) * 8 .. + 8 for j < CH in registers, so the row is read once.
+// With ADD the block first forms the residual sum s = x + a (rounded to the
+// activation type, as a separate add would) and writes it, then normalizes s:
+// the add and the norm that follows it cost one pass. The per-warp sums of
+// squares alternate between two shared slots, one barrier per row.
+constexpr int NORM_FWD_THREADS = 256;
+
+template <typename T, int CH, bool ADD>
+__global__ void __launch_bounds__(NORM_FWD_THREADS)
+rmsnorm_fwd_row_kernel(const T* __restrict__ x, const T* __restrict__ a, T* __restrict__ s_out,
+                       const float* __restrict__ w, T* __restrict__ y, float* __restrict__ rstd, int rows,
+                       int cols, float eps) {
+  __shared__ float red[2][NORM_FWD_THREADS / 32];
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  int parity = 0;
+  for (long row = blockIdx.x; row < rows; row += gridDim.x, parity ^= 1) {
+    float v[CH][8];
+    float ss = 0.f;
+#pragma unroll
+    for (int j = 0; j < CH; ++j) {
+      const int c = (threadIdx.x + j * NORM_FWD_THREADS) * 8;
+      if (c < cols) {
+        V8<T>::load(x + row * cols + c, v[j]);
+        if (ADD) {
+          float av[8];
+          V8<T>::load(a + row * cols + c, av);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) v[j][i] = V8<T>::round(v[j][i] + av[i]);
+          V8<T>::store(s_out + row * cols + c, v[j]);
+        }
+#pragma unroll
+        for (int i = 0; i < 8; ++i) ss += v[j][i] * v[j][i];
+      } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[j][i] = 0.f;
+      }
+    }
+    ss = warp_sum(ss);
+    if (lane == 0) red[parity][warp] = ss;
+    __syncthreads();
+    float total = 0.f;
+#pragma unroll
+    for (int i = 0; i < NORM_FWD_THREADS / 32; ++i) total += red[parity][i];
+    const float r = rsqrtf(total / cols + eps);
+    if (threadIdx.x == 0) rstd[row] = r;
+#pragma unroll
+    for (int j = 0; j < CH; ++j) {
+      const int c = (threadIdx.x + j * NORM_FWD_THREADS) * 8;
+      if (c < cols) {
+        float wv[8];
+        V8<float>::load(w + c, wv);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[j][i] = V8<T>::round(v[j][i] * r) * V8<T>::round(wv[i]);
+        V8<T>::store(y + row * cols + c, v[j]);
+      }
+    }
+  }
+}
+
 constexpr int NORM_BWD_THREADS = 256;
 
 // One block works on one row at a time with all its threads: thread t owns
@@ -111,11 +171,14 @@ constexpr int NORM_BWD_THREADS = 256;
 // (written once at the end, no shared-memory reduction) and the row's
 // x / dy stay in registers between the dot product and dx. One barrier per
 // pair of rows: the per-warp dot partials alternate between two shared slots.
-template <typename T, int CH>
+// RES: dx also receives dres, the gradient that reaches the normalized input
+// through the residual stream (x feeds both the norm and the next residual
+// add), so the two gradient paths are summed in this pass.
+template <typename T, int CH, bool RES>
 __global__ void __launch_bounds__(NORM_BWD_THREADS)
 rmsnorm_bwd_kernel(const T* __restrict__ dy, const T* __restrict__ x, const float* __restrict__ w,
-                   const float* __restrict__ rstd, T* __restrict__ dx, float* __restrict__ dw_partial, int rows,
-                   int cols) {
+                   const float* __restrict__ rstd, const T* __restrict__ dres, T* __restrict__ dx,
+                   float* __restrict__ dw_partial, int rows, int cols) {
   __shared__ float red[2][2 * (NORM_BWD_THREADS / 32)];
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   float wv[CH][8], acc[CH][8];
@@ -183,6 +246,12 @@ rmsnorm_bwd_kernel(const T* __restrict__ dy, const T* __restrict__ x, const floa
           float o[8];
 #pragma unroll
           for (int i = 0; i < 8; ++i) o[i] = r[q] * (gv[q][j][i] * wv[j][i] - xh[q][j][i] * d);
+          if (RES) {
+            float rv[8];
+            V8<T>::load(dres + row * cols + c, rv);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) o[i] += rv[i];
+          }
           V8<T>::store(dx + row * cols + c, o);
         }
       }
@@ -455,9 +524,45 @@ int grid_for(long work, int threads, int cap = 148 * 16) {
 }  // namespace
 
 // ====================================================================== host
+template <typename T, int CH, bool ADD>
+static void launch_norm_fwd(const void* x, const void* a, void* s_out, const float* w, void* y, float* rstd, int rows,
+                            int cols, float eps, cudaStream_t s) {
+  const int grid = rows < 148 * 8 ? rows : 148 * 8;
+  rmsnorm_fwd_row_kernel<T, CH, ADD><<<grid, NORM_FWD_THREADS, 0, s>>>(
+      static_cast<const T*>(x), static_cast<const T*>(a), static_cast<T*>(s_out), w, static_cast<T*>(y), rstd, rows,
+      cols, eps);
+}
+
+template <bool ADD>
+static cudaError_t norm_fwd_rows(const void* x, const void* a, void* s_out, const float* w, void* y, float* rstd,
+                                 int rows, int cols, float eps, int dtype, cudaStream_t s) {
+  const int chunks = (cols + 8 * NORM_FWD_THREADS - 1) / (8 * NORM_FWD_THREADS);
+#define NMB_NF(CH)                                                                                          \
+  {                                                                                                         \
+    if (dtype == 1) launch_norm_fwd<__nv_bfloat16, CH, ADD>(x, a, s_out, w, y, rstd, rows, cols, eps, s);  \
+    else launch_norm_fwd<float, CH, ADD>(x, a, s_out, w, y, rstd, rows, cols, eps, s);                     \
+    return cudaGetLastError();                                                                              \
+  }
+  if (chunks <= 1) NMB_NF(1)
+  if (chunks <= 2) NMB_NF(2)
+  if (chunks <= 4) NMB_NF(4)
+#undef NMB_NF
+  return cudaErrorInvalidValue;
+}
+
+cudaError_t add_rmsnorm_fwd(const void* x, const void* a, void* s_out, const float* w, void* y, float* rstd,
+                            int rows, int cols, float eps, int dtype, cudaStream_t s) {
+  if (cols % 8 || cols > 8 * NORM_FWD_THREADS * 4) return cudaErrorInvalidValue;
+  if (rows <= 0) return cudaSuccess;
+  return norm_fwd_rows<true>(x, a, s_out, w, y, rstd, rows, cols, eps, dtype, s);
+}
+
 cudaError_t rmsnorm_fwd(const void* x, const float* w, void* y, float* rstd, int rows, int cols, float eps, int dtype,
                         cudaStream_t s) {
   if (cols % 8) return cudaErrorInvalidValue;
+  if (rows <= 0) return cudaSuccess;
+  if (cols <= 8 * NORM_FWD_THREADS * 4)  // rows of up to 8192 columns: one block per row, row in registers
+    return norm_fwd_rows<false>(x, nullptr, nullptr, w, y, rstd, rows, cols, eps, dtype, s);
   const int threads = 256, warps = threads / 32;
   const int grid = grid_for((long)rows * 32, threads, 148 * 32);
   (void)warps;
@@ -470,32 +575,40 @@ cudaError_t rmsnorm_fwd(const void* x, const float* w, void* y, float* rstd, int
   return cudaGetLastError();
 }
 
-int rmsnorm_bwd_blocks(int rows) {
+int rmsnorm_bwd_blocks(int rows, int max_blocks) {
   int b = (rows + 7) / 8;  // >= 8 rows per block (one row at a time)
-  return b < 296 ? (b < 1 ? 1 : b) : 296;
+  return b < max_blocks ? (b < 1 ? 1 : b) : max_blocks;
 }
 
-template <typename T, int C>
-static cudaError_t launch_norm_bwd(const void* dy, const void* x, const float* w, const float* rstd, void* dx,
-                                   float* part, int rows, int cols, cudaStream_t s) {
-  const int blocks = rmsnorm_bwd_blocks(rows);
-  rmsnorm_bwd_kernel<T, C><<<blocks, NORM_BWD_THREADS, 0, s>>>(static_cast<const T*>(dy), static_cast<const T*>(x),
-                                                               w, rstd, static_cast<T*>(dx), part, rows, cols);
+template <typename T, int C, bool RES>
+static cudaError_t launch_norm_bwd(const void* dy, const void* x, const float* w, const float* rstd, const void* dres,
+                                   void* dx, float* part, int rows, int cols, int blocks, cudaStream_t s) {
+  rmsnorm_bwd_kernel<T, C, RES><<<blocks, NORM_BWD_THREADS, 0, s>>>(
+      static_cast<const T*>(dy), static_cast<const T*>(x), w, rstd, static_cast<const T*>(dres), static_cast<T*>(dx),
+      part, rows, cols);
   return cudaGetLastError();
 }
 
 cudaError_t rmsnorm_bwd(const void* dy, const void* x, const float* w, const float* rstd, void* dx, float* part,
-                        int rows, int cols, int dtype, cudaStream_t s) {
+                        int rows, int cols, int dtype, cudaStream_t s, const void* dres, int max_blocks) {
   if (cols % 8) return cudaErrorInvalidValue;
   const int chunks = (cols + 8 * NORM_BWD_THREADS - 1) / (8 * NORM_BWD_THREADS);  // 8-column chunks per thread
   if (chunks > 4) return cudaErrorInvalidValue;  // up to 8192 columns
-#define NMB_NORM(C)                                                                                  \
-  return dtype == 1 ? launch_norm_bwd<__nv_bfloat16, C>(dy, x, w, rstd, dx, part, rows, cols, s)      \
-                    : launch_norm_bwd<float, C>(dy, x, w, rstd, dx, part, rows, cols, s);
+  const int blocks = rmsnorm_bwd_blocks(rows, max_blocks);
+#define NMB_NORM_RES(C, RES)                                                                                   \
+  return dtype == 1 ? launch_norm_bwd<__nv_bfloat16, C, RES>(dy, x, w, rstd, dres, dx, part, rows, cols, blocks, s) \
+                    : launch_norm_bwd<float, C, RES>(dy, x, w, rstd, dres, dx, part, rows, cols, blocks, s);
+#define NMB_NORM(C)            \
+  if (dres != nullptr) {       \
+    NMB_NORM_RES(C, true)      \
+  } else {                     \
+    NMB_NORM_RES(C, false)     \
+  }
   if (chunks <= 1) { NMB_NORM(1) }
   if (chunks <= 2) { NMB_NORM(2) }
   NMB_NORM(4)
 #undef NMB_NORM
+#undef NMB_NORM_RES
 }
 
 cudaError_t reduce_rows_add(const float* partial, float* out, int nrows, int cols, cudaStream_t s) {

@@ -13,10 +13,19 @@ namespace nmb {
 // dtype tags: 0 = fp32, 1 = bf16
 cudaError_t rmsnorm_fwd(const void* x, const float* w, void* y, float* rstd, int rows, int cols, float eps,
                         int dtype, cudaStream_t s);
-// dx and per-block weight-gradient partials ([partial_rows, cols] fp32, partial_rows = rmsnorm_bwd_blocks()).
+// Residual add fused with the norm that follows it: s = x + a (rounded to the
+// dtype), y = rmsnorm(s) * w; cols <= 8192.
+cudaError_t add_rmsnorm_fwd(const void* x, const void* a, void* s_out, const float* w, void* y, float* rstd,
+                            int rows, int cols, float eps, int dtype, cudaStream_t s);
+// Default cap on the blocks (and weight-gradient partial rows) of the backward:
+// 2 per SM (4 per SM measured slower: twice the partial rows to reduce).
+constexpr int kNormBwdMaxBlocks = 296;
+// dx and per-block weight-gradient partials ([partial_rows, cols] fp32,
+// partial_rows = rmsnorm_bwd_blocks(rows, max_blocks)); dx += dres when dres is given.
 cudaError_t rmsnorm_bwd(const void* dy, const void* x, const float* w, const float* rstd, void* dx,
-                        float* dw_partial, int rows, int cols, int dtype, cudaStream_t s);
-int rmsnorm_bwd_blocks(int rows);
+                        float* dw_partial, int rows, int cols, int dtype, cudaStream_t s, const void* dres = nullptr,
+                        int max_blocks = kNormBwdMaxBlocks);
+int rmsnorm_bwd_blocks(int rows, int max_blocks = kNormBwdMaxBlocks);
 // out[c] += sum_b partial[b, c]
 cudaError_t reduce_rows_add(const float* partial, float* out, int nrows, int cols, cudaStream_t s);
 

@@ -12,7 +12,7 @@
 //  * Size limits: the kernel handles up to kMaxCols (8192) columns; wider rows
 //    are rejected with NMB_NOALLOC_BAD_ARGUMENT. The array holds
 //    kScratchFloats fp32 values (4.6 MiB). A call needs
-//    rmsnorm_bwd_blocks(rows) * cols of them (at most 296 * cols), so every
+//    rmsnorm_bwd_blocks(rows, 296) * cols of them (at most 296 * cols), so every
 //    `rows` works for cols <= 4096; larger requests are rejected with
 //    NMB_NOALLOC_TOO_LARGE before anything is launched.
 //  * The array lives in this library's device module. With eager module
@@ -43,7 +43,8 @@
 
 namespace {
 
-constexpr long kScratchFloats = 296L * 4096L;
+constexpr int kPartialRows = 296;  // cap on the backward's blocks, i.e. on the partial rows
+constexpr long kScratchFloats = (long)kPartialRows * 4096L;
 constexpr int kMaxCols = 8192;  // 256 threads x 8 columns x 4 chunks in rmsnorm_bwd_kernel
 constexpr int kMaxDevices = 64;
 
@@ -87,12 +88,12 @@ extern "C" int nmb_rmsnorm_bwd_noalloc(const void* dy, const void* x, const floa
   if (!dy || !x || !w || !rstd || !dx || !dweight || rows <= 0 || cols <= 0 || cols % 8 != 0 ||
       cols > kMaxCols || (dtype != 0 && dtype != 1))
     return NMB_NOALLOC_BAD_ARGUMENT;
-  const int blocks = nmb::rmsnorm_bwd_blocks(rows);
+  const int blocks = nmb::rmsnorm_bwd_blocks(rows, kPartialRows);
   if ((long)blocks * cols > kScratchFloats) return NMB_NOALLOC_TOO_LARGE;
   int code = NMB_NOALLOC_OK;
   float* partials = scratch_for_current_device(&code, /*refresh=*/false);
   if (partials == nullptr) return code;
-  cudaError_t err = nmb::rmsnorm_bwd(dy, x, w, rstd, dx, partials, rows, cols, dtype, stream);
+  cudaError_t err = nmb::rmsnorm_bwd(dy, x, w, rstd, dx, partials, rows, cols, dtype, stream, nullptr, kPartialRows);
   if (err == cudaSuccess) err = nmb::reduce_rows_add(partials, dweight, blocks, cols, stream);
   if (err != cudaSuccess) {
     g_last_cuda_error = static_cast<int>(err);

@@ -14,7 +14,7 @@
 //    results; order them on one stream or with events.
 //  * Limits: cols must be a multiple of 8 and at most
 //    nmb_rmsnorm_bwd_noalloc_max_cols() (8192), else NMB_NOALLOC_BAD_ARGUMENT;
-//    rmsnorm_bwd_blocks(rows) * cols (at most 296 * cols) must fit the array,
+//    rmsnorm_bwd_blocks(rows, 296) * cols (at most 296 * cols) must fit the array,
 //    else NMB_NOALLOC_TOO_LARGE. Any row count fits for cols <= 4096.
 //  * Set-up: call nmb_noalloc_prepare() once per device, with that device
 //    current, before the region that must not allocate, and again after a

@@ -322,6 +322,38 @@ def rms_norm(x, weight, eps):
     return _RMSNorm.apply(x, weight, eps)
 
 
+class _AddRMSNorm(torch.autograd.Function):
+    """The residual add after a sublayer and the norm that follows it:
+    ``s = x + a`` and ``h = rmsnorm(s) * w`` in one pass
+    (``nano_megatron/model.py:165-166``). Backward: the norm's input gradient
+    plus the residual-stream gradient of ``s`` in one pass; that sum is the
+    gradient of both ``x`` and ``a``."""
+
+    @staticmethod
+    def forward(ctx, x, a, weight, eps):
+        s, h, rstd = ops.add_rmsnorm(x, a, weight.detach(), eps)
+        ctx.save_for_backward(s, weight, rstd)
+        ctx.main_grad = getattr(weight, "main_grad", None)
+        return s, h
+
+    @staticmethod
+    def backward(ctx, ds, dh):
+        s, weight, rstd = ctx.saved_tensors
+        main_grad = ctx.main_grad
+        if dh is None:  # h unused: the add alone
+            return ds, ds, None, None
+        dx, dw = ops.rmsnorm_bwd(dh.contiguous(), s, weight.detach(), rstd, main_grad,
+                                 None if ds is None else ds.contiguous())
+        if main_grad is not None:
+            _grad_written(main_grad)
+        return dx, dx, (None if main_grad is not None else dw.to(weight.dtype)), None
+
+
+def add_rms_norm(x, a, weight, eps):
+    """``(x + a, rmsnorm(x + a) * weight)`` for 2-D ``x``, ``a`` of one shape."""
+    return _AddRMSNorm.apply(x, a, weight, eps)
+
+
 # ---------------------------------------------------------------- attention
 class _Attention(torch.autograd.Function):
     @staticmethod

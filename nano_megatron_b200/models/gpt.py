@@ -28,7 +28,7 @@ from ..parallel.context import ParallelContext
 from .. import ops
 from .buffers import FlatBuffers
 from .config import GPTConfig, divide
-from .functional import (WeightRef, causal_attention, column_linear, discarded_forward,
+from .functional import (WeightRef, add_rms_norm, causal_attention, column_linear, discarded_forward,
                          gate_up_swiglu, gate_up_swiglu_supported, lm_head_cross_entropy,
                          lm_head_logits, row_linear, swiglu)
 from .layers import (ColumnParallelLinear, RMSNorm, RowParallelLinear,
@@ -120,8 +120,13 @@ class TransformerLayer(nn.Module):
         self.mlp = ParallelMLP(config, ctx)
 
     def forward(self, x, batch, cos, sin, dtype):
-        x = x + self.attn(self.attn_norm(x), batch, cos, sin, dtype)
-        return x + self.mlp(self.mlp_norm(x), dtype)
+        a = self.attn(self.attn_norm(x), batch, cos, sin, dtype)
+        # residual add and the MLP's norm in one pass
+        lead = x.shape[:-1]
+        x, h = add_rms_norm(x.reshape(-1, x.shape[-1]), a.reshape(-1, a.shape[-1]),
+                            self.mlp_norm.weight, self.mlp_norm.eps)
+        x, h = x.view(*lead, -1), h.view(*lead, -1)
+        return x + self.mlp(h, dtype)
 
 
 class ParallelLMHead(nn.Module):

@@ -45,8 +45,12 @@ def rmsnorm(x, weight, eps):
     return _impl(x).rmsnorm(x, weight, eps)
 
 
-def rmsnorm_bwd(dy, x, weight, rstd, wgrad_out):
-    return _impl(x).rmsnorm_bwd(dy, x, weight, rstd, wgrad_out)
+def add_rmsnorm(x, a, weight, eps):
+    return _impl(x).add_rmsnorm(x, a, weight, eps)
+
+
+def rmsnorm_bwd(dy, x, weight, rstd, wgrad_out, dres=None):
+    return _impl(x).rmsnorm_bwd(dy, x, weight, rstd, wgrad_out, dres)
 
 
 def attention(qkv, batch, heads, head_dim, cos, sin):

@@ -191,11 +191,23 @@ def _partial(device, rows, cols):
     return buf
 
 
-def rmsnorm_bwd(dy, x, weight, rstd, wgrad_out):
+def add_rmsnorm(x, a, weight, eps):
+    """``s = x + a`` and ``(rmsnorm(s) * weight, rstd)`` in one pass: ``(s, y, rstd)``."""
+    _dtype_ok(x)
+    x, a = x.contiguous(), a.contiguous()
+    s, y = torch.empty_like(x), torch.empty_like(x)
+    rstd = torch.empty(x.shape[0], dtype=torch.float32, device=x.device)
+    C.add_rmsnorm_fwd(x, a, s, weight.contiguous().float(), y, rstd, float(eps))
+    _count()
+    return s, y, rstd
+
+
+def rmsnorm_bwd(dy, x, weight, rstd, wgrad_out, dres=None):
     dx = torch.empty_like(x)
     nblk = C.rmsnorm_bwd_blocks(x.shape[0])
     part = _partial(x.device, nblk, x.shape[1])
-    C.rmsnorm_bwd(dy.contiguous(), x, weight.contiguous().float(), rstd, dx, part)
+    C.rmsnorm_bwd(dy.contiguous(), x, weight.contiguous().float(), rstd, dx, part,
+                  None if dres is None else dres.contiguous())
     _count(2)
     if wgrad_out is not None:
         C.reduce_rows_add(part, nblk, wgrad_out)

@@ -43,9 +43,17 @@ def rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float):
     return y, rstd.squeeze(-1)
 
 
+def add_rmsnorm(x: torch.Tensor, a: torch.Tensor, weight: torch.Tensor, eps: float):
+    """``s = x + a`` (in ``x.dtype``) and ``rmsnorm(s)``: returns ``(s, y, rstd)``."""
+    s = x + a
+    y, rstd = rmsnorm(s, weight, eps)
+    return s, y, rstd
+
+
 def rmsnorm_bwd(dy: torch.Tensor, x: torch.Tensor, weight: torch.Tensor,
-                rstd: torch.Tensor, wgrad_out: torch.Tensor | None):
-    """Gradient of :func:`rmsnorm`; adds the weight gradient into ``wgrad_out``.
+                rstd: torch.Tensor, wgrad_out: torch.Tensor | None, dres: torch.Tensor | None = None):
+    """Gradient of :func:`rmsnorm`; adds the weight gradient into ``wgrad_out``
+    and, when given, the residual-stream gradient ``dres`` into ``dx``.
 
     Returns ``(dx, dweight)``; ``dweight`` is None when it was accumulated.
     """
@@ -57,10 +65,13 @@ def rmsnorm_bwd(dy: torch.Tensor, x: torch.Tensor, weight: torch.Tensor,
     dw = (dyf * xhat.to(x.dtype).float()).sum(0)
     g = dyf * weight.float()
     dx = r * (g - xhat * (g * xhat).mean(-1, keepdim=True))
+    dx = dx.to(x.dtype)
+    if dres is not None:
+        dx = dx + dres
     if wgrad_out is not None:
         wgrad_out.add_(dw.to(wgrad_out.dtype))
-        return dx.to(x.dtype), None
-    return dx.to(x.dtype), dw
+        return dx, None
+    return dx, dw
 
 
 # --------------------------------------------------------------------- RoPE

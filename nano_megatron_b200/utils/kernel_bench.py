@@ -141,6 +141,9 @@ def bench_memory(args):
     cases = [
         ("rmsnorm fwd", lambda: K.rmsnorm(x, w, 1e-6), T * H * B2 * 2 + T * B4),
         ("rmsnorm bwd", lambda: K.rmsnorm_bwd(dy, x, w, rstd, dw), T * H * B2 * 3 + T * B4),
+        ("residual add + rmsnorm fwd", lambda: K.add_rmsnorm(x, dy, w, 1e-6), T * H * B2 * 4 + T * B4),
+        ("rmsnorm bwd + residual gradient", lambda: K.rmsnorm_bwd(dy, x, w, rstd, dw, dres=dy),
+         T * H * B2 * 4 + T * B4),
         ("swiglu fwd", lambda: K.swiglu(gu), T * F * B2 * 3),
         ("swiglu bwd", lambda: K.swiglu_bwd(da, gu), T * F * B2 * 5),
         ("rope (q and k, in place)", lambda: K.C.rope_inplace(qkv, cos, sin, 1, heads, 128, 1.0),

@@ -29,7 +29,7 @@ import torch
 _CUDA_OPS = {
     "mm_nn": "gemm", "mm_nt": "gemm", "mm_tn_acc": "gemm (weight gradient)",
     "mm_swiglu": "gemm + swiglu epilogue",
-    "rmsnorm": "rmsnorm", "rmsnorm_bwd": "rmsnorm backward",
+    "rmsnorm": "rmsnorm", "rmsnorm_bwd": "rmsnorm backward", "add_rmsnorm": "residual add + rmsnorm",
     "attention": "attention forward", "attention_bwd": "attention backward",
     "swiglu": "swiglu", "swiglu_bwd": "swiglu backward",
     "embedding": "embedding", "embedding_bwd": "embedding backward",

@@ -78,7 +78,7 @@ def test_gemm_strided_column_slice_accumulate():
 
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
-@pytest.mark.parametrize("rows,cols", [(1000, 256), (4096, 4096), (77, 2560)])
+@pytest.mark.parametrize("rows,cols", [(1000, 256), (4096, 4096), (77, 2560), (300, 8192), (64, 12288)])
 def test_rmsnorm(dtype, rows, cols):
     torch.manual_seed(4)
     x = torch.randn(rows, cols, device=DEV).to(dtype)
@@ -87,12 +87,35 @@ def test_rmsnorm(dtype, rows, cols):
     yr, rr = R.rmsnorm(x, w, 1e-6)
     tol = 1e-2 if dtype == torch.bfloat16 else 1e-5
     assert _rel(y, yr) < tol and _rel(rstd, rr) < 1e-5
+    if cols > 8192:  # the backward kernel takes rows of up to 8192 columns
+        return
     dy = torch.randn_like(x)
     wg = torch.zeros(cols, device=DEV)
     dx, _ = KC.rmsnorm_bwd(dy, x, w, rstd, wg)
     wr = torch.zeros(cols, device=DEV)
     dxr, _ = R.rmsnorm_bwd(dy, x, w, rr, wr)
     assert _rel(dx, dxr) < tol and _rel(wg, wr) < (1e-2 if dtype == torch.bfloat16 else 1e-5)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("rows,cols", [(2048, 4096), (77, 2560)])
+def test_add_rmsnorm_and_residual_gradient(dtype, rows, cols):
+    """Residual add fused with the norm (forward), and the norm backward with
+    the residual-stream gradient added to dx, against the unfused reference."""
+    torch.manual_seed(6)
+    x = torch.randn(rows, cols, device=DEV).to(dtype)
+    a = torch.randn(rows, cols, device=DEV).to(dtype)
+    w = torch.rand(cols, device=DEV) + 0.5
+    s, y, rstd = KC.add_rmsnorm(x, a, w, 1e-6)
+    assert torch.equal(s, x + a)  # the same rounding as a separate add
+    yr, rr = R.rmsnorm(x + a, w, 1e-6)
+    tol = 1e-2 if dtype == torch.bfloat16 else 1e-5
+    assert _rel(y, yr) < tol and _rel(rstd, rr) < 1e-5
+    dy, ds = torch.randn_like(x), torch.randn_like(x)
+    wg, wr = torch.zeros(cols, device=DEV), torch.zeros(cols, device=DEV)
+    dx, _ = KC.rmsnorm_bwd(dy, s, w, rstd, wg, dres=ds)
+    dxr, _ = R.rmsnorm_bwd(dy, s, w, rr, wr, dres=ds)
+    assert _rel(dx, dxr) < tol and _rel(wg, wr) < tol
 
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])

@@ -70,7 +70,7 @@ def test_noalloc_rejects_sizes_beyond_the_scratch_array():
     lib = _lib()
     # 20000 rows use the maximum of 296 partial rows; 296 x 8192 floats do not fit.
     cols, rows = 8192, 20000
-    assert _C.rmsnorm_bwd_blocks(rows) * cols > lib.nmb_rmsnorm_bwd_noalloc_scratch_floats()
+    assert _C.rmsnorm_bwd_blocks(rows, 296) * cols > lib.nmb_rmsnorm_bwd_noalloc_scratch_floats()
     x = torch.zeros(rows, cols, device=DEV, dtype=torch.bfloat16)
     w = torch.ones(cols, device=DEV)
     rstd = torch.ones(rows, device=DEV)
@@ -117,7 +117,7 @@ def test_noalloc_rejects_rows_wider_than_its_kernel():
     lib = _lib()
     cols = lib.nmb_rmsnorm_bwd_noalloc_max_cols() + 8
     rows = 16  # few rows: the scratch array alone would have room
-    assert _C.rmsnorm_bwd_blocks(rows) * cols <= lib.nmb_rmsnorm_bwd_noalloc_scratch_floats()
+    assert _C.rmsnorm_bwd_blocks(rows, 296) * cols <= lib.nmb_rmsnorm_bwd_noalloc_scratch_floats()
     x = torch.zeros(rows, cols, device=DEV, dtype=torch.bfloat16)
     w = torch.ones(cols, device=DEV)
     rstd = torch.ones(rows, device=DEV)
