@@ -24,6 +24,15 @@
 // masked in the epilogue. Requirements: 16-byte aligned bases and row strides
 // (every dim multiple of 8 bf16 elements), N % 8 == 0.
 //
+// CTA-pair mode (PAIR, for the large products): a cluster of two CTAs works on
+// one 256x256 tile with cta_group::2 MMAs. Each CTA stages 128 rows of A and
+// 128 columns of B per k-block (32 KB instead of 48 KB, so six stages fit
+// instead of four) with TMA loads whose bytes count on CTA 0's full barrier;
+// CTA 0's MMA warp issues every MMA and its commits arrive on the barrier of
+// both CTAs (free the stage, accumulator ready); each CTA's TMEM holds its 128
+// rows of the accumulator and its epilogue writes them, then arrives on CTA
+// 0's "accumulator free" barrier. No load uses cluster multicast.
+//
 // Split-K (accumulate mode only): when the output has too few tiles to fill
 // the last wave of CTAs, each tile's K range is cut into `splits` pieces and
 // every (piece, tile) pair is its own work unit; the fp32 reduce-add of the
@@ -43,6 +52,7 @@
 
 #include <cuda.h>
 #include <cuda_bf16.h>
+#include <cstdlib>
 #include <cuda_runtime.h>
 
 #include "gemm.cuh"
@@ -61,6 +71,11 @@ constexpr int STAGING_BYTES = 4 * 2 * STG_BUF;  // two buffers per epilogue warp
 constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + STAGING_BYTES + 1024 /*align*/ + 256 /*barriers*/;
 constexpr int THREADS = 192;
 constexpr int GROUP_M = 16;
+// CTA-pair mode: a 256x256 tile per pair; each CTA stages 128 rows of A and
+// 128 columns of B (32 KB per k-block), so six stages fit where one CTA fits four.
+constexpr int PAIR_STAGES = 6;
+constexpr int PAIR_STAGE_BYTES = A_TILE_BYTES + B_TILE_BYTES / 2;
+static_assert(PAIR_STAGES * PAIR_STAGE_BYTES == STAGES * STAGE_BYTES, "both modes use the same shared memory");
 
 __device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int& tm, int& tn) {
   const int span = GROUP_M * num_n;
@@ -72,7 +87,7 @@ __device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int& tm
   tn = r / size;
 }
 
-template <bool A_MN, bool B_MN, int OUT>
+template <bool A_MN, bool B_MN, int OUT, bool PAIR>
 __global__ void __launch_bounds__(THREADS, 1)
 gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                  const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmG,
@@ -80,10 +95,14 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
                  int* err) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* staging = smem + STAGES * STAGE_BYTES;
+  constexpr int ST = PAIR ? PAIR_STAGES : STAGES;            // ring depth
+  constexpr int SB = PAIR ? PAIR_STAGE_BYTES : STAGE_BYTES;  // bytes per stage in this CTA
+  constexpr int TM = PAIR ? 2 * BM : BM;                     // tile rows (per pair / per CTA)
+  constexpr int BN_CTA = PAIR ? BN / 2 : BN;                 // B columns staged by this CTA
+  uint8_t* staging = smem + ST * SB;
   uint64_t* full = reinterpret_cast<uint64_t*>(staging + STAGING_BYTES);
-  uint64_t* empty = full + STAGES;
-  uint64_t* tfull = empty + STAGES;
+  uint64_t* empty = full + ST;
+  uint64_t* tfull = empty + ST;
   uint64_t* tempty = tfull + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -92,8 +111,13 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
   const int lane = threadIdx.x % 32;
   constexpr bool SWIGLU = OUT == 3;
   const int F = N / 2;  // SwiGLU: features per half
-  const int num_m = (M + BM - 1) / BM;
+  const int num_m = (M + TM - 1) / TM;
   const int num_n = SWIGLU ? (F + BN / 2 - 1) / (BN / 2) : (N + BN - 1) / BN;
+  // the pair: CTA `rank` of cluster `first_unit`; units are scheduled per pair
+  const int rank = PAIR ? (int)cluster_ctarank() : 0;
+  const bool leader = rank == 0;
+  const int first_unit = PAIR ? blockIdx.x / 2 : blockIdx.x;
+  const int unit_stride = PAIR ? gridDim.x / 2 : gridDim.x;
   const int num_tiles = num_m * num_n;
   const int num_k = (K + BK - 1) / BK;
   // work unit u: tile u % num_tiles, K piece u / num_tiles (one piece unless split)
@@ -105,23 +129,30 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
   };
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < STAGES; ++s) {
+    for (int s = 0; s < ST; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull[b], 1);
-      mbar_init(&tempty[b], 128);
+      // pair: one arrival per epilogue warp of either CTA (on CTA 0's barrier)
+      mbar_init(&tempty[b], PAIR ? 8 : 128);
     }
     *abort_flag = 0;
     fence_barrier_init();
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, 512);
-    tmem_relinquish();
+    if (PAIR) {
+      tmem_alloc_pair(tmem_slot, 512);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(tmem_slot, 512);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
   __syncthreads();
+  if (PAIR) cluster_sync();  // the peer's barriers exist before anything arrives on them
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
@@ -131,45 +162,57 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
     tma_prefetch_desc(&tmB);
     int stage = 0;
     uint32_t phase = 0;
-    for (int u = blockIdx.x; u < num_units && !*abort_flag; u += gridDim.x) {
+    // A load of this CTA: a 64 x 64 box at (x, y), counted on this CTA's
+    // full barrier, or on the pair leader's in pair mode
+    auto load = [&](uint8_t* dst, const CUtensorMap* map, int s, int x, int y) {
+      if (PAIR) tma_load_2d_pair(dst, map, &full[s], x, y);
+      else tma_load_2d(dst, map, &full[s], x, y);
+    };
+    const int a_row0 = rank * BM;      // this CTA's rows within a tile
+    const int b_col0 = rank * BN_CTA;  // this CTA's columns within a tile
+    for (int u = first_unit; u < num_units && !*abort_flag; u += unit_stride) {
       int tm, tn, kb0, kb1;
       tile_coords(u % num_tiles, num_m, num_n, tm, tn);
       k_range(u, kb0, kb1);
       for (int kb = kb0; kb < kb1; ++kb) {
         if (!mbar_wait(&empty[stage], phase ^ 1, err)) { *abort_flag = 1; break; }
-        uint8_t* a_dst = smem + stage * STAGE_BYTES;
+        uint8_t* a_dst = smem + stage * SB;
         uint8_t* b_dst = a_dst + A_TILE_BYTES;
-        mbar_arrive_expect_tx(&full[stage], STAGE_BYTES);
+        if (leader) mbar_arrive_expect_tx(&full[stage], PAIR ? 2 * SB : SB);  // both CTAs' halves
         const int k0 = kb * BK;
+        const int arow = tm * TM + a_row0;
         if (A_MN) {
           // two 64(m) x 64(k) boxes
-          tma_load_2d(a_dst, &tmA, &full[stage], tm * BM, k0);
-          tma_load_2d(a_dst + 8192, &tmA, &full[stage], tm * BM + 64, k0);
+          load(a_dst, &tmA, stage, arow, k0);
+          load(a_dst + 8192, &tmA, stage, arow + 64, k0);
         } else {
-          tma_load_2d(a_dst, &tmA, &full[stage], k0, tm * BM);
+          load(a_dst, &tmA, stage, k0, arow);
         }
         if (SWIGLU) {
-          // gate columns [n0, n0+128) then up columns [F+n0, F+n0+128)
+          // accumulator columns [0,128) = gate [n0, n0+128), [128,256) = up [F+n0, F+n0+128);
+          // in pair mode CTA 0 stages the gate half and CTA 1 the up half
 #pragma unroll
-          for (int j = 0; j < 4; ++j)
-            tma_load_2d(b_dst + j * 8192, &tmB, &full[stage], (j >> 1) * F + tn * (BN / 2) + 64 * (j & 1), k0);
+          for (int j = 0; j < BN_CTA / 64; ++j) {
+            const int half = PAIR ? rank : (j >> 1);
+            load(b_dst + j * 8192, &tmB, stage, half * F + tn * (BN / 2) + 64 * (j & 1), k0);
+          }
         } else if (B_MN) {
 #pragma unroll
-          for (int j = 0; j < 4; ++j) tma_load_2d(b_dst + j * 8192, &tmB, &full[stage], tn * BN + 64 * j, k0);
+          for (int j = 0; j < BN_CTA / 64; ++j) load(b_dst + j * 8192, &tmB, stage, tn * BN + b_col0 + 64 * j, k0);
         } else {
-          tma_load_2d(b_dst, &tmB, &full[stage], k0, tn * BN);
+          load(b_dst, &tmB, stage, k0, tn * BN + b_col0);
         }
-        if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        if (++stage == ST) { stage = 0; phase ^= 1; }
       }
     }
-  } else if (warp == 1 && lane == 0) {
+  } else if (warp == 1 && lane == 0 && leader) {
     // ------------------------------------------------------------- MMA issue
-    constexpr uint32_t idesc = idesc_bf16_f32(BM, BN, A_MN, B_MN);
+    constexpr uint32_t idesc = idesc_bf16_f32(TM, BN, A_MN, B_MN);
     int stage = 0;
     uint32_t phase = 0;
     int acc = 0;
     uint32_t acc_phase = 0;
-    for (int u = blockIdx.x; u < num_units && !*abort_flag; u += gridDim.x) {
+    for (int u = first_unit; u < num_units && !*abort_flag; u += unit_stride) {
       if (!mbar_wait(&tempty[acc], acc_phase ^ 1, err)) { *abort_flag = 1; break; }
       tc_fence_after();
       const uint32_t d_tmem = tmem_base + acc * BN;
@@ -178,7 +221,7 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
       for (int kb = kb0; kb < kb1; ++kb) {
         if (!mbar_wait(&full[stage], phase, err)) { *abort_flag = 1; break; }
         tc_fence_after();
-        const uint32_t a_base = smem_u32(smem + stage * STAGE_BYTES);
+        const uint32_t a_base = smem_u32(smem + stage * SB);
         const uint32_t b_base = a_base + A_TILE_BYTES;
 #pragma unroll
         for (int kk = 0; kk < BK / 16; ++kk) {
@@ -188,12 +231,15 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
                                        : smem_desc_sw128(a_base + kk * 32, 0, 1024);
           const uint64_t b_desc = B_MN ? smem_desc_sw128(b_base + kk * 2048, 8192, 1024)
                                        : smem_desc_sw128(b_base + kk * 32, 0, 1024);
-          mma_bf16_ss(d_tmem, a_desc, b_desc, idesc, (kb > kb0) || kk != 0);
+          if (PAIR) mma_bf16_ss_pair(d_tmem, a_desc, b_desc, idesc, (kb > kb0) || kk != 0);
+          else mma_bf16_ss(d_tmem, a_desc, b_desc, idesc, (kb > kb0) || kk != 0);
         }
-        mma_commit(&empty[stage]);
-        if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        if (PAIR) mma_commit_pair(&empty[stage]);  // frees the stage in both CTAs
+        else mma_commit(&empty[stage]);
+        if (++stage == ST) { stage = 0; phase ^= 1; }
       }
-      mma_commit(&tfull[acc]);
+      if (PAIR) mma_commit_pair(&tfull[acc]);
+      else mma_commit(&tfull[acc]);
       if (++acc == 2) { acc = 0; acc_phase ^= 1; }
     }
   } else if (warp >= 2) {
@@ -204,13 +250,23 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
     int nbox = 0;
     int acc = 0;
     uint32_t acc_phase = 0;
-    for (int u = blockIdx.x; u < num_units; u += gridDim.x) {
+    // the accumulator of a tile is free again once every epilogue warp read it
+    auto release_acc = [&](int b) {
+      tc_fence_before();
+      if (PAIR) {
+        __syncwarp();
+        if (lane == 0) mbar_arrive_leader(&tempty[b]);
+      } else {
+        mbar_arrive(&tempty[b]);
+      }
+    };
+    for (int u = first_unit; u < num_units; u += unit_stride) {
       if (*abort_flag) break;
       int tm, tn;
       tile_coords(u % num_tiles, num_m, num_n, tm, tn);
       if (!mbar_wait(&tfull[acc], acc_phase, err)) { *abort_flag = 1; break; }
       tc_fence_after();
-      const int row0 = tm * BM + quarter * 32;
+      const int row0 = tm * TM + rank * BM + quarter * 32;
       const uint32_t t_row = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN;
       if (SWIGLU) {
         // One box of a row = 64 bf16 (128 B) in the 128-byte swizzle: stage it
@@ -266,8 +322,7 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
           }
           store_box(&tmC, g, col);
         }
-        tc_fence_before();
-        mbar_arrive(&tempty[acc]);
+        release_acc(acc);
         if (++acc == 2) { acc = 0; acc_phase ^= 1; }
         continue;
       }
@@ -308,8 +363,7 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
         }
         ++nbox;
       }
-      tc_fence_before();
-      mbar_arrive(&tempty[acc]);
+      release_acc(acc);
       if (++acc == 2) { acc = 0; acc_phase ^= 1; }
     }
     // every store / reduce must be complete before the CTA (and its smem) goes
@@ -318,9 +372,11 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
 
   tc_fence_before();
   __syncthreads();
+  if (PAIR) cluster_sync();  // the leader's last MMAs and commits into this CTA are done
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, 512);
+    if (PAIR) tmem_dealloc_pair(tmem_base, 512);
+    else tmem_dealloc(tmem_base, 512);
   }
 }
 
@@ -359,25 +415,29 @@ int split_count(int tiles, int num_k, int sms) {
   return best;
 }
 
-template <bool A_MN, bool B_MN, int OUT>
+template <bool A_MN, bool B_MN, int OUT, bool PAIR>
 cudaError_t launch(const GemmArgs& g, cudaStream_t stream) {
-  auto kernel = gemm_bf16_kernel<A_MN, B_MN, OUT>;
+  auto kernel = gemm_bf16_kernel<A_MN, B_MN, OUT, PAIR>;
   static bool configured = false;
   if (!configured) {
     cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
     if (e != cudaSuccess) return e;
     configured = true;
   }
+  constexpr int TM = PAIR ? 2 * BM : BM;
+  constexpr int BN_CTA = PAIR ? BN / 2 : BN;
   CUtensorMap ta, tb;
   // A: K-major stored [M][K] (lda = row stride), or M-major stored [K][M].
   if (!make_tmap_bf16_2d(&ta, g.A, A_MN ? g.M : g.K, A_MN ? g.K : g.M, g.lda, 64, A_MN ? 64 : BM)) return cudaErrorInvalidValue;
-  if (!make_tmap_bf16_2d(&tb, g.B, B_MN ? g.N : g.K, B_MN ? g.K : g.N, g.ldb, 64, B_MN ? 64 : BN)) return cudaErrorInvalidValue;
+  if (!make_tmap_bf16_2d(&tb, g.B, B_MN ? g.N : g.K, B_MN ? g.K : g.N, g.ldb, 64, B_MN ? 64 : BN_CTA))
+    return cudaErrorInvalidValue;
   constexpr bool fp32_out = OUT == 1 || OUT == 2;
   const int out_cols = OUT == 3 ? g.N / 2 : g.N;
-  const int tiles = ((g.M + BM - 1) / BM) * (OUT == 3 ? (out_cols + BN / 2 - 1) / (BN / 2) : (g.N + BN - 1) / BN);
-  const int splits = OUT == 2 ? split_count(tiles, (g.K + BK - 1) / BK, g.num_sms) : 1;
+  const int tiles = ((g.M + TM - 1) / TM) * (OUT == 3 ? (out_cols + BN / 2 - 1) / (BN / 2) : (g.N + BN - 1) / BN);
+  const int slots = PAIR ? g.num_sms / 2 : g.num_sms;  // concurrent work units
+  const int splits = OUT == 2 ? split_count(tiles, (g.K + BK - 1) / BK, slots) : 1;
   const int units = tiles * splits;
-  const int grid = units < g.num_sms ? units : g.num_sms;
+  const int grid = (units < slots ? units : slots) * (PAIR ? 2 : 1);
   CUtensorMap tc, tg, tu;
   if (!make_tmap_out_2d(&tc, g.C, fp32_out, out_cols, g.M, g.ldc * (fp32_out ? 4 : 2), 32))
     return cudaErrorInvalidValue;
@@ -390,8 +450,43 @@ cudaError_t launch(const GemmArgs& g, cudaStream_t stream) {
         !make_tmap_out_2d(&tu, gu + out_cols, false, out_cols, g.M, g.ldgu * 2, 32))
       return cudaErrorInvalidValue;
   }
-  kernel<<<grid, THREADS, SMEM_BYTES, stream>>>(ta, tb, tc, tg, tu, g.M, g.N, g.K, save_gu, splits, g.err);
-  return cudaGetLastError();
+  if (!PAIR) {
+    kernel<<<grid, THREADS, SMEM_BYTES, stream>>>(ta, tb, tc, tg, tu, g.M, g.N, g.K, save_gu, splits, g.err);
+    return cudaGetLastError();
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid, 1, 1);
+  cfg.blockDim = dim3(THREADS, 1, 1);
+  cfg.dynamicSmemBytes = SMEM_BYTES;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, ta, tb, tc, tg, tu, g.M, g.N, g.K, save_gu, splits, g.err);
+}
+
+// CTA pairs (one 256x256 tile per pair, six-stage rings) for the large
+// products: measured 1513-1583 TFLOP/s against 1399-1451 with one CTA per tile
+// at 8192 x {12288, 28672} x 4096 and 8192 x 4096 x 14336, and 7-18 % faster
+// weight gradients there; at 8192 x 3072 x 4096 or K = 1024 the pair was
+// slower (longer per-tile pipeline fill for the same number of waves).
+// NMB_GEMM_PAIR=0 selects one CTA per tile everywhere.
+bool use_pair(const GemmArgs& g) {
+  static int enabled = -1;
+  if (enabled < 0) {
+    const char* v = getenv("NMB_GEMM_PAIR");
+    enabled = (v != nullptr && v[0] == '0') ? 0 : 1;
+  }
+  return enabled == 1 && g.M >= 2048 && g.N >= 4096 && g.K >= 2048 && g.num_sms >= 2;
+}
+
+template <bool A_MN, bool B_MN, int OUT>
+cudaError_t launch_any(const GemmArgs& g, cudaStream_t stream) {
+  return use_pair(g) ? launch<A_MN, B_MN, OUT, true>(g, stream) : launch<A_MN, B_MN, OUT, false>(g, stream);
 }
 
 }  // namespace
@@ -440,17 +535,17 @@ bool make_tmap_bf16_3d(CUtensorMap* map, const void* base, const uint64_t dims[3
 
 cudaError_t gemm_bf16(const GemmArgs& g, cudaStream_t stream) {
   if (g.M <= 0 || g.N <= 0 || g.K <= 0) return cudaSuccess;
-  if (!g.a_mn && g.b_mn && g.out == OutMode::kBf16) return launch<false, true, 0>(g, stream);
-  if (!g.a_mn && g.b_mn && g.out == OutMode::kF32) return launch<false, true, 1>(g, stream);
-  if (!g.a_mn && !g.b_mn && g.out == OutMode::kBf16) return launch<false, false, 0>(g, stream);
-  if (!g.a_mn && !g.b_mn && g.out == OutMode::kF32) return launch<false, false, 1>(g, stream);
-  if (g.a_mn && g.b_mn && g.out == OutMode::kF32Accumulate) return launch<true, true, 2>(g, stream);
-  if (g.a_mn && g.b_mn && g.out == OutMode::kF32) return launch<true, true, 1>(g, stream);
-  if (!g.a_mn && !g.b_mn && g.out == OutMode::kF32Accumulate) return launch<false, false, 2>(g, stream);
-  if (!g.a_mn && g.b_mn && g.out == OutMode::kF32Accumulate) return launch<false, true, 2>(g, stream);
+  if (!g.a_mn && g.b_mn && g.out == OutMode::kBf16) return launch_any<false, true, 0>(g, stream);
+  if (!g.a_mn && g.b_mn && g.out == OutMode::kF32) return launch_any<false, true, 1>(g, stream);
+  if (!g.a_mn && !g.b_mn && g.out == OutMode::kBf16) return launch_any<false, false, 0>(g, stream);
+  if (!g.a_mn && !g.b_mn && g.out == OutMode::kF32) return launch_any<false, false, 1>(g, stream);
+  if (g.a_mn && g.b_mn && g.out == OutMode::kF32Accumulate) return launch_any<true, true, 2>(g, stream);
+  if (g.a_mn && g.b_mn && g.out == OutMode::kF32) return launch_any<true, true, 1>(g, stream);
+  if (!g.a_mn && !g.b_mn && g.out == OutMode::kF32Accumulate) return launch_any<false, false, 2>(g, stream);
+  if (!g.a_mn && g.b_mn && g.out == OutMode::kF32Accumulate) return launch_any<false, true, 2>(g, stream);
   if (!g.a_mn && g.b_mn && g.out == OutMode::kSwiGLU) {
     if (g.N % 16 != 0) return cudaErrorInvalidValue;  // F % 8 == 0: 16-byte aligned up half
-    return launch<false, true, 3>(g, stream);
+    return launch_any<false, true, 3>(g, stream);
   }
   return cudaErrorInvalidValue;
 }
