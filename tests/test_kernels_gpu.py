@@ -25,8 +25,12 @@ def _rel(a, b):
     return ((a.float() - b.float()).norm() / b.float().norm().clamp_min(1e-12)).item()
 
 
+# shapes with M >= 2048, N >= 4096, K >= 2048 run the CTA-pair kernel (ragged ones too)
+PAIR_SHAPES = [(2048, 4096, 2048), (2304, 4360, 2112)]
+
+
 @pytest.mark.parametrize("M,N,K", [(128, 256, 64), (512, 768, 1024), (300, 264, 200), (2048, 3072, 4096),
-                                   (8, 8, 8), (1000, 1032, 72)])
+                                   (8, 8, 8), (1000, 1032, 72)] + PAIR_SHAPES)
 def test_gemm_nn(M, N, K):
     torch.manual_seed(0)
     a = torch.randn(M, K, device=DEV).bfloat16()
@@ -37,7 +41,8 @@ def test_gemm_nn(M, N, K):
     assert _rel(got, ref) < 5e-3, _rel(got, ref)
 
 
-@pytest.mark.parametrize("M,N,K", [(128, 256, 64), (512, 768, 1024), (300, 264, 200), (4096, 4096, 1024)])
+@pytest.mark.parametrize("M,N,K", [(128, 256, 64), (512, 768, 1024), (300, 264, 200), (4096, 4096, 1024)]
+                         + PAIR_SHAPES)
 def test_gemm_nt(M, N, K):
     torch.manual_seed(1)
     a = torch.randn(M, K, device=DEV).bfloat16()
@@ -48,7 +53,8 @@ def test_gemm_nt(M, N, K):
 
 
 @pytest.mark.parametrize("M,N,K", [(128, 256, 64), (512, 768, 1024), (264, 392, 200), (4096, 1024, 2048),
-                                   (8192, 1024, 1024), (8192, 4096, 1024), (6000, 392, 264)])
+                                   (8192, 1024, 1024), (8192, 4096, 1024), (6000, 392, 264),
+                                   (2048, 4096, 2048), (2112, 4360, 2304), (8192, 4096, 2048)])
 def test_gemm_tn_accumulate(M, N, K):
     """out[K,N] += a[M,K]^T b[M,N] in fp32 (weight-gradient accumulation). The
     last three shapes have few output tiles and a long reduction, so the kernel
@@ -130,7 +136,8 @@ def test_swiglu(dtype):
 
 
 @pytest.mark.parametrize("M,K,F,save", [(1024, 512, 1024, True), (384, 256, 704, True),
-                                         (256, 128, 344, False), (2048, 1024, 3584, False)])
+                                         (256, 128, 344, False), (2048, 1024, 3584, False),
+                                         (2048, 2048, 2048, True), (2304, 2112, 2184, True)])
 def test_swiglu_gemm_epilogue(M, K, F, save):
     """One GEMM with the SwiGLU epilogue against the GEMM + SwiGLU kernels
     (same rounding points) and against fp32 torch; ragged feature counts
