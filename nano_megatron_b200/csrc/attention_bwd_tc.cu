@@ -9,7 +9,7 @@
 //          back into TMEM as bf16)
 //     dV += P^T dO and dK += dS^T Q      (tcgen05 with A from TMEM; the
 //          accumulators stay in TMEM)
-//   dQ kernel (one CTA = 128 queries; loops over the 64-key blocks up to it):
+//   dQ kernel (one CTA = 128 queries; loops over the 128-key blocks up to it):
 //     S = Q K^T, dP = dO V^T, dS = P (dP - D[q]) (back into TMEM), dQ += dS K.
 //
 // The dQ kernel recomputes S and dP instead of having the dK/dV kernel add
@@ -17,12 +17,12 @@
 // a fixed summation order and no fp32 atomic traffic.
 //
 // Both kernels: warp 0 issues TMA loads (tiles straight out of qkv / dO via
-// 3-D tensor maps) through a 4-stage ring, warp 1 issues the MMAs from an event
-// loop, and two elementwise warpgroups (warps 2-5, 6-9) take alternate blocks,
-// each with its own TMEM columns, so one group's exp/convert work overlaps the
-// tensor core's products for the other. The grid lists heads fastest, so the
-// CTAs with the most blocks of every head are dispatched first. Every wait is
-// bounded.
+// 3-D tensor maps) through a ring, warp 1 issues the MMAs from an event loop,
+// and two elementwise warpgroups (warps 2-5, 6-9) do the exp/convert work. In
+// the dK/dV kernel the groups take alternate 64-query blocks, each with its
+// own TMEM columns; in the dQ kernel both groups share every 128-key block
+// (see there). The grid lists heads fastest, so the CTAs with the most blocks
+// of every head are dispatched first. Every wait is bounded.
 // D[q] = rowsum(dO * O) comes from flash_bwd_dot_kernel (attention.cu).
 
 #include <cuda.h>
@@ -319,35 +319,50 @@ flash_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tm_qkv_big, const __gr
 }
 
 // ================================================================= dQ kernel
-// One CTA = 128 queries of one (batch, head), looping over the 64-key blocks
-// up to the diagonal. Two elementwise warpgroups (warps 2-5 and 6-9) take
-// alternate key blocks, each with its own S/dP TMEM columns, so one group's
-// exp/convert work overlaps the tensor core's work for the other; dS goes back
-// into TMEM (bf16, over the dP columns just read) as the A operand of the dQ
-// product. Warp 1 issues the MMAs from an event loop (S/dP of block ns as soon
-// as its K/V stage has landed and block ns-2's dQ product was issued, dQ += dS
-// K of block na as soon as its group published dS), and warp 0 streams K/V
-// through a 4-stage ring. dQ accumulates in TMEM in key-block order
-// (deterministic).
-// smem: Q 32K | dO 32K | K[4] 4x16K | V[4] 4x16K
+// One CTA = 128 queries of one (batch, head), looping over the 128-key blocks
+// up to the diagonal. Per block: S = Q K^T (A = Q held in TMEM) and dP = dO V^T,
+// both M=128 x N=128; dS = P (dP - D[q]) goes back into TMEM as bf16 and is
+// the A operand of dQ += dS K. Both elementwise warpgroups work on every
+// block, group g on keys [64g, 64g + 64) of it. S and dP have barriers of
+// their own: the groups load S and hand its columns back while dP is still on
+// the tensor core, then load dP and hand those back while S of block j + 1
+// runs, so each hand-off round trip (commit, load, release, issue) hides
+// behind the other product instead of idling the tensor core. dS has columns
+// of its own. At M=128 an MMA takes about max(N/2, 32 + N/4) cycles (the 128x16 A
+// tile streams in 32 cycles, from TMEM or shared memory alike), so these
+// N=128 products run at the full rate where N=64 ones reach two thirds of it.
+// Warp 0 streams K/V through a 3-stage ring; Q is staged once in the V slot of
+// stage 2 and copied into TMEM by group 0 before that slot is first filled.
+// Warp 1 issues the MMAs from an event loop. dQ accumulates in TMEM in
+// key-block order (deterministic).
+// smem: dO 32K | [K 32K | V 32K] x 3
+// TMEM columns: S 0 | dP 128 | dQ 256 | dS 384 (bf16 pairs) | Q 448 (bf16 pairs)
 constexpr int Q_THREADS = 320;
-constexpr int Q_STAGES = 4;
-constexpr int Q_OFF_Q = 0, Q_OFF_DO = TILE_BIG, Q_OFF_K = 2 * TILE_BIG, Q_OFF_V = Q_OFF_K + Q_STAGES * TILE_SMALL,
-              Q_OFF_BAR = Q_OFF_V + Q_STAGES * TILE_SMALL;
+constexpr int Q_STAGES = 3;
+constexpr int Q_STAGE = 2 * TILE_BIG;
+constexpr int Q_OFF_DO = 0, Q_OFF_KV = TILE_BIG, Q_OFF_BAR = Q_OFF_KV + Q_STAGES * Q_STAGE;
+constexpr int Q_OFF_QSTAGE = Q_OFF_KV + 2 * Q_STAGE + TILE_BIG;  // V slot of stage 2
 constexpr int Q_SMEM = Q_OFF_BAR + 256 + 1024;
+constexpr uint32_t Q_TM_S = 0, Q_TM_DP = 128, Q_TM_DQ = 256, Q_TM_DS = 384, Q_TM_Q = 448;
+static_assert(Q_SMEM <= 232448, "dQ kernel shared memory");
 
 __global__ void __launch_bounds__(Q_THREADS, 1)
-flash_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tm_qkv_big, const __grid_constant__ CUtensorMap tm_qkv_small,
-                       const __grid_constant__ CUtensorMap tm_do_big, const BwdArgs a) {
+flash_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tm_qkv_big, const __grid_constant__ CUtensorMap tm_do_big,
+                       const BwdArgs a) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Q_OFF_BAR);
-  uint64_t* qdo_full = bars;
-  uint64_t* kv_full = bars + 1;                // [Q_STAGES]
-  uint64_t* kv_empty = kv_full + Q_STAGES;     // [Q_STAGES]
-  uint64_t* st_full = kv_empty + Q_STAGES;     // [2] per group: S and dP ready
-  uint64_t* ds_full = st_full + 2;             // [2] per group: dS in TMEM
-  uint64_t* acc_done = ds_full + 2;
+  uint64_t* qdo_full = bars;                 // Q (staged) and dO landed
+  uint64_t* kv_full = bars + 1;              // [Q_STAGES]
+  uint64_t* kv_empty = kv_full + Q_STAGES;   // [Q_STAGES]
+  uint64_t* s_full = kv_empty + Q_STAGES;    // S of the block ready
+  uint64_t* s_free = s_full + 1;             // S loaded by both groups
+  uint64_t* dp_full = s_free + 1;            // dP of the block ready
+  uint64_t* dp_free = dp_full + 1;           // dP loaded by both groups
+  uint64_t* ds_full = dp_free + 1;           // dS in TMEM
+  uint64_t* ds_empty = ds_full + 1;          // the dQ product that read dS is done
+  uint64_t* q_tmem = ds_empty + 1;           // Q copied into TMEM (its staging slot is free)
+  uint64_t* acc_done = q_tmem + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_done + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -355,7 +370,7 @@ flash_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tm_qkv_big, const __g
   const int nqb = a.S / BIG;
   const int qb = nqb - 1 - blockIdx.y;  // longest rows first (heads vary fastest in the grid)
   const int bh = blockIdx.x, b = bh / a.heads, h = bh % a.heads;
-  const int nblk = 2 * qb + 2;          // 64-key blocks up to the diagonal
+  const int nblk = qb + 1;              // 128-key blocks up to the diagonal
   const int q_col = h * HD, k_col = a.heads * HD + h * HD, v_col = 2 * a.heads * HD + h * HD, do_col = h * HD;
 
   if (threadIdx.x == 0) {
@@ -364,10 +379,13 @@ flash_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tm_qkv_big, const __g
       mbar_init(&kv_full[i], 1);
       mbar_init(&kv_empty[i], 1);
     }
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&st_full[i], 1);
-      mbar_init(&ds_full[i], 128);
-    }
+    mbar_init(s_full, 1);
+    mbar_init(s_free, 256);
+    mbar_init(dp_full, 1);
+    mbar_init(dp_free, 256);
+    mbar_init(ds_full, 256);
+    mbar_init(ds_empty, 1);
+    mbar_init(q_tmem, 128);
     mbar_init(acc_done, 1);
     *abort_flag = 0;
     fence_barrier_init();
@@ -379,7 +397,6 @@ flash_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tm_qkv_big, const __g
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  // TMEM columns: S of group g at 64g, dP|dS of group g at 128 + 64g, dQ at 256
   const uint32_t tmem = *tmem_slot;
   const uint32_t sbase = smem_u32(smem);
 
@@ -388,63 +405,80 @@ flash_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tm_qkv_big, const __g
 #pragma unroll
     for (int st = 0; st < Q_STAGES; ++st) issued[st] = -1;
     mbar_arrive_expect_tx(qdo_full, 2 * TILE_BIG);
-    tma_load_3d(smem + Q_OFF_Q, &tm_qkv_big, qdo_full, q_col, b, qb * BIG);
-    tma_load_3d(smem + Q_OFF_Q + HALF_BIG, &tm_qkv_big, qdo_full, q_col + 64, b, qb * BIG);
+    tma_load_3d(smem + Q_OFF_QSTAGE, &tm_qkv_big, qdo_full, q_col, b, qb * BIG);
+    tma_load_3d(smem + Q_OFF_QSTAGE + HALF_BIG, &tm_qkv_big, qdo_full, q_col + 64, b, qb * BIG);
     tma_load_3d(smem + Q_OFF_DO, &tm_do_big, qdo_full, do_col, b, qb * BIG);
     tma_load_3d(smem + Q_OFF_DO + HALF_BIG, &tm_do_big, qdo_full, do_col + 64, b, qb * BIG);
     for (int j = 0; j < nblk; ++j) {
       const int st = j % Q_STAGES;
       if (!lane_wait(&kv_empty[st], ((j / Q_STAGES) & 1) ^ 1, a.err, abort_flag)) break;
-      uint8_t* kd = smem + Q_OFF_K + st * TILE_SMALL;
-      uint8_t* vd = smem + Q_OFF_V + st * TILE_SMALL;
-      mbar_arrive_expect_tx(&kv_full[st], 2 * TILE_SMALL);
-      tma_load_3d(kd, &tm_qkv_small, &kv_full[st], k_col, b, j * SMALL);
-      tma_load_3d(kd + HALF_SMALL, &tm_qkv_small, &kv_full[st], k_col + 64, b, j * SMALL);
-      tma_load_3d(vd, &tm_qkv_small, &kv_full[st], v_col, b, j * SMALL);
-      tma_load_3d(vd + HALF_SMALL, &tm_qkv_small, &kv_full[st], v_col + 64, b, j * SMALL);
+      // stage 2's V slot held Q until group 0 copied it into TMEM
+      if (j == 2 && !lane_wait(q_tmem, 0, a.err, abort_flag)) break;
+      uint8_t* kd = smem + Q_OFF_KV + st * Q_STAGE;
+      uint8_t* vd = kd + TILE_BIG;
+      mbar_arrive_expect_tx(&kv_full[st], 2 * TILE_BIG);
+      tma_load_3d(kd, &tm_qkv_big, &kv_full[st], k_col, b, j * BIG);
+      tma_load_3d(kd + HALF_BIG, &tm_qkv_big, &kv_full[st], k_col + 64, b, j * BIG);
+      tma_load_3d(vd, &tm_qkv_big, &kv_full[st], v_col, b, j * BIG);
+      tma_load_3d(vd + HALF_BIG, &tm_qkv_big, &kv_full[st], v_col + 64, b, j * BIG);
       issued[st] = (j / Q_STAGES) & 1;
     }
     mbar_wait(qdo_full, 0, nullptr, 1000000000ull);
     for (int st = 0; st < Q_STAGES; ++st)
       if (issued[st] >= 0) mbar_wait(&kv_full[st], issued[st], nullptr, 1000000000ull);
   } else if (warp == 1 && lane == 0) {
-    constexpr uint32_t idesc_s = idesc_bf16_f32(BIG, SMALL, false, false);  // S, dP
-    constexpr uint32_t idesc_q = idesc_bf16_f32(BIG, HD, false, true);      // dQ
-    bool ok = lane_wait(qdo_full, 0, a.err, abort_flag);
-    int ns = 0, na = 0;
+    constexpr uint32_t idesc_s = idesc_bf16_f32(BIG, BIG, false, false);  // S, dP (N = 128 keys)
+    constexpr uint32_t idesc_q = idesc_bf16_f32(BIG, HD, false, true);    // dQ
+    bool ok = lane_wait(qdo_full, 0, a.err, abort_flag) && lane_wait(q_tmem, 0, a.err, abort_flag);
+    int ns = 0, nd = 0, na = 0;  // next S, dP and dQ product to issue
     uint64_t idle_since = 0;
+    // Every barrier here completes once per block in block order, and none
+    // can complete twice before this loop has seen it, so the parity tests
+    // never skip a phase.
     while (ok && na < nblk) {
       bool progressed = false;
-      if (ns < nblk && ns < na + 2) {
-        const int g = ns & 1, st = ns % Q_STAGES;
+      // S(ns) reuses the S columns once both groups have loaded S(ns-1)
+      if (ns < nblk && ns <= nd && (ns == 0 || mbar_try_wait(s_free, (ns - 1) & 1))) {
+        const int st = ns % Q_STAGES;
         if (mbar_try_wait(&kv_full[st], (ns / Q_STAGES) & 1)) {
           tc_fence_after();
-          const uint32_t ks = sbase + Q_OFF_K + st * TILE_SMALL, vs = sbase + Q_OFF_V + st * TILE_SMALL;
+          const uint32_t ks = sbase + Q_OFF_KV + st * Q_STAGE;
 #pragma unroll
-          for (int kk = 0; kk < HD / 16; ++kk) {
-            mma_bf16_ss(tmem + g * SMALL, kmajor_desc(sbase + Q_OFF_Q, kk, HALF_BIG),
-                        kmajor_desc(ks, kk, HALF_SMALL), idesc_s, kk > 0);
-            mma_bf16_ss(tmem + 128 + g * SMALL, kmajor_desc(sbase + Q_OFF_DO, kk, HALF_BIG),
-                        kmajor_desc(vs, kk, HALF_SMALL), idesc_s, kk > 0);
-          }
-          mma_commit(&st_full[g]);
+          for (int kk = 0; kk < HD / 16; ++kk)
+            // A = Q from TMEM (bf16 pairs, 8 columns per k-step), B = K
+            mma_bf16_ts(tmem + Q_TM_S, tmem + Q_TM_Q + kk * 8, kmajor_desc(ks, kk, HALF_BIG), idesc_s, kk > 0);
+          mma_commit(s_full);
           ++ns;
           progressed = true;
         }
       }
-      if (na < ns) {
-        const int g = na & 1, st = na % Q_STAGES;
-        if (mbar_try_wait(&ds_full[g], (na >> 1) & 1)) {
-          tc_fence_after();
-          const uint32_t ks = sbase + Q_OFF_K + st * TILE_SMALL;
+      // dP(nd) after S(nd), once both groups have loaded dP(nd-1)
+      if (nd < ns && (nd == 0 || mbar_try_wait(dp_free, (nd - 1) & 1))) {
+        const int st = nd % Q_STAGES;
+        tc_fence_after();
+        const uint32_t vs = sbase + Q_OFF_KV + st * Q_STAGE + TILE_BIG;
 #pragma unroll
-          for (int kk = 0; kk < SMALL / 16; ++kk)
-            mma_bf16_ts(tmem + 256, tmem + 128 + g * SMALL + kk * 8, smem_desc_sw128(ks + kk * 2048, HALF_SMALL, 1024),
-                        idesc_q, (na > 0 || kk > 0));
-          mma_commit(&kv_empty[st]);
-          ++na;
-          progressed = true;
-        }
+        for (int kk = 0; kk < HD / 16; ++kk)
+          mma_bf16_ss(tmem + Q_TM_DP, kmajor_desc(sbase + Q_OFF_DO, kk, HALF_BIG), kmajor_desc(vs, kk, HALF_BIG),
+                      idesc_s, kk > 0);
+        mma_commit(dp_full);
+        ++nd;
+        progressed = true;
+      }
+      if (na < nd && mbar_try_wait(ds_full, na & 1)) {
+        const int st = na % Q_STAGES;
+        tc_fence_after();
+        const uint32_t ks = sbase + Q_OFF_KV + st * Q_STAGE;
+#pragma unroll
+        for (int kk = 0; kk < BIG / 16; ++kk)
+          // A = dS (bf16 pairs, 8 columns per 16 keys); B = the K block viewed
+          // N-major: [2 d-halves][128 keys][128 B]
+          mma_bf16_ts(tmem + Q_TM_DQ, tmem + Q_TM_DS + kk * 8, smem_desc_sw128(ks + kk * 2048, HALF_BIG, 1024),
+                      idesc_q, (na > 0 || kk > 0));
+        mma_commit(&kv_empty[st]);
+        mma_commit(ds_empty);
+        ++na;
+        progressed = true;
       }
       if (progressed) {
         idle_since = 0;
@@ -462,7 +496,7 @@ flash_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tm_qkv_big, const __g
     }
     mma_commit(acc_done);
   } else if (warp >= 2) {
-    const int g = (warp - 2) / 4;       // elementwise group
+    const int g = (warp - 2) / 4;       // elementwise group: keys [64g, 64g + 64) of each block
     const int quarter = warp & 3;       // TMEM lane quarter this warp may access
     const int r = quarter * 32 + lane;  // query row
     const int q = qb * BIG + r;
@@ -471,24 +505,80 @@ flash_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tm_qkv_big, const __g
     const float lse2 = a.lse2[(long)bh * a.S + q];
     const float dq = a.dvec[(long)bh * a.S + q];
     bool ok = true;
-    for (int j = g, n = 0; j < nblk && ok; j += 2, ++n) {
-      ok = warp_wait(&st_full[g], n & 1, a.err, abort_flag);
-      if (!ok) break;
-      tc_fence_after();
-      float s[SMALL], dp[SMALL];
-      const uint32_t dp_addr = tmem + lane_off + 128 + g * SMALL;
-      ld_two_rows64(tmem + lane_off + g * SMALL, dp_addr, s, dp);
-      const bool diagonal = j * SMALL + SMALL > qb * BIG;
+    if (g == 0) {
+      // Q row r into TMEM as bf16 pairs (column c = elements 2c, 2c+1): the A
+      // operand of S = Q K^T. Row r of a 128B-swizzled half keeps its 16-byte
+      // chunk j at chunk j ^ (r & 7); the 8 rows a quarter-warp reads hit 8
+      // different chunks, so the loads are free of bank conflicts.
+      ok = warp_wait(qdo_full, 0, a.err, abort_flag);
+      if (ok) {
+        const uint8_t* qrow = smem + Q_OFF_QSTAGE + r * 128;
 #pragma unroll
-      for (int c = 0; c < SMALL; ++c) {
-        float pr = fast_exp2(fmaf(s[c], sl2, -lse2));
-        if (diagonal && j * SMALL + c > q) pr = 0.f;
-        dp[c] = pr * (dp[c] - dq);
+        for (int half = 0; half < 2; ++half) {
+          uint32_t u[32];
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const uint4 v = *reinterpret_cast<const uint4*>(qrow + half * HALF_BIG + ((j ^ (r & 7)) << 4));
+            u[4 * j + 0] = v.x;
+            u[4 * j + 1] = v.y;
+            u[4 * j + 2] = v.z;
+            u[4 * j + 3] = v.w;
+          }
+          tmem_st_32x32b_x32(tmem + lane_off + Q_TM_Q + half * 32, u);
+        }
+        tmem_wait_st();
       }
-      st_row64(dp_addr, dp);  // dS (bf16) over the dP columns just read
+      tc_fence_before();
+      mbar_arrive(q_tmem);
+    }
+    for (int j = 0; j < nblk && ok; ++j) {
+      const int k0 = j * BIG + g * SMALL;  // key of this group's first column
+      const bool diagonal = j == qb;
+      float p[SMALL];
+      {
+        ok = warp_wait(s_full, j & 1, a.err, abort_flag);
+        if (!ok) break;
+        tc_fence_after();
+        uint32_t u[2][32];
+        tmem_ld_32x32b_x32(tmem + lane_off + Q_TM_S + g * SMALL, u[0]);
+        tmem_ld_32x32b_x32(tmem + lane_off + Q_TM_S + g * SMALL + 32, u[1]);
+        tmem_wait_ld_regs(u[0]);
+        tmem_wait_ld_regs(u[1]);
+        tc_fence_before();
+        mbar_arrive(s_free);  // the S columns may take block j + 1
+#pragma unroll
+        for (int c = 0; c < SMALL; ++c) {
+          p[c] = fast_exp2(fmaf(__uint_as_float(u[c >> 5][c & 31]), sl2, -lse2));
+          if (diagonal && k0 + c > q) p[c] = 0.f;
+        }
+      }
+      uint32_t u[SMALL / 2];
+      {
+        ok = warp_wait(dp_full, j & 1, a.err, abort_flag);
+        if (!ok) break;
+        tc_fence_after();
+        uint32_t v[2][32];
+        tmem_ld_32x32b_x32(tmem + lane_off + Q_TM_DP + g * SMALL, v[0]);
+        tmem_ld_32x32b_x32(tmem + lane_off + Q_TM_DP + g * SMALL + 32, v[1]);
+        tmem_wait_ld_regs(v[0]);
+        tmem_wait_ld_regs(v[1]);
+        tc_fence_before();
+        mbar_arrive(dp_free);  // the dP columns may take block j + 1
+#pragma unroll
+        for (int c = 0; c < SMALL; c += 2)
+          u[c / 2] = pack_bf16x2(p[c] * (__uint_as_float(v[c >> 5][c & 31]) - dq),
+                                 p[c + 1] * (__uint_as_float(v[(c + 1) >> 5][(c + 1) & 31]) - dq));
+      }
+      if (j > 0) {
+        // dS of block j - 1 must have been read by its dQ product
+        ok = warp_wait(ds_empty, (j - 1) & 1, a.err, abort_flag);
+        if (!ok) break;
+        tc_fence_after();
+      }
+      tmem_st_32x32b_x32(tmem + lane_off + Q_TM_DS + g * (SMALL / 2), u);
       tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(&ds_full[g]);
+      mbar_arrive(ds_full);
     }
     if (ok) ok = warp_wait(acc_done, 0, a.err, abort_flag);
     tc_fence_after();
@@ -497,7 +587,7 @@ flash_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tm_qkv_big, const __g
 #pragma unroll
     for (int c = 0; c < 64; c += 32) {
       uint32_t v[32];
-      tmem_ld_32x32b_x32(tmem + lane_off + 256 + g * 64 + c, v);
+      tmem_ld_32x32b_x32(tmem + lane_off + Q_TM_DQ + g * 64 + c, v);
       tmem_wait_ld_regs(v);
       if (ok) {
 #pragma unroll
@@ -564,7 +654,7 @@ cudaError_t flash_attn_bwd_tc(const __nv_bfloat16* dout, const __nv_bfloat16* qk
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   dim3 grid_q(batch * heads, S / BIG);
-  flash_bwd_dq_tc_kernel<<<grid_q, Q_THREADS, Q_SMEM, stream>>>(qkv_big, qkv_small, do_big, a);
+  flash_bwd_dq_tc_kernel<<<grid_q, Q_THREADS, Q_SMEM, stream>>>(qkv_big, do_big, a);
   return cudaGetLastError();
 }
 

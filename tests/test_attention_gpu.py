@@ -19,7 +19,7 @@ def _rel(a, b):
     return ((a.float() - b.float()).norm() / b.float().norm().clamp_min(1e-12)).item()
 
 
-@pytest.mark.parametrize("S,b,h", [(64, 1, 1), (128, 2, 2), (512, 1, 4), (1024, 2, 3)])
+@pytest.mark.parametrize("S,b,h", [(64, 1, 1), (128, 2, 2), (512, 1, 4), (1024, 2, 3), (2048, 1, 2)])
 def test_flash_attention_fwd_bwd(S, b, h):
     torch.manual_seed(S + b + h)
     d = 128
