@@ -26,9 +26,11 @@ cudaError_t flash_attn_bwd_dot(const __nv_bfloat16* dout, const __nv_bfloat16* o
 
 // tcgen05 backward (dK/dV kernel + dQ kernel, no atomics); dvec holds
 // [2][batch*heads*S] floats: D from flash_attn_bwd_dot, then scratch for
-// lse*log2(e); S must be a multiple of 128.
+// lse*log2(e); S must be a multiple of 128. With cosv/sinv ([S][head_dim/2]
+// fp32) the inverse rotary embedding is applied to dQ and dK as they are
+// stored; null leaves them unrotated.
 cudaError_t flash_attn_bwd_tc(const __nv_bfloat16* dout, const __nv_bfloat16* qkv, const float* lse,
                               const float* dvec, __nv_bfloat16* dqkv, int S, int batch, int heads, int head_dim,
-                              int* err, cudaStream_t stream);
+                              const float* cosv, const float* sinv, int* err, cudaStream_t stream);
 
 }  // namespace nmb

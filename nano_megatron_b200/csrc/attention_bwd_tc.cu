@@ -95,11 +95,57 @@ __device__ __forceinline__ void store_tmem_row(uint32_t taddr, __nv_bfloat16* ds
 }
 
 
+// Columns [c0, c0 + 32) and [c0 + 64, c0 + 96) of a 128-column fp32 TMEM row,
+// times `scale`, as bf16 to the same columns of `dst`. With `cosv` set, the
+// pairs (d, d + 64) are first turned back by the rotary angle of position
+// `pos` (the inverse of the forward's NeoX rotation: x1 c + x2 s, x2 c - x1 s;
+// cos/sin tables [S][64]), so no separate RoPE pass runs over the gradient.
+__device__ __forceinline__ void store_tmem_pairs(uint32_t taddr, int c0, __nv_bfloat16* dst, float scale, bool write,
+                                                 const float* cosv, const float* sinv, long pos) {
+  uint32_t lo[32], hi[32];
+  tmem_ld_32x32b_x32(taddr + c0, lo);
+  tmem_ld_32x32b_x32(taddr + 64 + c0, hi);
+  tmem_wait_ld_regs(lo);
+  tmem_wait_ld_regs(hi);
+  if (!write) return;
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    float o1[8], o2[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      o1[e] = __uint_as_float(lo[8 * k + e]) * scale;
+      o2[e] = __uint_as_float(hi[8 * k + e]) * scale;
+    }
+    if (cosv != nullptr) {
+      const float4* cp = reinterpret_cast<const float4*>(cosv + pos * 64 + c0 + 8 * k);
+      const float4* sp = reinterpret_cast<const float4*>(sinv + pos * 64 + c0 + 8 * k);
+      const float4 ca = cp[0], cb = cp[1], sa = sp[0], sb = sp[1];
+      const float cv[8] = {ca.x, ca.y, ca.z, ca.w, cb.x, cb.y, cb.z, cb.w};
+      const float sv[8] = {sa.x, sa.y, sa.z, sa.w, sb.x, sb.y, sb.z, sb.w};
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const float x1 = o1[e], x2 = o2[e];
+        o1[e] = x1 * cv[e] + x2 * sv[e];
+        o2[e] = x2 * cv[e] - x1 * sv[e];
+      }
+    }
+    uint4 u1, u2;
+    u1.x = pack_bf16x2(o1[0], o1[1]); u1.y = pack_bf16x2(o1[2], o1[3]);
+    u1.z = pack_bf16x2(o1[4], o1[5]); u1.w = pack_bf16x2(o1[6], o1[7]);
+    u2.x = pack_bf16x2(o2[0], o2[1]); u2.y = pack_bf16x2(o2[2], o2[3]);
+    u2.z = pack_bf16x2(o2[4], o2[5]); u2.w = pack_bf16x2(o2[6], o2[7]);
+    *reinterpret_cast<uint4*>(dst + c0 + 8 * k) = u1;
+    *reinterpret_cast<uint4*>(dst + 64 + c0 + 8 * k) = u2;
+  }
+}
+
 struct BwdArgs {
   const float* lse;   // [batch*heads, S]
   const float* lse2;  // lse * log2(e), [batch*heads, S]
   const float* dvec;  // [batch*heads, S]
   __nv_bfloat16* dqkv;
+  const float* cosv;  // rotary tables [S][64] for dQ and dK, or null (no rotation)
+  const float* sinv;
   int S, batch, heads;
   float scale;
   int* err;
@@ -307,7 +353,10 @@ flash_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tm_qkv_big, const __gr
     const long ld = 3L * a.heads * HD;
     __nv_bfloat16* row = a.dqkv + ((long)key * a.batch + b) * ld;
     if (g == 0) store_tmem_row(tmem + lane_off + 256, row + v_col, 1.f, ok);      // dV
-    else store_tmem_row(tmem + lane_off + 384, row + k_col, a.scale, ok);         // dK
+    else {                                                                         // dK
+      store_tmem_pairs(tmem + lane_off + 384, 0, row + k_col, a.scale, ok, a.cosv, a.sinv, key);
+      store_tmem_pairs(tmem + lane_off + 384, 32, row + k_col, a.scale, ok, a.cosv, a.sinv, key);
+    }
   }
 
   tc_fence_before();
@@ -582,25 +631,9 @@ flash_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tm_qkv_big, const __g
     }
     if (ok) ok = warp_wait(acc_done, 0, a.err, abort_flag);
     tc_fence_after();
-    // group g writes columns [64g, 64g + 64) of the dQ row
-    __nv_bfloat16* dst = a.dqkv + ((long)q * a.batch + b) * 3L * a.heads * HD + q_col + g * 64;
-#pragma unroll
-    for (int c = 0; c < 64; c += 32) {
-      uint32_t v[32];
-      tmem_ld_32x32b_x32(tmem + lane_off + Q_TM_DQ + g * 64 + c, v);
-      tmem_wait_ld_regs(v);
-      if (ok) {
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          uint4 u;
-          u.x = pack_bf16x2(__uint_as_float(v[8 * k + 0]) * a.scale, __uint_as_float(v[8 * k + 1]) * a.scale);
-          u.y = pack_bf16x2(__uint_as_float(v[8 * k + 2]) * a.scale, __uint_as_float(v[8 * k + 3]) * a.scale);
-          u.z = pack_bf16x2(__uint_as_float(v[8 * k + 4]) * a.scale, __uint_as_float(v[8 * k + 5]) * a.scale);
-          u.w = pack_bf16x2(__uint_as_float(v[8 * k + 6]) * a.scale, __uint_as_float(v[8 * k + 7]) * a.scale);
-          *reinterpret_cast<uint4*>(dst + c + 8 * k) = u;
-        }
-      }
-    }
+    // group g writes the column pairs (d, d + 64) for d in [32g, 32g + 32) of the dQ row
+    __nv_bfloat16* dst = a.dqkv + ((long)q * a.batch + b) * 3L * a.heads * HD + q_col;
+    store_tmem_pairs(tmem + lane_off + Q_TM_DQ, 32 * g, dst, a.scale, ok, a.cosv, a.sinv, q);
   }
 
   tc_fence_before();
@@ -627,7 +660,7 @@ bool qkv_map(CUtensorMap* m, const void* base, int S, int batch, long cols, uint
 
 cudaError_t flash_attn_bwd_tc(const __nv_bfloat16* dout, const __nv_bfloat16* qkv, const float* lse,
                               const float* dvec, __nv_bfloat16* dqkv, int S, int batch, int heads, int head_dim,
-                              int* err, cudaStream_t stream) {
+                              const float* cosv, const float* sinv, int* err, cudaStream_t stream) {
   if (head_dim != HD || S % BIG != 0) return cudaErrorInvalidValue;
   static bool configured = false;
   if (!configured) {
@@ -648,7 +681,7 @@ cudaError_t flash_attn_bwd_tc(const __nv_bfloat16* dout, const __nv_bfloat16* qk
   const long rows = (long)batch * heads * S;
   float* lse2 = const_cast<float*>(dvec) + rows;
   scale_kernel<<<(int)((rows + 255) / 256), 256, 0, stream>>>(lse, lse2, rows, LOG2E);
-  BwdArgs a{lse, lse2, dvec, dqkv, S, batch, heads, 1.0f / sqrtf((float)HD), err};
+  BwdArgs a{lse, lse2, dvec, dqkv, cosv, sinv, S, batch, heads, 1.0f / sqrtf((float)HD), err};
   dim3 grid_kv(batch * heads, S / BIG);
   flash_bwd_dkdv_kernel<<<grid_kv, KV_THREADS, KV_SMEM, stream>>>(qkv_big, qkv_small, do_small, a);
   cudaError_t e = cudaGetLastError();

@@ -218,8 +218,22 @@ at::Tensor flash_attn_bwd(const at::Tensor& dout, const at::Tensor& qkv, const a
 }
 
 at::Tensor flash_attn_bwd_tc(const at::Tensor& dout, const at::Tensor& qkv, const at::Tensor& out,
-                             const at::Tensor& lse, int64_t batch, int64_t heads, int64_t hd, const at::Tensor& err) {
+                             const at::Tensor& lse, int64_t batch, int64_t heads, int64_t hd, const at::Tensor& err,
+                             const c10::optional<at::Tensor>& cos, const c10::optional<at::Tensor>& sin) {
   need(dout, "dout"); need(qkv, "qkv"); need(out, "out"); need(lse, "lse");
+  TORCH_CHECK(cos.has_value() == sin.has_value(), "cos and sin go together");
+  const float* cosp = nullptr;
+  const float* sinp = nullptr;
+  if (cos.has_value()) {
+    need(*cos, "cos"); need(*sin, "sin");
+    TORCH_CHECK(cos->scalar_type() == at::kFloat && sin->scalar_type() == at::kFloat, "fp32 rotary tables");
+    TORCH_CHECK(cos->size(0) * batch >= qkv.size(0) && cos->size(1) == hd / 2 && sin->sizes() == cos->sizes(),
+                "rotary tables [S][head_dim/2]");
+    cosp = cos->data_ptr<float>();
+    sinp = sin->data_ptr<float>();
+    TORCH_CHECK(reinterpret_cast<uintptr_t>(cosp) % 16 == 0 && reinterpret_cast<uintptr_t>(sinp) % 16 == 0,
+                "rotary tables must be 16-byte aligned");
+  }
   TORCH_CHECK(dout.scalar_type() == at::kBFloat16 && qkv.scalar_type() == at::kBFloat16, "bf16 only");
   const int S = qkv.size(0) / batch;
   auto dqkv = at::empty_like(qkv);
@@ -229,7 +243,7 @@ at::Tensor flash_attn_bwd_tc(const at::Tensor& dout, const at::Tensor& qkv, cons
   ok(nmb::flash_attn_bwd_dot(bf(dout), bf(out), dvec.data_ptr<float>(), S, batch, heads, stream()),
      "flash_attn_bwd_dot");
   ok(nmb::flash_attn_bwd_tc(bf(dout), bf(qkv), lse.data_ptr<float>(), dvec.data_ptr<float>(),
-                            reinterpret_cast<__nv_bfloat16*>(dqkv.data_ptr()), S, batch, heads, hd,
+                            reinterpret_cast<__nv_bfloat16*>(dqkv.data_ptr()), S, batch, heads, hd, cosp, sinp,
                             err.data_ptr<int>(), stream()),
      "flash_attn_bwd_tc");
   return dqkv;
@@ -290,5 +304,7 @@ void register_elementwise(pybind11::module& m) {
   m.def("flash_attn_fwd", &flash_attn_fwd);
   m.def("flash_attn_fwd_tc", &flash_attn_fwd_tc);
   m.def("flash_attn_bwd", &flash_attn_bwd);
-  m.def("flash_attn_bwd_tc", &flash_attn_bwd_tc);
+  m.def("flash_attn_bwd_tc", &flash_attn_bwd_tc, pybind11::arg("dout"), pybind11::arg("qkv"), pybind11::arg("out"),
+        pybind11::arg("lse"), pybind11::arg("batch"), pybind11::arg("heads"), pybind11::arg("hd"), pybind11::arg("err"),
+        pybind11::arg("cos") = pybind11::none(), pybind11::arg("sin") = pybind11::none());
 }

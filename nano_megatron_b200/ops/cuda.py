@@ -286,11 +286,14 @@ def attention_bwd(do, saved, batch, heads, head_dim, cos, sin):
         return _attention_bwd_f32(do.contiguous(), saved, batch, heads, head_dim, cos, sin)
     qkv, o, lse = saved
     if (qkv.shape[0] // batch) % 128 == 0:
-        dqkv = C.flash_attn_bwd_tc(do.contiguous(), qkv, o, lse, batch, heads, head_dim, status_word(qkv.device))
+        # the inverse RoPE is applied to dQ and dK as the kernels store them
+        dqkv = C.flash_attn_bwd_tc(do.contiguous(), qkv, o, lse, batch, heads, head_dim, status_word(qkv.device),
+                                   cos.contiguous(), sin.contiguous())
+        _count(4)  # D = rowsum(dO * O), lse scaling, dK/dV kernel, dQ kernel
     else:
         dqkv = C.flash_attn_bwd(do.contiguous(), qkv, o, lse, batch, heads, head_dim)
-    C.rope_inplace(dqkv, cos, sin, batch, heads, head_dim, -1.0)
-    _count(4 if (qkv.shape[0] // batch) % 128 == 0 else 4)
+        C.rope_inplace(dqkv, cos, sin, batch, heads, head_dim, -1.0)
+        _count(4)
     return dqkv
 
 
