@@ -280,6 +280,20 @@ void softmax_bwd_f32(const at::Tensor& P, const at::Tensor& dP, at::Tensor& dS, 
 
 }  // namespace
 
+// Cycles per tcgen05.mma (M=128, N=n, A from TMEM when ts) over a chain of
+// `iters` products on one SM; synchronizes.
+double mma_cycles(int64_t n, bool ts, int64_t iters, const at::Tensor& err) {
+  need(err, "err");
+  const at::cuda::CUDAGuard g(err.device());
+  auto out = at::zeros({1}, err.options().dtype(at::kLong));
+  ok(nmb::tc_mma_cycles((int)n, ts, (int)iters, reinterpret_cast<long long*>(out.data_ptr<int64_t>()),
+                        err.data_ptr<int>(), stream()),
+     "tc_mma_cycles");
+  const long long cycles = out.item<int64_t>();
+  TORCH_CHECK(cycles > 0, "mma_cycles: the probe's wait ran out");
+  return (double)cycles / (double)(iters / 8 * 8);
+}
+
 void register_elementwise(pybind11::module& m) {
   m.def("rmsnorm_fwd", &rmsnorm_fwd);
   m.def("rmsnorm_bwd", &rmsnorm_bwd, pybind11::arg("dy"), pybind11::arg("x"), pybind11::arg("w"),
@@ -304,6 +318,8 @@ void register_elementwise(pybind11::module& m) {
   m.def("flash_attn_fwd", &flash_attn_fwd);
   m.def("flash_attn_fwd_tc", &flash_attn_fwd_tc);
   m.def("flash_attn_bwd", &flash_attn_bwd);
+  m.def("mma_cycles", &mma_cycles, pybind11::arg("n"), pybind11::arg("ts"), pybind11::arg("iters") = 2048,
+        pybind11::arg("err"));
   m.def("flash_attn_bwd_tc", &flash_attn_bwd_tc, pybind11::arg("dout"), pybind11::arg("qkv"), pybind11::arg("out"),
         pybind11::arg("lse"), pybind11::arg("batch"), pybind11::arg("heads"), pybind11::arg("hd"), pybind11::arg("err"),
         pybind11::arg("cos") = pybind11::none(), pybind11::arg("sin") = pybind11::none());

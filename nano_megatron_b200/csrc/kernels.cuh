@@ -56,4 +56,9 @@ cudaError_t adamw_flat(float* p, const float* g, float* m, float* v, __nv_bfloat
 cudaError_t weighted_sq_norm(const int64_t* ptrs, const int64_t* numels, const double* weights, int nseg,
                              double* out, cudaStream_t s);
 
+// Cycles of one tcgen05.mma (M=128, N = 64/128/256, A from TMEM when `ts`)
+// in a chain of `iters` products on one SM: one CTA writes the chain's total
+// cycles to out[0] (-1 if a wait ran out). tc_probe.cu.
+cudaError_t tc_mma_cycles(int n, bool ts, int iters, long long* out, int* err, cudaStream_t stream);
+
 }  // namespace nmb

@@ -3,6 +3,12 @@
     python -m nano_megatron_b200.utils.kernel_bench attention --seq 8192 --heads 32 [--sdpa]
     python -m nano_megatron_b200.utils.kernel_bench gemm --shapes 8192x12288x4096 [--cublas]
     python -m nano_megatron_b200.utils.kernel_bench memory [--rows 8192 --hidden 4096 --ffn 14336]
+    python -m nano_megatron_b200.utils.kernel_bench mma
+
+``mma`` reports the cycles one tcgen05.mma (M=128, bf16 in, fp32 out) takes
+in a long chain on one SM, for N = 64, 128, 256 and the A operand from shared
+memory (SS) or TMEM (TS), against N/2 cycles of arithmetic at the dense bf16
+rate (8192 FLOP per cycle per SM).
 
 Times each op with CUDA events on the current stream after warm-up and prints
 one JSON line per case. ``--iters 1 --warmup 1`` gives a capture-sized run.
@@ -162,6 +168,22 @@ def bench_memory(args):
     K.check_status(dev)
 
 
+def bench_mma(args):
+    from nano_megatron_b200 import _C
+    from nano_megatron_b200.ops import cuda as K
+
+    dev = torch.device("cuda", 0)
+    err = K.status_word(dev)
+    for ts in (False, True):
+        for n in (64, 128, 256):
+            cyc = _C.mma_cycles(n, ts, args.chain, err)
+            ideal = 128 * n * 16 * 2 / 8192
+            print(json.dumps({"op": "tcgen05.mma", "M": 128, "N": n, "K": 16, "A": "tmem" if ts else "smem",
+                              "cycles": round(cyc, 1), "arith_cycles": ideal, "efficiency": round(ideal / cyc, 3)}),
+                  flush=True)
+    K.check_status(dev)
+
+
 def main(argv=None):
     p = argparse.ArgumentParser()
     sub = p.add_subparsers(dest="what", required=True)
@@ -179,11 +201,13 @@ def main(argv=None):
     pm.add_argument("--ffn", type=int, default=14336)
     pm.add_argument("--vocab", type=int, default=32064, help="LM-head shard width for the CE gradient")
     pm.add_argument("--params", type=int, default=1 << 28, help="parameters in the AdamW buffer")
+    pq = sub.add_parser("mma")
+    pq.add_argument("--chain", type=int, default=2048, help="products per measured chain")
     for sp in (pa, pg, pm):
         sp.add_argument("--iters", type=int, default=5)
         sp.add_argument("--warmup", type=int, default=2)
     args = p.parse_args(argv)
-    {"attention": bench_attention, "gemm": bench_gemm, "memory": bench_memory}[args.what](args)
+    {"attention": bench_attention, "gemm": bench_gemm, "memory": bench_memory, "mma": bench_mma}[args.what](args)
 
 
 if __name__ == "__main__":

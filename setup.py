@@ -25,6 +25,7 @@ SOURCES = [
     "fused_tp.cu", "dp_reduce.cu",
     "noalloc.cu",
     "fp32.cu",
+    "tc_probe.cu",
 ]
 
 NVCC_FLAGS = [

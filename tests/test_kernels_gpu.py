@@ -294,3 +294,16 @@ def test_bounded_peer_wait_times_out_into_the_status_word():
     assert torch.equal(bufs[0], torch.ones(n, device=DEV))  # gave up before touching data
     KC.check_status(DEV)  # cleared; the context still works
     assert float((bufs[0] + 1).sum()) == 2.0 * n
+
+
+def test_tcgen05_mma_cycle_probe():
+    """The one-SM tcgen05.mma cycle probe runs and orders the shapes sensibly:
+    a wider product never takes fewer cycles, and N=128 is near its 64-cycle
+    arithmetic time."""
+    from nano_megatron_b200 import _C
+    err = KC.status_word(DEV)
+    for ts in (False, True):
+        c64, c128, c256 = (_C.mma_cycles(n, ts, 1024, err) for n in (64, 128, 256))
+        assert 32 <= c64 <= c128 <= c256, (ts, c64, c128, c256)
+        assert 60 <= c128 <= 90, (ts, c128)
+    KC.check_status(DEV)
