@@ -40,6 +40,29 @@ def build_rope_cache(seq_len, head_dim, device, base=10000.0):
     return ops.rope_cache(seq_len, head_dim, base, device)
 
 
+def apply_rope(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
+    """NeoX rotary embedding of ``x [..., s, head_dim]`` (positions on dim -2).
+
+    The two halves ``(a, b)`` of the last dimension become
+    ``(a cos - b sin, b cos + a sin)`` with the first ``s`` rows of the
+    ``[seq, head_dim/2]`` tables of :func:`build_rope_cache`; the result has the
+    promoted dtype of ``x`` and the tables. The model itself rotates q/k inside
+    its attention op (and un-rotates the gradient inside the backward kernels);
+    this is the standalone form for callers that hold separate q/k tensors
+    (reference ``nano_megatron/model.py:84-89``, ``[b, heads, s, head_dim]``).
+    """
+    s, half = x.shape[-2], x.shape[-1] // 2
+    dt = torch.promote_types(x.dtype, cos.dtype)
+    c = cos[:s].to(dt)
+    sn = sin[:s].to(dt)
+    a = x[..., :half].to(dt)
+    b = x[..., half:].to(dt)
+    out = torch.empty(x.shape, dtype=dt, device=x.device)
+    torch.addcmul(a * c, b, sn, value=-1.0, out=out[..., :half])
+    torch.addcmul(b * c, a, sn, out=out[..., half:])
+    return out
+
+
 def layers_for_stage(n_layer: int, pp_size: int, pp_rank: int) -> tuple[int, int]:
     """Contiguous, equal split of the layers over the pipeline stages."""
     per_stage = divide(n_layer, pp_size)

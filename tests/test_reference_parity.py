@@ -71,3 +71,22 @@ def test_training_steps_match(ref):
         torch.testing.assert_close(sum(l2), sum(l1), rtol=1e-5, atol=1e-6)
     for p1, p2 in zip(r.parameters(), m.parameters()):
         torch.testing.assert_close(p2, p1, rtol=1e-4, atol=1e-5)
+
+
+def test_state_dicts_load_both_ways(ref):
+    """A reference model's state dict loads into this model with strict key and
+    shape checks, and the other way round; the loaded models agree."""
+    model_mod, _ = ref
+    from nano_megatron_b200.models import GPT, GPTConfig
+    kw = dict(vocab_size=64, n_layer=2, n_head=4, n_embd=32, seq_len=8)
+    torch.manual_seed(1)
+    r = model_mod.GPT(model_mod.GPTConfig(**kw))
+    torch.manual_seed(2)
+    m = GPT(GPTConfig(**kw))
+    m.load_state_dict(r.state_dict(), strict=True)
+    x = torch.randint(0, 64, (2, 8))
+    torch.testing.assert_close(m(x), r(x), rtol=0, atol=0)
+    torch.manual_seed(3)
+    m2 = GPT(GPTConfig(**kw))
+    r.load_state_dict(m2.state_dict(), strict=True)
+    torch.testing.assert_close(r(x), m2(x), rtol=0, atol=0)
