@@ -28,6 +28,13 @@ particular CTA of a peer being resident), every gathered row and every summed
 partial read is the current call's data from the right rank (workspace reuse
 across calls never lets a fast rank overwrite what a slow one still reads),
 and every tile is computed exactly once per call.
+
+Inside a CTA, the producer hands claimed tiles to the MMA warp and the
+epilogue through a small queue (``qfull`` / ``qempty`` with two consumers,
+then a double-buffered ``ep_tile`` and a named barrier for the epilogue
+warps); ``test_tile_queue`` checks that no queue slot or ``ep_tile`` entry is
+overwritten before every reader saw it and that both consumers see the claimed
+sequence.
 """
 
 import random
@@ -201,6 +208,122 @@ def test_model_catches_a_missing_ready_wait(monkeypatch):
     for seed in range(40):
         try:
             simulate(seed, 3, SEQUENCES["back-to-back"], slices=4, tiles_per_chunk=2, max_slots=2)
+        except AssertionError:
+            caught += 1
+    assert caught > 0
+
+
+# ------------------------------------------------- intra-CTA tile queue
+class QBarrier:
+    def __init__(self, name, count=1):
+        self.name, self.count, self.pending, self.completed = name, count, count, 0
+
+    def arrive(self):
+        self.pending -= 1
+        if self.pending == 0:
+            self.completed += 1
+            self.pending = self.count
+
+    def poll(self, k):
+        assert self.completed in (k, k + 1), f"{self.name}: waiting for completion {k}, {self.completed} completed"
+        return (self.completed & 1) != (k & 1)
+
+
+def queue_cta(seed, claims, queue=4, warps=4, broken=None):
+    """The producer hands claimed tiles (then -1) through a ``queue``-slot ring
+    to the MMA warp and the epilogue leader (``qempty`` expects both); the
+    leader passes each to the epilogue warps through ``ep_tile[it & 1]`` and a
+    named barrier per iteration. ``broken``: "one_consumer" arms qempty for one
+    arrival; "single_ep_tile" uses one ep_tile entry."""
+    rng = random.Random(seed)
+    qfull = [QBarrier(f"qfull{s}") for s in range(queue)]
+    qempty = [QBarrier(f"qempty{s}", 1 if broken == "one_consumer" else 2) for s in range(queue)]
+    tq = [None] * queue
+    readers = [set() for _ in range(queue)]   # who read the current content of a slot
+    ep_tile, ep_seen = [None, None], [set(), set()]
+    got = {"mma": [], "ep": [[] for _ in range(warps)]}
+    arrived = [0]                              # named barrier: arrivals of the current generation
+    generation = [0]
+
+    def wait(bar, k):
+        while not bar.poll(k):
+            yield
+
+    def producer():
+        for it, t in enumerate(claims + [-1]):
+            s = it % queue
+            if it >= queue:
+                yield from wait(qempty[s], it // queue - 1)
+            assert tq[s] is None or readers[s] >= {"mma", "ep"}, f"queue slot {s} overwritten before both read it"
+            tq[s], readers[s] = t, set()
+            qfull[s].arrive()
+            yield
+
+    def mma():
+        for it in range(len(claims) + 1):
+            s = it % queue
+            yield from wait(qfull[s], it // queue)
+            t = tq[s]
+            readers[s].add("mma")
+            qempty[s].arrive()
+            if t < 0:
+                return
+            got["mma"].append(t)
+            yield
+
+    def bar_sync():
+        gen = generation[0]
+        arrived[0] += 1
+        if arrived[0] == warps:
+            arrived[0] = 0
+            generation[0] += 1
+        while generation[0] == gen:
+            yield
+
+    def epilogue(w):
+        for it in range(len(claims) + 1):
+            b = 0 if broken == "single_ep_tile" else it & 1
+            if w == 0:
+                s = it % queue
+                yield from wait(qfull[s], it // queue)
+                nxt = tq[s]
+                readers[s].add("ep")
+                qempty[s].arrive()
+                assert ep_tile[b] is None or ep_seen[b] == set(range(warps)), "ep_tile overwritten before every warp read it"
+                ep_tile[b], ep_seen[b] = nxt, set()
+            yield from bar_sync()
+            t = ep_tile[b]
+            ep_seen[b].add(w)
+            if t < 0:
+                return
+            got["ep"][w].append(t)
+            yield
+
+    roles = [producer(), mma()] + [epilogue(w) for w in range(warps)]
+    for _ in range(100000):
+        if not roles:
+            break
+        r = rng.choice(roles)
+        try:
+            next(r)
+        except StopIteration:
+            roles.remove(r)
+    assert not roles, "the queue deadlocked"
+    assert got["mma"] == claims and all(g == claims for g in got["ep"])
+
+
+@pytest.mark.parametrize("n", [0, 1, 3, 4, 9, 17])
+def test_tile_queue(n):
+    for seed in range(30):
+        queue_cta(seed, list(range(10, 10 + n)))
+
+
+@pytest.mark.parametrize("broken", ["one_consumer", "single_ep_tile"])
+def test_tile_queue_checker_catches_a_broken_protocol(broken):
+    caught = 0
+    for seed in range(40):
+        try:
+            queue_cta(seed, list(range(12)), broken=broken)
         except AssertionError:
             caught += 1
     assert caught > 0
