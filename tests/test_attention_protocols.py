@@ -30,6 +30,11 @@ import random
 
 import pytest
 
+from tests._kernel_constants import constant
+
+Q_STAGES = constant("attention_bwd_tc.cu", "Q_STAGES")
+KV_STAGES = constant("attention_bwd_tc.cu", "KV_STAGES")
+
 
 class Barrier:
     def __init__(self, name, count):
@@ -104,7 +109,7 @@ def run(machine, roles, max_steps=100000):
 
 
 # ---------------------------------------------------------------- dQ kernel
-def dq_kernel(rng, nblk, stages=3, broken=None):
+def dq_kernel(rng, nblk, stages=Q_STAGES, broken=None):
     """128-key blocks, both groups on every block, separate S and dP hand-offs,
     dS in columns of its own, Q staged in the V slot of stage 2 until copied
     into TMEM. ``broken``: "s_free" issues S(j+1) without waiting for both
@@ -203,7 +208,7 @@ def dq_kernel(rng, nblk, stages=3, broken=None):
 
 
 # ------------------------------------------------------------ dK / dV kernel
-def dkdv_kernel(rng, nblk, stages=4, ahead=2):
+def dkdv_kernel(rng, nblk, stages=KV_STAGES, ahead=2):
     """64-query blocks taken alternately by two groups, each with its own
     S^T/dP^T columns (P^T/dS^T written over them); S^T/dP^T of block ns are
     issued while ns < na + ``ahead`` (the kernel uses 2: the same group's

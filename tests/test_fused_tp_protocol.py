@@ -42,6 +42,10 @@ import sys
 
 import pytest
 
+from tests._kernel_constants import constant
+
+K_QUEUE = constant("fused_tp.cu", "kQueue")
+
 AG, RS = "ag", "rs"
 
 
@@ -229,7 +233,7 @@ class QBarrier:
         return (self.completed & 1) != (k & 1)
 
 
-def queue_cta(seed, claims, queue=4, warps=4, broken=None):
+def queue_cta(seed, claims, queue=K_QUEUE, warps=4, broken=None):
     """The producer hands claimed tiles (then -1) through a ``queue``-slot ring
     to the MMA warp and the epilogue leader (``qempty`` expects both); the
     leader passes each to the epilogue warps through ``ep_tile[it & 1]`` and a

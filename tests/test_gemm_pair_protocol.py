@@ -26,6 +26,10 @@ import random
 
 import pytest
 
+from tests._kernel_constants import constant
+
+PAIR_STAGES = constant("gemm.cu", "PAIR_STAGES")
+
 
 class Barrier:
     def __init__(self, name, count):
@@ -175,7 +179,8 @@ def simulate(seed, units, kblocks, stages, broken=None):
     assert multiplied == [(u, kb) for u in range(units) for kb in range(kblocks)]
 
 
-@pytest.mark.parametrize("units,kblocks,stages", [(1, 1, 6), (3, 2, 6), (5, 7, 6), (4, 13, 6), (6, 3, 2)])
+@pytest.mark.parametrize("units,kblocks,stages", [(1, 1, PAIR_STAGES), (3, 2, PAIR_STAGES), (5, 7, PAIR_STAGES),
+                                                  (4, 13, PAIR_STAGES), (6, 3, 2)])
 def test_gemm_pair_handshake(units, kblocks, stages):
     for seed in range(25):
         simulate(seed + 31 * units + kblocks, units, kblocks, stages)
