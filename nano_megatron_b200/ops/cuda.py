@@ -268,9 +268,15 @@ def _attention_bwd_f32(do, saved, batch, heads, head_dim, cos, sin):
 def attention(qkv, batch, heads, head_dim, cos, sin, inplace=False):
     """RoPE + causal flash attention. With ``inplace`` the rotation is applied
     to ``qkv`` itself (the model passes its private QKV GEMM output). fp32
-    inputs take the exact-fp32 materialized path."""
+    inputs take the exact-fp32 materialized path; so do bf16 inputs whose head
+    size the flash kernels do not cover (they are built for 128), upcast and
+    with the output cast back: any head size that is a multiple of 16 runs,
+    at O(S^2) memory per (batch, head) pair."""
     if qkv.dtype == torch.float32:
         return _attention_f32(qkv, batch, heads, head_dim, cos, sin)
+    if head_dim != 128:
+        o, saved = _attention_f32(qkv.float(), batch, heads, head_dim, cos, sin)
+        return o.to(qkv.dtype), saved
     qkv = qkv.contiguous() if inplace else qkv.clone(memory_format=torch.contiguous_format)
     C.rope_inplace(qkv, cos, sin, batch, heads, head_dim, 1.0)
     if (qkv.shape[0] // batch) % 128 == 0:
@@ -282,8 +288,9 @@ def attention(qkv, batch, heads, head_dim, cos, sin, inplace=False):
 
 
 def attention_bwd(do, saved, batch, heads, head_dim, cos, sin):
-    if len(saved) == 2:
-        return _attention_bwd_f32(do.contiguous(), saved, batch, heads, head_dim, cos, sin)
+    if len(saved) == 2:  # the materialized path (fp32, or bf16 with a head size other than 128)
+        dqkv = _attention_bwd_f32(do.float().contiguous(), saved, batch, heads, head_dim, cos, sin)
+        return dqkv if do.dtype == torch.float32 else dqkv.to(do.dtype)
     qkv, o, lse = saved
     if (qkv.shape[0] // batch) % 128 == 0:
         # the inverse RoPE is applied to dQ and dK as the kernels store them
