@@ -268,13 +268,14 @@ def _attention_bwd_f32(do, saved, batch, heads, head_dim, cos, sin):
 def attention(qkv, batch, heads, head_dim, cos, sin, inplace=False):
     """RoPE + causal flash attention. With ``inplace`` the rotation is applied
     to ``qkv`` itself (the model passes its private QKV GEMM output). fp32
-    inputs take the exact-fp32 materialized path; so do bf16 inputs whose head
-    size the flash kernels do not cover (they are built for 128), upcast and
-    with the output cast back: any head size that is a multiple of 16 runs,
-    at O(S^2) memory per (batch, head) pair."""
+    inputs take the exact-fp32 materialized path; so do bf16 inputs the flash
+    kernels do not cover (head size other than 128, or a sequence length that
+    is not a multiple of 64), upcast and with the output cast back: any head
+    size that is a multiple of 16 and any length run, at O(S^2) memory per
+    (batch, head) pair."""
     if qkv.dtype == torch.float32:
         return _attention_f32(qkv, batch, heads, head_dim, cos, sin)
-    if head_dim != 128:
+    if head_dim != 128 or (qkv.shape[0] // batch) % 64 != 0:
         o, saved = _attention_f32(qkv.float(), batch, heads, head_dim, cos, sin)
         return o.to(qkv.dtype), saved
     qkv = qkv.contiguous() if inplace else qkv.clone(memory_format=torch.contiguous_format)

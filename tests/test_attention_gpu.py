@@ -94,13 +94,13 @@ def test_tcgen05_backward_matches_mma_sync_backward(S, b, h):
         assert _rel(b_, a_) < 2e-2, (name, _rel(b_, a_))
 
 
-@pytest.mark.parametrize("d", [32, 64])
-def test_attention_other_head_sizes(d):
-    """bf16 attention with a head size the flash kernels do not cover (they
-    are built for 128) runs the exact materialized path and matches the fp32
-    reference, forward and backward."""
-    torch.manual_seed(d)
-    S, b, h = 256, 2, 3
+@pytest.mark.parametrize("S,d", [(256, 32), (256, 64), (100, 128), (72, 128)])
+def test_attention_other_head_sizes(S, d):
+    """bf16 attention the flash kernels do not cover (head size other than 128,
+    or a length that is not a multiple of 64) runs the exact materialized path
+    and matches the fp32 reference, forward and backward."""
+    torch.manual_seed(d + S)
+    b, h = 2, 3
     cos, sin = R.rope_cache(S, d, 10000.0, DEV)
     qkv = torch.randn(S * b, 3 * h * d, device=DEV).bfloat16()
     o, saved = KC.attention(qkv, b, h, d, cos, sin)
