@@ -63,6 +63,30 @@ def apply_rope(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.T
     return out
 
 
+def cuda_shape_problems(config: GPTConfig, ctx: ParallelContext) -> list[str]:
+    """What keeps ``config`` at this layout off the CUDA kernels, as messages
+    (empty when it fits): per-rank GEMM widths must be multiples of 8 (16-byte
+    rows for TMA), the RMSNorm kernels take up to 8192 columns, and the RoPE
+    kernel rotates 8-element chunks of each half of a head. Attention itself
+    takes any head size and length (sizes the flash kernels do not cover run
+    the exact materialized path)."""
+    problems = []
+    t = ctx.tp_size
+    if config.n_embd % 8 or (config.n_embd // t) % 8:
+        problems.append(f"n_embd {config.n_embd} (per rank {config.n_embd // t}) must be a multiple of 8")
+    if config.n_embd > 8192:
+        problems.append(f"n_embd {config.n_embd} is above the RMSNorm kernels' 8192 columns")
+    if (config.ffn_size // t) % 8:
+        problems.append(f"the SwiGLU width per rank ({config.ffn_size // t}) must be a multiple of 8")
+    if (config.vocab_size // t) % 8:
+        pad = -(-config.vocab_size // (8 * t)) * 8 * t
+        problems.append(f"the vocabulary shard per rank ({config.vocab_size // t}) must be a multiple of 8: "
+                        f"pad vocab_size to {pad}")
+    if config.head_dim % 16:
+        problems.append(f"head_dim {config.head_dim} must be a multiple of 16 for the RoPE kernel")
+    return problems
+
+
 def layers_for_stage(n_layer: int, pp_size: int, pp_rank: int) -> tuple[int, int]:
     """Contiguous, equal split of the layers over the pipeline stages."""
     per_stage = divide(n_layer, pp_size)
@@ -207,6 +231,7 @@ class GPT(nn.Module):
         self.register_buffer("rope_cos", cos, persistent=False)
         self.register_buffer("rope_sin", sin, persistent=False)
         self.flat_buffers: FlatBuffers | None = None
+        self._cuda_checked = False
         self._build_buffers()
 
     # ---------------------------------------------------------- flat buffers
@@ -274,6 +299,11 @@ class GPT(nn.Module):
         cfg, ctx = self.config, self.ctx
         dtype = cfg.activation_dtype
         sp = cfg.sequence_parallel and ctx.tp_size > 1
+        if x.is_cuda and not self._cuda_checked:
+            problems = cuda_shape_problems(cfg, ctx)
+            if problems:
+                raise ValueError("this configuration does not fit the CUDA kernels: " + "; ".join(problems))
+            self._cuda_checked = True
         if self.first_stage:
             batch = x.shape[0]
             ids = x.t().contiguous()  # [S, b]
