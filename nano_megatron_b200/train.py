@@ -28,7 +28,7 @@ from .models.functional import set_grad_observer
 from .parallel.grads import (GradBucketer, clip_coefficient, clip_grad_norm, finalize_gradients,
                              grad_norm_squared, synchronize_model_parameters)
 from .parallel.pipeline import forward_backward_1f1b
-from .utils.checkpoint import load_checkpoint, save_checkpoint
+from .utils.checkpoint import import_reference_checkpoint, load_checkpoint, save_checkpoint
 from .utils.data import TokenStream, synthetic_batches
 
 
@@ -195,9 +195,13 @@ def _train_loop(args, rank, watch, fault):
                           dp_rank=ctx.dp_rank, dp_size=ctx.dp_size) if args.data else None)
     training_state = {"lr": args.lr, "clip": args.clip, "micro_batch_size": args.micro_batch_size,
                       "num_microbatches": args.num_microbatches}
-    start_step, loaded_extra = (load_checkpoint(args.load, trainer.model, trainer.optimizer, ctx,
-                                                data=stream, map_location=device)
-                                if args.load else (0, {}))
+    # --load resumes this implementation's checkpoints, --load-reference a step
+    # directory saved by the reference implementation (same layout, torch AdamW state)
+    resume, loader = ((args.load, load_checkpoint) if args.load else
+                      (args.load_reference, import_reference_checkpoint))
+    start_step, loaded_extra = (loader(resume, trainer.model, trainer.optimizer, ctx, data=stream,
+                                       map_location=device)
+                                if resume else (0, {}))
     if loaded_extra and loaded_extra != training_state:
         raise RuntimeError(f"checkpoint training configuration mismatch: saved={loaded_extra}, "
                            f"current={training_state}")
@@ -276,6 +280,8 @@ def build_parser():
     p.add_argument("--save", help="directory for rank-local checkpoint steps")
     p.add_argument("--save-every", type=int, default=0, help="0 saves only the final step")
     p.add_argument("--load", help="exact checkpoint step directory to resume")
+    p.add_argument("--load-reference", default=None,
+                   help="resume a step directory saved by the reference implementation (nano_megatron)")
     # extensions
     p.add_argument("--ffn-hidden-size", type=int, default=None, help="SwiGLU width (default 4*n_embd)")
     p.add_argument("--rope-theta", type=float, default=10000.0)
@@ -305,6 +311,8 @@ def main(argv=None):
         raise ValueError("steps and save-every must be non-negative")
     if args.num_microbatches <= 0 or args.micro_batch_size <= 0:
         raise ValueError("num-microbatches and micro-batch-size must be positive")
+    if args.load and args.load_reference:
+        raise ValueError("--load and --load-reference are exclusive")
     train(args)
 
 

@@ -274,3 +274,129 @@ def load_checkpoint(directory, model, optimizer, ctx: ParallelContext, *, data=N
         data.load_state_dict(shard["data"])
     _apply_random_states(shard["rng"])
     return shard["step"], shard.get("extra") or {}
+
+
+# --------------------------------------------------- reference checkpoints
+REFERENCE_FORMAT_VERSION = 1
+
+
+def _reference_config_problems(saved: dict | None, model) -> list[str]:
+    """The reference's model configuration against this model's: every field the
+    reference records must match, and the settings the reference fixes (SwiGLU
+    width 4 x n_embd, RoPE theta 10000) must hold here too."""
+    ours = _model_config(model)
+    if saved is None or ours is None:
+        return [f"model configuration: checkpoint {saved!r}, this model {ours!r}"]
+    problems = [f"model configuration {key}: checkpoint {value!r}, this model {ours.get(key)!r}"
+                for key, value in saved.items() if ours.get(key) != value]
+    config = model.config
+    if config.ffn_size != 4 * config.n_embd:
+        problems.append(f"SwiGLU width {config.ffn_size}: the reference's models use 4 x n_embd = {4 * config.n_embd}")
+    if config.rope_theta != 10000.0:
+        problems.append(f"RoPE theta {config.rope_theta}: the reference's models use 10000")
+    return problems
+
+
+def _adamw_problems(state: dict, model, optimizer) -> list[str]:
+    groups = state.get("param_groups") or []
+    if len(groups) != 1:
+        return [f"optimizer: {len(groups)} parameter groups, one expected"]
+    group = groups[0]
+    problems = []
+    if len(group.get("params", ())) != len(list(model.parameters())):
+        problems.append(f"optimizer: {len(group.get('params', ()))} parameters, this model has "
+                        f"{len(list(model.parameters()))}")
+    if group.get("amsgrad") or group.get("maximize"):
+        problems.append("optimizer: amsgrad / maximize AdamW state has no counterpart in FusedAdamW")
+    steps = {int(s["step"]) for s in (state.get("state") or {}).values()}
+    if len(steps) > 1:
+        problems.append(f"optimizer: parameters at different step counts {sorted(steps)}")
+    if not hasattr(optimizer, "exp_avg") or not hasattr(optimizer, "flat"):
+        problems.append("optimizer: a reference AdamW state loads into FusedAdamW only")
+    return problems
+
+
+def _load_adamw(state: dict, model, optimizer) -> None:
+    """torch.optim.AdamW moments, per parameter in ``model.parameters()`` order,
+    into FusedAdamW's flat moments: each parameter's moments go to the same
+    strided place in the flat moment buffers as its values in the flat
+    parameter buffer."""
+    group = state["param_groups"][0]
+    per_param = state.get("state") or {}
+    base = optimizer.flat.data.storage_offset()
+    optimizer.exp_avg.zero_()
+    optimizer.exp_avg_sq.zero_()
+    for index, p in zip(group["params"], model.parameters()):
+        entry = per_param.get(index)
+        if entry is None:
+            continue
+        offset = p.data.storage_offset() - base
+        for flat, key in ((optimizer.exp_avg, "exp_avg"), (optimizer.exp_avg_sq, "exp_avg_sq")):
+            torch.as_strided(flat, p.shape, p.stride(), offset).copy_(entry[key])
+    steps = {int(s["step"]) for s in per_param.values()}
+    optimizer.step_count = steps.pop() if steps else 0
+    optimizer.param_groups = [dict(lr=group["lr"], betas=tuple(group["betas"]), eps=group["eps"],
+                                   weight_decay=group["weight_decay"])]
+
+
+def import_reference_checkpoint(directory, model, optimizer, ctx: ParallelContext, *, data=None,
+                                map_location="cpu") -> tuple[int, dict]:
+    """Resume from a step directory written by the reference's ``save_checkpoint``
+    (``nano_megatron/checkpoint.py:70-126``): the same file layout, a
+    ``torch.optim.AdamW`` state, the reference's generator and token-stream
+    states. Checks the manifest, this rank's topology, the model configuration
+    and the optimizer state first and reports every problem in one
+    :class:`CheckpointError`; then loads the model, places the AdamW moments
+    into ``optimizer`` (a :class:`~nano_megatron_b200.optim.FusedAdamW`),
+    restores the generators and the stream position. Returns ``(step, extra)``
+    like :func:`load_checkpoint`; the next save writes this implementation's
+    format."""
+    directory = Path(directory)
+    problems: list[str] = []
+    if not (directory / MANIFEST).is_file():
+        _fail(directory, ["no manifest.pt: the save did not complete"])
+    manifest = _read(directory / MANIFEST, "manifest", "cpu", problems)
+    if manifest is None:
+        _fail(directory, problems)
+    table = [("format version", manifest.get("version"), REFERENCE_FORMAT_VERSION),
+             ("world size", manifest.get("world_size"), ctx.world_size),
+             ("parallel sizes", manifest.get("parallel_sizes"), _sizes(ctx))]
+    problems += [f"{name}: checkpoint {saved!r}, this run {now!r}" for name, saved, now in table if saved != now]
+    missing = [n for n in manifest.get("shards") or () if not (directory / n).is_file()]
+    if missing:
+        problems.append(f"listed shards missing on disk: {missing}")
+    if problems:
+        _fail(directory, problems)
+    shard = _read(directory / shard_name(ctx.rank), "shard", map_location, problems)
+    if shard is None:
+        _fail(directory, problems)
+    table = [("shard format version", shard.get("version"), REFERENCE_FORMAT_VERSION),
+             ("rank topology", shard.get("topology"), topology(ctx)),
+             ("step (shard vs manifest)", shard.get("step"), manifest.get("step"))]
+    problems += [f"{name}: checkpoint {saved!r}, expected {now!r}" for name, saved, now in table if saved != now]
+    problems += _reference_config_problems(shard.get("model_config"), model)
+    problems += _adamw_problems(shard.get("optimizer") or {}, model, optimizer)
+    stream = shard.get("data")
+    if stream is not None and data is None:
+        problems.append("the shard holds a data-stream position but no stream was passed")
+    rng = shard.get("rng") or {}
+    if "cuda" in rng and not torch.cuda.is_available():
+        problems.append("the shard holds CUDA generator states but CUDA is not available")
+    if problems:
+        _fail(directory, problems)
+
+    model.load_state_dict(shard["model"])
+    _load_adamw(shard["optimizer"], model, optimizer)
+    if stream is not None:
+        identity = stream.get("identity") or {}
+        data.load_state_dict({
+            "cursor": stream.get("cursor"),
+            "layout": {key: stream.get(key) for key in ("dtype", "seq_len", "dp_rank", "dp_size")},
+            "file": {"path": identity.get("path"), "bytes": identity.get("size_bytes"),
+                     "mtime_ns": identity.get("mtime_ns")},
+        })
+    states = {"cpu": rng["torch"], "python": rng["python"]}
+    if "cuda" in rng:
+        states["cuda"] = rng["cuda"]
+    _apply_random_states(states)
+    return shard["step"], shard.get("extra") or {}
