@@ -11,7 +11,6 @@ import socket
 import pytest
 import torch
 import torch.distributed as dist
-import torch.multiprocessing as mp
 
 pytestmark = pytest.mark.gpu
 
