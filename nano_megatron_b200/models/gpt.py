@@ -93,15 +93,47 @@ def layers_for_stage(n_layer: int, pp_size: int, pp_rank: int) -> tuple[int, int
     return pp_rank * per_stage, (pp_rank + 1) * per_stage
 
 
-def _fused_ref(buffers: FlatBuffers | None, params) -> WeightRef:
-    if buffers is None:
-        raise RuntimeError("fused projections need the model's flat buffers")
+def _fused_ref(buffers: FlatBuffers, params) -> WeightRef:
     region = buffers.region_of(params[0])
     return WeightRef(region.data_block, params, region.compute_block, region.grad_block)
 
 
+def _column_group(x, linears, buffers: FlatBuffers | None, ctx: ParallelContext, mode: str,
+                  dtype: torch.dtype):
+    """``x @ [W_1 | W_2 | ...]`` for column-parallel layers that share an input:
+    one GEMM over the fused region inside a model; each layer on its own (one
+    GEMM and one input collective each) for modules built outside one."""
+    weights = tuple(lin.weight for lin in linears)
+    if buffers is not None:
+        return column_linear(x, _fused_ref(buffers, weights), ctx, mode, dtype)
+    return torch.cat([column_linear(x, WeightRef.of(w), ctx, mode, dtype) for w in weights], dim=1)
+
+
+def _compute_dtype(x: torch.Tensor) -> torch.dtype:
+    """The dtype a module called in the reference's form computes in: the
+    autocast dtype when autocast is on for ``x``'s device, else ``x``'s."""
+    kind = x.device.type
+    if torch.is_autocast_enabled(kind):
+        return torch.get_autocast_dtype(kind)
+    return x.dtype if x.is_floating_point() else torch.float32
+
+
+def _batch_first_call(fn, x: torch.Tensor, *args):
+    """Run ``fn(rows, batch, *args)`` on ``x [b, s, H]`` as sequence-major rows
+    ``[s*b, H]`` and return its rows ``[s'*b, N]`` as ``[b, s', N]``."""
+    b = x.shape[0]
+    rows = x.transpose(0, 1).reshape(-1, x.shape[-1])
+    y = fn(rows, b, *args)
+    return y.view(-1, b, y.shape[-1]).transpose(0, 1).contiguous()
+
+
 class ParallelAttention(nn.Module):
-    """MHA sharded over heads; one fused QKV GEMM, one row-parallel output GEMM."""
+    """MHA sharded over heads; one fused QKV GEMM, one row-parallel output GEMM.
+
+    Parity: ``nano_megatron/model.py:92-128``. ``forward(x, cos, sin)`` is the
+    reference's call (batch-first ``[b, s, H]``); the model runs
+    :meth:`forward_rows` on its sequence-major token rows.
+    """
 
     def __init__(self, config: GPTConfig, ctx: ParallelContext):
         super().__init__()
@@ -120,17 +152,26 @@ class ParallelAttention(nn.Module):
     def fused_groups(self, prefix: str):
         return [[f"{prefix}q.weight", f"{prefix}k.weight", f"{prefix}v.weight"]]
 
-    def forward(self, x, batch, cos, sin, dtype):
-        """``x [s*b, H]`` (already normed) -> ``[s*b, H]``."""
+    def forward(self, x, cos, sin):
+        """``x [b, s, H]`` (``s = S/tp`` under sequence parallelism) -> ``[b, s, H]``."""
+        return _batch_first_call(self.forward_rows, x, cos, sin, _compute_dtype(x))
+
+    def forward_rows(self, x, batch, cos, sin, dtype):
+        """``x [s*b, H]`` (already normed, sequence-major rows) -> ``[s*b, H]``."""
         sp = self.sequence_parallel and self.ctx.tp_size > 1
-        qkv_ref = _fused_ref(self.flat_buffers, (self.q.weight, self.k.weight, self.v.weight))
-        qkv = column_linear(x, qkv_ref, self.ctx, "ag" if sp else "f", dtype)
+        qkv = _column_group(x, (self.q, self.k, self.v), self.flat_buffers, self.ctx,
+                            "ag" if sp else "f", dtype)
         o = causal_attention(qkv, batch, self.n_head_local, self.head_dim, cos, sin)
         return row_linear(o, WeightRef.of(self.proj.weight), self.ctx, "rs" if sp else "g", dtype)
 
 
 class ParallelMLP(nn.Module):
-    """SwiGLU: fused gate|up column-parallel GEMM, row-parallel down GEMM."""
+    """SwiGLU: fused gate|up column-parallel GEMM, row-parallel down GEMM.
+
+    Parity: ``nano_megatron/model.py:131-153`` (with a configurable width;
+    the reference's is ``4 * n_embd``). ``forward(x)`` is the reference's call
+    (batch-first ``[b, s, H]``); the model runs :meth:`forward_rows`.
+    """
 
     def __init__(self, config: GPTConfig, ctx: ParallelContext):
         super().__init__()
@@ -145,19 +186,32 @@ class ParallelMLP(nn.Module):
     def fused_groups(self, prefix: str):
         return [[f"{prefix}gate.weight", f"{prefix}up.weight"]]
 
-    def forward(self, x, dtype):
+    def forward(self, x):
+        """``x [b, s, H]`` (``s = S/tp`` under sequence parallelism) -> ``[b, s, H]``."""
+        return _batch_first_call(lambda rows, _b, dtype: self.forward_rows(rows, dtype), x,
+                                 _compute_dtype(x))
+
+    def forward_rows(self, x, dtype):
+        """``x [s*b, H]`` (sequence-major rows) -> ``[s*b, H]``."""
         sp = self.sequence_parallel and self.ctx.tp_size > 1
         mode = "ag" if sp else "f"
-        gu_ref = _fused_ref(self.flat_buffers, (self.gate.weight, self.up.weight))
-        if dtype == torch.bfloat16 and gate_up_swiglu_supported(x, self.gate.weight.shape[1], self.ctx, mode):
+        if (self.flat_buffers is not None and dtype == torch.bfloat16
+                and gate_up_swiglu_supported(x, self.gate.weight.shape[1], self.ctx, mode)):
+            gu_ref = _fused_ref(self.flat_buffers, (self.gate.weight, self.up.weight))
             a = gate_up_swiglu(x, gu_ref, self.ctx, mode, dtype)
         else:
-            a = swiglu(column_linear(x, gu_ref, self.ctx, mode, dtype))
+            a = swiglu(_column_group(x, (self.gate, self.up), self.flat_buffers, self.ctx, mode, dtype))
         return row_linear(a, WeightRef.of(self.down.weight), self.ctx, "rs" if sp else "g", dtype)
 
 
 class TransformerLayer(nn.Module):
-    """Pre-norm block: ``x + attn(norm(x))`` then ``x + mlp(norm(x))``."""
+    """Pre-norm block: ``x + attn(norm(x))`` then ``x + mlp(norm(x))``.
+
+    Parity: ``nano_megatron/model.py:156-166``. ``forward(x, cos, sin)`` is the
+    reference's call (batch-first ``[b, s, H]``); the model runs
+    :meth:`forward_rows`, where the first residual add and the MLP's norm are
+    one kernel.
+    """
 
     def __init__(self, config: GPTConfig, ctx: ParallelContext):
         super().__init__()
@@ -166,18 +220,24 @@ class TransformerLayer(nn.Module):
         self.mlp_norm = RMSNorm(config.n_embd)
         self.mlp = ParallelMLP(config, ctx)
 
-    def forward(self, x, batch, cos, sin, dtype):
-        a = self.attn(self.attn_norm(x), batch, cos, sin, dtype)
+    def forward(self, x, cos, sin):
+        """``x [b, s, H]`` -> ``[b, s, H]``."""
+        return _batch_first_call(self.forward_rows, x, cos, sin, _compute_dtype(x))
+
+    def forward_rows(self, x, batch, cos, sin, dtype):
+        """``x [s*b, H]`` (sequence-major rows) -> ``[s*b, H]``."""
+        a = self.attn.forward_rows(self.attn_norm(x), batch, cos, sin, dtype)
         # residual add and the MLP's norm in one pass
-        lead = x.shape[:-1]
-        x, h = add_rms_norm(x.reshape(-1, x.shape[-1]), a.reshape(-1, a.shape[-1]),
-                            self.mlp_norm.weight, self.mlp_norm.eps)
-        x, h = x.view(*lead, -1), h.view(*lead, -1)
-        return x + self.mlp(h, dtype)
+        x, h = add_rms_norm(x, a.reshape(-1, a.shape[-1]), self.mlp_norm.weight, self.mlp_norm.eps)
+        return x + self.mlp.forward_rows(h, dtype)
 
 
 class ParallelLMHead(nn.Module):
-    """Vocab-sharded output projection ``[V/tp, H]`` (the embedding's layout, so they can tie)."""
+    """Vocab-sharded output projection ``[V/tp, H]`` (the embedding's layout, so they can tie).
+
+    Parity: ``nano_megatron/model.py:169-192``. The model's last stage uses the
+    fused LM head + cross entropy instead of :meth:`forward` when it has labels.
+    """
 
     def __init__(self, config: GPTConfig, ctx: ParallelContext):
         super().__init__()
@@ -188,8 +248,26 @@ class ParallelLMHead(nn.Module):
         self.sequence_parallel = config.sequence_parallel
         nn.init.normal_(self.weight, std=config.init_std)
 
+    def forward(self, x):
+        """``x [b, s, H]`` -> vocab-sharded logits ``[b, S, V/tp]``: the sequence
+        is all-gathered first under sequence parallelism, else f applies."""
+        mode = "ag" if self.sequence_parallel and self.ctx.tp_size > 1 else "f"
+        return _batch_first_call(
+            lambda rows, _b, dtype: lm_head_logits(rows, WeightRef.of(self.weight), self.ctx, mode, dtype),
+            x, _compute_dtype(x))
+
 
 class GPT(nn.Module):
+    """This rank's pipeline stage of the model.
+
+    Parity: ``nano_megatron/model.py:200-281`` (size checks, stage split, tie
+    at one stage, RoPE tables as non-persistent buffers, whole-block
+    recompute in training). Differences: parameters are views of flat fp32
+    buffers (``flat_buffers``), compute is in ``config.activation_dtype``
+    without autocast, and a non-last stage returns its hidden state
+    sequence-first ``[s, b, H]``.
+    """
+
     def __init__(self, config: GPTConfig, ctx: ParallelContext | None = None,
                  device: torch.device | str | None = None):
         super().__init__()
@@ -284,10 +362,10 @@ class GPT(nn.Module):
                 # drops; the second is the recomputation before backward
                 calls[0] += 1
                 with discarded_forward(calls[0] == 1):
-                    return layer(h, batch, cos, sin, dtype)
+                    return layer.forward_rows(h, batch, cos, sin, dtype)
 
             return checkpoint(run, h, batch, cos, sin, dtype, use_reentrant=False)
-        return layer(h, batch, cos, sin, dtype)
+        return layer.forward_rows(h, batch, cos, sin, dtype)
 
     def forward(self, x, labels=None):
         """Token ids ``[b, S]`` on the first stage, hidden ``[s, b, H]`` elsewhere.
@@ -306,9 +384,8 @@ class GPT(nn.Module):
             self._cuda_checked = True
         if self.first_stage:
             batch = x.shape[0]
-            ids = x.t().contiguous()  # [S, b]
-            h = self.embedding(ids, sequence_parallel=sp, out_dtype=dtype)
-            h = h.reshape(-1, cfg.n_embd)
+            ids = x.t().reshape(-1)  # sequence-major token order
+            h = self.embedding.embed_rows(ids, sequence_parallel=sp, out_dtype=dtype)
         else:
             batch = x.shape[1]
             h = x.reshape(-1, cfg.n_embd)

@@ -13,8 +13,11 @@ function                                    forward                backward
 
 Activations in this framework are stored sequence-first (``[s, b, H]`` or the
 flattened ``[s*b, H]``), so a sequence shard is one contiguous slab and the
-gather/scatter need no transposes. ``seq_dim=1`` is accepted for batch-first
-callers and transposes around the collective.
+model's own gather/scatter (``all_gather_sequence`` and
+``reduce_scatter_sequence``, sequence on dim 0 by default) need no transposes.
+The four public functions keep the reference's batch-first convention: the
+sequence is dim 1 of ``[b, s, ...]`` unless ``seq_dim=0`` is passed for a
+sequence-first tensor.
 
 These are the generic (NCCL / Gloo) paths. On CUDA with tensor parallelism the
 linear layers use fused all-gather->GEMM and GEMM->reduce-scatter kernels
@@ -127,10 +130,12 @@ def reduce_from_tensor_parallel_region(x: torch.Tensor, ctx: ParallelContext) ->
 
 
 def gather_from_sequence_parallel_region(x: torch.Tensor, ctx: ParallelContext,
-                                         seq_dim: int = 0) -> torch.Tensor:
+                                         seq_dim: int = 1) -> torch.Tensor:
+    """All-gather the sequence shards (dim ``seq_dim``, 1 for batch-first ``[b, s, ...]``)."""
     return _GatherSeq.apply(x, ctx.tp_group, ctx.tp_size, seq_dim)
 
 
 def reduce_scatter_to_sequence_parallel_region(x: torch.Tensor, ctx: ParallelContext,
-                                               seq_dim: int = 0) -> torch.Tensor:
+                                               seq_dim: int = 1) -> torch.Tensor:
+    """SUM the full-sequence partials and keep this rank's shard of dim ``seq_dim``."""
     return _ReduceScatterSeq.apply(x, ctx.tp_group, ctx.tp_size, seq_dim)

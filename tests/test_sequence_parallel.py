@@ -1,5 +1,6 @@
 """Real Gloo processes: sequence all-gather / reduce-scatter values and their
-adjoint gradients, sequence-first (dim 0) and batch-first (dim 1)."""
+adjoint gradients, sequence-first (dim 0) and batch-first (dim 1, the default
+of the public functions, as in the reference)."""
 
 import os
 import tempfile
@@ -24,12 +25,13 @@ def _worker(rank, world, init_file, q):
             if dim == 1:
                 full = full.transpose(0, 1).contiguous()  # [2, 4, 3, 2]
             shard = torch.chunk(full, world, dim=dim)[rank].clone().requires_grad_(True)
-            gathered = gather_from_sequence_parallel_region(shard, ctx, seq_dim=dim)
+            kw = {"seq_dim": 0} if dim == 0 else {}
+            gathered = gather_from_sequence_parallel_region(shard, ctx, **kw)
             torch.testing.assert_close(gathered, full)
             gathered.square().sum().backward()
             torch.testing.assert_close(shard.grad, torch.chunk(2 * full, world, dim=dim)[rank] * world)
             partial = (full / world).requires_grad_(True)
-            reduced = reduce_scatter_to_sequence_parallel_region(partial, ctx, seq_dim=dim)
+            reduced = reduce_scatter_to_sequence_parallel_region(partial, ctx, **kw)
             torch.testing.assert_close(reduced, torch.chunk(full, world, dim=dim)[rank])
             reduced.sum().backward()
             torch.testing.assert_close(partial.grad, torch.ones_like(full))
