@@ -118,7 +118,7 @@ class TokenStream:
         self.cursor = cursor
 
 
-def synthetic_batches(config, micro_batch_size: int, num_microbatches: int, step: int,
+def synthetic_batches(config, micro_bs: int, num_microbatches: int, step: int,
                       data_parallel_rank: int = 0):
     """Uniform random ``(inputs, labels)`` microbatches for one step of one DP rank.
 
@@ -128,7 +128,7 @@ def synthetic_batches(config, micro_batch_size: int, num_microbatches: int, step
     the two implementations train on identical data.
     """
     gen = torch.Generator().manual_seed(1234 + 100_003 * step + data_parallel_rank)
-    shape = (micro_batch_size, config.seq_len)
+    shape = (micro_bs, config.seq_len)
     batches = []
     for _ in range(num_microbatches):
         inputs = torch.randint(0, config.vocab_size, shape, generator=gen)
