@@ -52,6 +52,7 @@ def single_rank_group(tmp_path):
     dist.destroy_process_group()
 
 
+@pytest.mark.distributed
 def test_buckets_cover_the_buffer_once_from_the_end(single_rank_group):
     ctx = single_rank_group
     _, model = _model()
@@ -65,6 +66,7 @@ def test_buckets_cover_the_buffer_once_from_the_end(single_rank_group):
         assert sorted(r for rs in b.bucket_regions for r in rs) == list(range(len(flat.regions)))
 
 
+@pytest.mark.distributed
 def test_bucketer_learns_writes_and_starts_buckets_during_last_backward(single_rank_group):
     ctx = single_rank_group
     cfg, model = _model(tie=True)

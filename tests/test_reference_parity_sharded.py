@@ -23,6 +23,7 @@ import torch.multiprocessing as mp
 
 REF = os.environ.get("NMB_REFERENCE_PATH") or os.path.join(
     os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "baseline", "_ref")
+pytestmark = pytest.mark.distributed
 
 TOL = dict(rtol=1e-4, atol=1e-6)
 
