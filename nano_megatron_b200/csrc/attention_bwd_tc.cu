@@ -1,5 +1,7 @@
 // Causal flash-attention backward on 5th-generation tensor cores (sm_100a),
-// head_dim 128, bf16 in / out, fp32 math. Two deterministic kernels, no atomics:
+// head_dim 128, bf16 in / out, fp32 math. Two deterministic kernels, no atomics.
+// Reference op: the autograd backward of the RoPE + causal SDPA of
+// nano_megatron/model.py:124-126 (the inverse rotation is applied in the stores).
 //
 //   dK/dV kernel (one CTA = 128 keys of one (batch, head); loops over the
 //   64-query blocks at or after it):

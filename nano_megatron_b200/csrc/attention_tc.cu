@@ -1,5 +1,7 @@
 // Causal flash-attention forward on 5th-generation tensor cores (sm_100a),
 // head_dim 128, bf16 in / out, fp32 softmax and accumulation.
+// Reference op: F.scaled_dot_product_attention(q, k, v, is_causal=True),
+// nano_megatron/model.py:126.
 //
 // One CTA computes 256 query rows -- two 128-row tiles -- of one (batch,
 // head). 16 warps in four warpgroups with separate register budgets

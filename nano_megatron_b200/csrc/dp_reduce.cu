@@ -1,6 +1,7 @@
 // Data-parallel gradient averaging over NVLink peer memory: one kernel does a
 // two-shot all-reduce of one span ("bucket") of the flat fp32 gradient buffer,
-// with the 1/dp scale applied in the same pass.
+// with the 1/dp scale applied in the same pass. Reference op: the flat
+// all-reduce and divide of nano_megatron/grads.py:35-54.
 //
 // Every rank of the DP group maps every other rank's gradient buffer and flag
 // area (symmetric memory). For a call with epoch e on rank r:

@@ -2,7 +2,9 @@
 // (`--dtype float32`): a strided SIMT GEMM (fp32 FMA, no TF32) and the
 // causal-softmax pieces of a materialized attention. They serve correctness
 // (fp32 results within the oracle tests' 1e-4 tolerances), not speed; bf16 on
-// the tensor-core kernels is the performance path.
+// the tensor-core kernels is the performance path. Reference ops: the fp32
+// matmuls and SDPA of nano_megatron/model.py with compute_dtype "float32"
+// (model.py:53-62).
 
 #include <cuda_runtime.h>
 

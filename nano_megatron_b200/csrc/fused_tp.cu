@@ -1,5 +1,9 @@
 // Tensor-parallel GEMMs fused with their sequence-parallel collectives over
-// NVLink peer memory (one kernel does the math and the communication):
+// NVLink peer memory (one kernel does the math and the communication).
+// Reference ops: x @ W with the sequence all-gather / reduce-scatter around it
+// (nano_megatron/tp_layers.py:54-88, mappings.py:109-134, used at
+// model.py:113-128 and 147-153), and the LM head with the vocab-parallel cross
+// entropy (model.py:185-192, cross_entropy.py:16-65).
 //
 //   all-gather -> GEMM   Y[M,N] = AG(x)[M,K] @ B     (QKV, gate|up forward;
 //                                                      row-parallel dgrad)

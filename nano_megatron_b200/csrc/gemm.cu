@@ -1,4 +1,6 @@
 // Persistent, warp-specialized bf16 GEMM on 5th-generation tensor cores (sm_100a).
+// Reference ops: the torch matmuls of the linear layers and LM head
+// (nano_megatron/tp_layers.py:58,82; model.py:192) and their autograd backward.
 //
 //   C[M,N] (op)= sum_k A(m,k) * B(k,n)      fp32 accumulation in TMEM
 //

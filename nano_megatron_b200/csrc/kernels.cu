@@ -12,6 +12,11 @@
 //   AdamW             one pass over the flat fp32 master buffer, applies the
 //                     clip coefficient on load and rewrites the bf16 copy
 //   sq-norm           weighted sum of squares of many segments into fp64
+//
+// Reference ops (nano_megatron/): RMSNorm model.py:73-75; SwiGLU
+// model.py:151-152; RoPE model.py:84-89; embedding tp_layers.py:112-127; CE
+// cross_entropy.py:18-65; AdamW train.py:85 (torch.optim.AdamW defaults);
+// squared norm grads.py:166-183.
 
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>

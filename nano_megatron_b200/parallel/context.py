@@ -19,7 +19,9 @@ import torch.distributed as dist
 
 @dataclass(frozen=True)
 class ParallelContext:
-    """Topology of one rank. Immutable; passed explicitly, never global."""
+    """Topology of one rank. Immutable; passed explicitly, never global.
+    Parity: ``nano_megatron/parallel.py:11-72`` (same fields; ``resources``
+    is added for per-group state such as symmetric workspaces)."""
 
     rank: int
     world_size: int
@@ -88,7 +90,9 @@ def grid_ranks(world_size: int, tp_size: int, pp_size: int):
 
 
 def init_parallel(tp_size: int = 1, pp_size: int = 1) -> ParallelContext:
-    """Create all TP, DP, PP and tied-embedding groups; return this rank's view."""
+    """Create all TP, DP, PP and tied-embedding groups; return this rank's view.
+    Parity: ``nano_megatron/parallel.py:75-143`` (grid order and group creation
+    order)."""
     if not dist.is_initialized():
         raise RuntimeError("init_parallel builds groups over an existing world: call "
                            "torch.distributed.init_process_group first")

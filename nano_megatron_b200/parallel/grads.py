@@ -36,7 +36,9 @@ def _flat_buffers(model):
 
 
 def all_reduce_replicated_gradients(model, ctx: ParallelContext, *, sequence_parallel: bool = False) -> None:
-    """One coalesced all-reduce of every TP-replicated gradient."""
+    """One coalesced all-reduce of every TP-replicated gradient (the reference
+    reduces each one on its own, ``nano_megatron/grads.py:16-32``): a SUM with
+    sequence parallelism, the TP mean without."""
     if ctx.tp_size == 1:
         return
     grads = [p.grad for p in model.parameters() if p.grad is not None and not _is_sharded(p)]
@@ -54,7 +56,8 @@ def all_reduce_replicated_gradients(model, ctx: ParallelContext, *, sequence_par
 
 
 def all_reduce_data_parallel_gradients(model, ctx: ParallelContext) -> None:
-    """Average gradients over the DP group (flat buffer: one collective)."""
+    """Average gradients over the DP group (flat buffer: one collective).
+    Parity: ``nano_megatron/grads.py:35-54``."""
     if ctx.dp_size == 1:
         return
     buffers = _flat_buffers(model)
@@ -232,7 +235,8 @@ class GradBucketer:
 
 
 def all_reduce_embedding_gradients(model, ctx: ParallelContext) -> None:
-    """SUM the tied embedding / LM-head gradient copies over the tied group."""
+    """SUM the tied embedding / LM-head gradient copies over the tied group.
+    Parity: ``nano_megatron/grads.py:57-78``."""
     if ctx.pp_size == 1 or ctx.tied_group is None:
         return
     if not (ctx.is_first_stage or ctx.is_last_stage):
@@ -244,7 +248,8 @@ def all_reduce_embedding_gradients(model, ctx: ParallelContext) -> None:
 
 
 def synchronize_tied_embeddings(model, ctx: ParallelContext) -> None:
-    """Broadcast the first stage's embedding into the last stage's LM head."""
+    """Broadcast the first stage's embedding into the last stage's LM head.
+    Parity: ``nano_megatron/grads.py:81-102``."""
     if ctx.pp_size == 1 or ctx.tied_group is None:
         return
     if not (ctx.is_first_stage or ctx.is_last_stage):
@@ -256,7 +261,8 @@ def synchronize_tied_embeddings(model, ctx: ParallelContext) -> None:
 
 
 def synchronize_model_parameters(model, ctx: ParallelContext, *, tie_embeddings: bool = False) -> None:
-    """Make replicated parameters agree after rank-dependent initialization."""
+    """Make replicated parameters agree after rank-dependent initialization.
+    Parity: ``nano_megatron/grads.py:105-127``."""
     if ctx.tp_size > 1:
         for p in model.parameters():
             if not _is_sharded(p):
@@ -278,7 +284,8 @@ def synchronize_model_parameters(model, ctx: ParallelContext, *, tie_embeddings:
 def finalize_gradients(model, ctx: ParallelContext, *, tie_embeddings: bool = False,
                        sequence_parallel: bool = False, skip_data_parallel: bool = False) -> None:
     """Replicated-TP, then tied, then DP reduction (``skip_data_parallel`` when a
-    bucketer already reduced the DP gradients during backward)."""
+    bucketer already reduced the DP gradients during backward).
+    Parity: ``nano_megatron/grads.py:130-140``."""
     all_reduce_replicated_gradients(model, ctx, sequence_parallel=sequence_parallel)
     if tie_embeddings:
         all_reduce_embedding_gradients(model, ctx)
@@ -299,7 +306,8 @@ def _norm_terms(model, ctx: ParallelContext, tie_embeddings: bool):
 
 
 def grad_norm_squared(model, ctx: ParallelContext, *, tie_embeddings: bool = False) -> torch.Tensor:
-    """Logical-model squared gradient norm (fp64), reduced over TP then PP."""
+    """Logical-model squared gradient norm (fp64), reduced over TP then PP
+    and never over DP (``nano_megatron/grads.py:162-187``)."""
     params = list(model.parameters())
     device = params[0].device if params else torch.device("cpu")
     terms = _norm_terms(model, ctx, tie_embeddings)
@@ -338,6 +346,7 @@ def clip_grad_norm(model, ctx: ParallelContext, max_norm: float, *, tie_embeddin
 
     With ``apply=False`` the gradients are left untouched and the caller
     applies the coefficient itself (the fused optimizer does it on load).
+    Parity: ``nano_megatron/grads.py:143-193``.
     """
     if max_norm < 0:
         raise ValueError(f"max_norm must be non-negative, got {max_norm}")

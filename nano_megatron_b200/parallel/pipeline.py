@@ -35,7 +35,9 @@ Batch = tuple[torch.Tensor, torch.Tensor]
 
 
 class _P2P:
-    """Posts exchanges with the neighbouring stages; defers send completion."""
+    """Posts exchanges with the neighbouring stages; defers send completion.
+    Parity: ``nano_megatron/pipeline.py:22-108`` (same P2P op order; the
+    reference waits on every request at once)."""
 
     def __init__(self, ctx: ParallelContext, shape, dtype, device):
         self.ctx, self.shape, self.dtype, self.device = ctx, shape, dtype, device
@@ -134,6 +136,8 @@ def forward_backward_1f1b(model: nn.Module, batches: Sequence[Batch], config, de
     ``model``) is called right before the final microbatch's backward, where
     overlapped gradient reduction can start; the argument form receives the
     number of backwards already run in this step.
+    Parity: ``nano_megatron/pipeline.py:152-224`` (validation, warm-up depth
+    ``min(pp - r - 1, M)``, steady 1F1B, cool-down).
     """
     num_microbatches = len(batches)
     if num_microbatches == 0:
