@@ -387,6 +387,10 @@ class GPT(nn.Module):
             ids = x.t().reshape(-1)  # sequence-major token order
             h = self.embedding.embed_rows(ids, sequence_parallel=sp, out_dtype=dtype)
         else:
+            s_local = cfg.seq_len // ctx.tp_size if sp else cfg.seq_len
+            if x.dim() != 3 or x.shape[0] != s_local or x.shape[2] != cfg.n_embd:
+                raise ValueError(f"a non-first pipeline stage takes its hidden state sequence-first "
+                                 f"[{s_local}, batch, {cfg.n_embd}]; got {tuple(x.shape)}")
             batch = x.shape[1]
             h = x.reshape(-1, cfg.n_embd)
         if h.dtype != dtype:

@@ -1,0 +1,33 @@
+"""A non-first pipeline stage takes its hidden state sequence-first
+``[s, b, H]``; any other layout is refused with the expected shape instead of
+being read with the batch and sequence axes swapped."""
+
+import pytest
+import torch
+
+from nano_megatron_b200 import GPT, GPTConfig, ParallelContext
+
+
+def _last_stage(**kw):
+    ctx = ParallelContext(rank=1, world_size=2, tp_size=1, tp_rank=0, pp_size=2, pp_rank=1,
+                          dp_size=1, dp_rank=0, pp_ranks=(0, 1))
+    cfg = GPTConfig(vocab_size=64, n_layer=2, n_head=4, n_embd=32, seq_len=8, **kw)
+    torch.manual_seed(0)
+    return GPT(cfg, ctx), cfg
+
+
+def test_sequence_first_hidden_state_is_accepted():
+    model, cfg = _last_stage()
+    h = torch.randn(cfg.seq_len, 3, cfg.n_embd)
+    labels = torch.randint(0, cfg.vocab_size, (3, cfg.seq_len))
+    loss = model(h, labels)
+    assert loss.ndim == 0 and torch.isfinite(loss)
+    logits = model(h)
+    assert logits.shape == (3, cfg.seq_len, cfg.vocab_size)
+
+
+@pytest.mark.parametrize("shape", [(3, 8, 32), (8, 3, 16), (24, 32)])
+def test_other_layouts_are_refused(shape):
+    model, _ = _last_stage()
+    with pytest.raises(ValueError, match=r"sequence-first \[8, batch, 32\]"):
+        model(torch.randn(*shape))
