@@ -346,14 +346,32 @@ def ce_local_stats(logits, target, vocab_start, vocab_end):
     return mx, se, tl, None
 
 
+# The CE-gradient kernel launches one grid row per token, and a grid has at
+# most 65535 rows; longer inputs run as consecutive launches over row blocks.
+_CE_GRAD_MAX_ROWS = 65535
+_CE_GRAD_BLOCK_ROWS = 32768
+
+
+def _ce_grad_launch(logits, target, gmax, gsum, scale1, d, vocab_start) -> None:
+    rows = logits.shape[0]
+    if rows <= _CE_GRAD_MAX_ROWS:
+        C.ce_grad(logits, target, gmax, gsum, scale1, 1.0, d, vocab_start)
+        _count()
+        return
+    for r0 in range(0, rows, _CE_GRAD_BLOCK_ROWS):
+        r1 = min(rows, r0 + _CE_GRAD_BLOCK_ROWS)
+        C.ce_grad(logits[r0:r1], target[r0:r1], gmax[r0:r1], gsum[r0:r1], scale1, 1.0, d[r0:r1], vocab_start)
+        _count()
+
+
 def ce_grad(logits, target, vocab_start, gmax, gsum, scale, out_dtype):
     """``scale`` may be a per-row tensor (generic path) or a device scalar."""
     d = torch.empty(logits.shape, dtype=logits.dtype, device=logits.device)
     if scale.numel() == 1:
-        C.ce_grad(logits, target.contiguous(), gmax, gsum, scale.float().reshape(1), 1.0, d, vocab_start)
+        _ce_grad_launch(logits, target.contiguous(), gmax, gsum, scale.float().reshape(1), d, vocab_start)
         return d if d.dtype == out_dtype else d.to(out_dtype)
-    C.ce_grad(logits, target.contiguous(), gmax, gsum, torch.ones(1, device=logits.device), 1.0, d,
-              vocab_start)
+    _ce_grad_launch(logits, target.contiguous(), gmax, gsum, torch.ones(1, device=logits.device), d,
+                    vocab_start)
     d = d * scale.unsqueeze(-1).to(d.dtype)
     return d if d.dtype == out_dtype else d.to(out_dtype)
 
@@ -374,8 +392,7 @@ def lm_head_ce_grad(X, w, labels, vocab_start, state, g_over_n, inplace=False):
     d = logits if inplace else torch.empty_like(logits)
     if inplace:
         torch.autograd.graph.increment_version(logits)
-    C.ce_grad(logits, labels.contiguous(), gm, gs, g_over_n.float().reshape(1), 1.0, d, vocab_start)
-    _count()
+    _ce_grad_launch(logits, labels.contiguous(), gm, gs, g_over_n.float().reshape(1), d, vocab_start)
     return d
 
 
