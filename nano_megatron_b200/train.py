@@ -7,7 +7,7 @@
 rank-local checkpoints. Flags and defaults are those of the reference
 (``nano_megatron/train.py:182-208``) plus ``--ffn-hidden-size``,
 ``--rope-theta``, ``--untie-embeddings``, ``--init-std``, ``--init-device``,
-``--timing`` and ``--no-fused-tp``.
+``--timing``, ``--no-fused-tp``, ``--load-reference`` and ``--save-format``.
 """
 
 from __future__ import annotations
@@ -28,7 +28,8 @@ from .models.functional import set_grad_observer
 from .parallel.grads import (GradBucketer, clip_coefficient, clip_grad_norm, finalize_gradients,
                              grad_norm_squared, synchronize_model_parameters)
 from .parallel.pipeline import forward_backward_1f1b
-from .utils.checkpoint import import_reference_checkpoint, load_checkpoint, save_checkpoint
+from .utils.checkpoint import (export_reference_checkpoint, import_reference_checkpoint, load_checkpoint,
+                               save_checkpoint)
 from .utils.data import TokenStream, synthetic_batches
 
 
@@ -247,9 +248,9 @@ def _train_loop(args, rank, watch, fault):
                           or (args.save_every > 0 and next_step % args.save_every == 0)):
             if poller is not None:
                 poller.final()  # never checkpoint state that a failed kernel produced
-            save_checkpoint(Path(args.save) / f"step_{next_step:08d}", trainer.model,
-                            trainer.optimizer, ctx, step=next_step, data=stream,
-                            extra=training_state)
+            saver = export_reference_checkpoint if args.save_format == "reference" else save_checkpoint
+            saver(Path(args.save) / f"step_{next_step:08d}", trainer.model, trainer.optimizer, ctx,
+                  step=next_step, data=stream, extra=training_state)
     if poller is not None:
         poller.final()
 
@@ -282,6 +283,9 @@ def build_parser():
     p.add_argument("--load", help="exact checkpoint step directory to resume")
     p.add_argument("--load-reference", default=None,
                    help="resume a step directory saved by the reference implementation (nano_megatron)")
+    p.add_argument("--save-format", choices=["native", "reference"], default="native",
+                   help="write --save steps in this implementation's format or in one the reference "
+                        "implementation's --load resumes")
     # extensions
     p.add_argument("--ffn-hidden-size", type=int, default=None, help="SwiGLU width (default 4*n_embd)")
     p.add_argument("--rope-theta", type=float, default=10000.0)

@@ -155,7 +155,19 @@ def save_checkpoint(directory, model, optimizer, ctx: ParallelContext, *, step: 
     """
     if not _valid_step(step):
         raise ValueError(f"save_checkpoint: step {step!r} is not a non-negative int")
-    directory = Path(directory)
+    return _write_step(Path(directory), ctx, step, FORMAT_VERSION, lambda: {
+        "version": FORMAT_VERSION, "topology": topology(ctx),
+        "model": _host_copy(model.state_dict()), "model_config": _model_config(model),
+        "optimizer": _host_copy(optimizer.state_dict()), "step": step,
+        "rng": _random_states(), "data": None if data is None else data.state_dict(),
+        "extra": dict(extra or {}),
+    })
+
+
+def _write_step(directory: Path, ctx: ParallelContext, step: int, version: int, make_shard) -> Path:
+    """The save protocol shared by both formats: withdraw the manifest, write
+    every rank's shard durably, then the manifest with the shards' sizes and
+    CRC-32s (readers that do not know those keys ignore them)."""
     directory.mkdir(parents=True, exist_ok=True)
     group_save = ctx.world_size > 1 and torch.distributed.is_initialized()
     manifest_path = directory / MANIFEST
@@ -165,13 +177,7 @@ def save_checkpoint(directory, model, optimizer, ctx: ParallelContext, *, step: 
     if group_save:
         torch.distributed.barrier()
 
-    shard = {
-        "version": FORMAT_VERSION, "topology": topology(ctx),
-        "model": _host_copy(model.state_dict()), "model_config": _model_config(model),
-        "optimizer": _host_copy(optimizer.state_dict()), "step": step,
-        "rng": _random_states(), "data": None if data is None else data.state_dict(),
-        "extra": dict(extra or {}),
-    }
+    shard = make_shard()
     path = directory / shard_name(ctx.rank)
     digest = _durable_save(shard, path)
 
@@ -185,7 +191,7 @@ def save_checkpoint(directory, model, optimizer, ctx: ParallelContext, *, step: 
         absent = [n for n in names if not (directory / n).is_file()]
         if absent:
             raise CheckpointError(f"{directory}: shards {absent} were not written; no manifest")
-        _durable_save({"version": FORMAT_VERSION, "step": step, "world_size": ctx.world_size,
+        _durable_save({"version": version, "step": step, "world_size": ctx.world_size,
                        "parallel_sizes": _sizes(ctx), "shards": names,
                        "shard_digests": dict(zip(names, digests))}, manifest_path)
     if group_save:
@@ -400,3 +406,77 @@ def import_reference_checkpoint(directory, model, optimizer, ctx: ParallelContex
         states["cuda"] = rng["cuda"]
     _apply_random_states(states)
     return shard["step"], shard.get("extra") or {}
+
+
+# GPTConfig fields this implementation adds; the reference's model configuration is the rest
+_EXTENSION_FIELDS = ("ffn_hidden_size", "rope_theta", "init_std")
+
+
+def _adamw_state_dict(model, optimizer) -> dict:
+    """FusedAdamW's flat moments as a ``torch.optim.AdamW`` state dict over
+    ``model.parameters()`` (the inverse of :func:`_load_adamw`): each
+    parameter's moments are read from the place its values occupy in the flat
+    parameter buffer; the group carries torch's own AdamW defaults."""
+    group = optimizer.param_groups[0]
+    template = torch.optim.AdamW([torch.zeros(1)], lr=group["lr"], betas=tuple(group["betas"]),
+                                 eps=group["eps"], weight_decay=group["weight_decay"])
+    params = list(model.parameters())
+    saved_group = {k: v for k, v in template.state_dict()["param_groups"][0].items() if k != "params"}
+    saved_group["params"] = list(range(len(params)))
+    state = {}
+    if optimizer.step_count > 0:
+        base = optimizer.flat.data.storage_offset()
+        for index, p in enumerate(params):
+            offset = p.data.storage_offset() - base
+            exp_avg, exp_avg_sq = (torch.as_strided(flat, p.shape, p.stride(), offset).detach().to("cpu", copy=True)
+                                   for flat in (optimizer.exp_avg, optimizer.exp_avg_sq))
+            state[index] = {"step": torch.tensor(float(optimizer.step_count), dtype=torch.float32),
+                            "exp_avg": exp_avg, "exp_avg_sq": exp_avg_sq}
+    return {"state": state, "param_groups": [saved_group]}
+
+
+def export_reference_checkpoint(directory, model, optimizer, ctx: ParallelContext, *, step: int,
+                                data=None, extra: dict | None = None) -> Path:
+    """Save a step directory that the reference's ``load_checkpoint``
+    (``nano_megatron/checkpoint.py:129-196``) resumes: the reference's model
+    configuration fields, a ``torch.optim.AdamW`` state made from the
+    FusedAdamW moments, its generator and token-stream state formats, and the
+    same file layout. Refuses, before writing anything, a model the reference
+    cannot describe (a SwiGLU width other than 4 x n_embd, RoPE theta other
+    than 10000) and an optimizer other than FusedAdamW. Collective like
+    :func:`save_checkpoint`; returns this rank's shard path."""
+    if not _valid_step(step):
+        raise ValueError(f"export_reference_checkpoint: step {step!r} is not a non-negative int")
+    config = getattr(model, "config", None)
+    problems = []
+    if config is None:
+        problems.append("the model has no GPTConfig")
+    else:
+        if config.ffn_size != 4 * config.n_embd:
+            problems.append(f"SwiGLU width {config.ffn_size}: the reference's models use 4 x n_embd = "
+                            f"{4 * config.n_embd}")
+        if config.rope_theta != 10000.0:
+            problems.append(f"RoPE theta {config.rope_theta}: the reference's models use 10000")
+    if not hasattr(optimizer, "exp_avg") or not hasattr(optimizer, "flat"):
+        problems.append("optimizer: only a FusedAdamW state converts to torch AdamW")
+    if problems:
+        raise CheckpointError(f"cannot write {directory} for the reference:\n  - " + "\n  - ".join(problems))
+    model_config = {k: v for k, v in asdict(config).items() if k not in _EXTENSION_FIELDS}
+
+    def make_shard():
+        stream = None
+        if data is not None:
+            state = data.state_dict()
+            stream = {"cursor": state["cursor"], **state["layout"],
+                      "identity": {"path": state["file"]["path"], "size_bytes": state["file"]["bytes"],
+                                   "mtime_ns": state["file"]["mtime_ns"]}}
+        states = _random_states()
+        rng = {"torch": states["cpu"], "python": states["python"]}
+        if "cuda" in states:
+            rng["cuda"] = states["cuda"]
+        return {"version": REFERENCE_FORMAT_VERSION, "topology": topology(ctx),
+                "model": _host_copy(model.state_dict()), "model_config": model_config,
+                "optimizer": _adamw_state_dict(model, optimizer), "step": step, "rng": rng,
+                "data": stream, "extra": dict(extra or {})}
+
+    return _write_step(Path(directory), ctx, step, REFERENCE_FORMAT_VERSION, make_shard)

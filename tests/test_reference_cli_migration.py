@@ -7,6 +7,9 @@ The reference CLI trains four steps at TP=2 with sequence parallelism on a
 token file, saving at step 2 and step 4. This package's CLI resumes the step-2
 directory with ``--load-reference`` and trains to step 4. Every rank's model
 state and data cursor at step 4 must match the reference's uninterrupted run.
+The other direction: this package's CLI saves in the reference's format
+(``--save-format reference``) and the reference's CLI resumes that step-2
+directory with its own ``--load``.
 """
 
 import os
@@ -60,3 +63,24 @@ def test_reference_run_continues_in_this_package(tmp_path):
         assert our_shard["model"].keys() == ref_shard["model"].keys()
         for name, value in ref_shard["model"].items():
             torch.testing.assert_close(our_shard["model"][name], value, rtol=1e-4, atol=1e-6, msg=name)
+
+
+def test_this_package_run_continues_in_the_reference(tmp_path):
+    if not os.path.isdir(os.path.join(REF, "nano_megatron")):
+        pytest.skip(f"reference package not found under {REF}")
+    tokens = tmp_path / "tokens.bin"
+    tokens.write_bytes(struct.pack("=4096H", *((5 * i + 1) % 64 for i in range(4096))))
+    our_out, ref_out = tmp_path / "ours", tmp_path / "reference"
+    _torchrun("nano_megatron_b200.train", COMMON + ["--steps=4", "--save-every=2", "--save-format=reference",
+                                                    f"--data={tokens}", f"--save={our_out}"], str(ROOT))
+    _torchrun("nano_megatron.train", COMMON + ["--steps=4", f"--data={tokens}", f"--save={ref_out}",
+                                               f"--load={our_out / 'step_00000002'}"], REF)
+    a, b = our_out / "step_00000004", ref_out / "step_00000004"
+    for rank in range(2):
+        our_shard = torch.load(a / f"rank_{rank:05d}.pt", weights_only=False)
+        ref_shard = torch.load(b / f"rank_{rank:05d}.pt", weights_only=False)
+        assert our_shard["step"] == ref_shard["step"] == 4
+        assert our_shard["data"]["cursor"] == ref_shard["data"]["cursor"]
+        assert our_shard["model"].keys() == ref_shard["model"].keys()
+        for name, value in our_shard["model"].items():
+            torch.testing.assert_close(ref_shard["model"][name], value, rtol=1e-4, atol=1e-6, msg=name)
