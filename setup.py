@@ -8,7 +8,7 @@ travels with the repository (no JIT cache). Only sm_100a code is generated.
 
 import os
 
-from setuptools import setup
+from setuptools import find_packages, setup
 from torch.utils.cpp_extension import BuildExtension, CUDAExtension
 
 HERE = os.path.dirname(os.path.abspath(__file__))
@@ -40,7 +40,10 @@ NVCC_FLAGS = [
 setup(
     name="nano_megatron_b200",
     version="0.1.0",
-    packages=["nano_megatron_b200"],
+    description="Megatron-style TP x SP x PP x DP GPT training with hand-written sm_100a (B200) kernels",
+    python_requires=">=3.10",
+    install_requires=["torch>=2.4"],
+    packages=find_packages(include=["nano_megatron_b200", "nano_megatron_b200.*"]),
     ext_modules=[
         CUDAExtension(
             name="nano_megatron_b200._C",
