@@ -7,8 +7,8 @@ package).
 Each case builds the reference's module, copies its state into this package's
 module of the same name and runs both on the same batch-first inputs; the
 outputs, the input gradients and every parameter gradient must agree to fp32
-rounding. This runs in one process at TP=1 and on Gloo ranks at TP=2 with and
-without sequence parallelism. Covered: ``ColumnParallelLinear``,
+rounding. This runs in one process at TP=1, on Gloo ranks at TP=2 with and
+without sequence parallelism, and at TP=4 with it. Covered: ``ColumnParallelLinear``,
 ``RowParallelLinear``, ``VocabParallelEmbedding``, ``RMSNorm``,
 ``ParallelAttention``, ``ParallelMLP``, ``TransformerLayer``,
 ``ParallelLMHead``, ``vocab_parallel_cross_entropy`` and the four
@@ -206,11 +206,10 @@ def _rank(rank, world, init_file, sp, ref_path, results):
 
 
 @pytest.mark.distributed
-@pytest.mark.parametrize("sp", [False, True], ids=["tp2", "tp2-sp"])
-def test_reference_modules_tp2(sp):
+@pytest.mark.parametrize("world,sp", [(2, False), (2, True), (4, True)], ids=["tp2", "tp2-sp", "tp4-sp"])
+def test_reference_modules_tp(world, sp):
     if not _have_reference():
         pytest.skip(f"reference package not found under {REF}")
-    world = 2
     spawn = mp.get_context("spawn")
     results = spawn.Queue()
     with tempfile.TemporaryDirectory() as tmp:
