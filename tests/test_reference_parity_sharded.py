@@ -107,8 +107,8 @@ def _run(tp, pp, dp, sp):
 
 
 @pytest.mark.parametrize("tp,pp,dp,sp", [(2, 1, 1, True), (2, 1, 1, False), (1, 2, 1, False), (2, 2, 1, True),
-                                         (1, 1, 2, False)],
-                         ids=["tp2-sp", "tp2", "pp2", "tp2xpp2-sp", "dp2"])
+                                         (1, 1, 2, False), (4, 1, 1, True), (2, 2, 2, True)],
+                         ids=["tp2-sp", "tp2", "pp2", "tp2xpp2-sp", "dp2", "tp4-sp", "tp2xpp2xdp2-sp"])
 def test_sharded_parity_with_reference(tp, pp, dp, sp):
     if not os.path.isdir(os.path.join(REF, "nano_megatron")):
         pytest.skip(f"reference package not found under {REF}")
