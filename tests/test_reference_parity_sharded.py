@@ -28,7 +28,7 @@ pytestmark = pytest.mark.distributed
 TOL = dict(rtol=1e-4, atol=1e-6)
 
 
-def _rank(rank, world, init_file, tp, pp, sp, ref_path, results):
+def _rank(rank, world, init_file, tp, pp, sp, tied, recompute, ref_path, results):
     sys.path.insert(0, ref_path)
     import nano_megatron.grads as rgrads
     import nano_megatron.model as rmodel
@@ -44,7 +44,8 @@ def _rank(rank, world, init_file, tp, pp, sp, ref_path, results):
     try:
         rctx = rpar.init_parallel(tp_size=tp, pp_size=pp)
         ctx = init_parallel(tp_size=tp, pp_size=pp)
-        kw = dict(vocab_size=64, n_layer=2 * pp, n_head=4, n_embd=32, seq_len=8, sequence_parallel=sp)
+        kw = dict(vocab_size=64, n_layer=2 * pp, n_head=4, n_embd=32, seq_len=8, sequence_parallel=sp,
+                  tie_word_embeddings=tied, recompute=recompute)
         rcfg, cfg = rmodel.GPTConfig(**kw), GPTConfig(**kw)
         torch.manual_seed(1000 + rank)
         ref = rmodel.GPT(rcfg, rctx)
@@ -59,8 +60,8 @@ def _rank(rank, world, init_file, tp, pp, sp, ref_path, results):
             a, b = torch.stack(l_ours).sum(), torch.stack(l_ref).sum()
             if not torch.allclose(a, b, **TOL):
                 failures.append(f"loss {a.item():.7f} != {b.item():.7f}")
-        rgrads.finalize_gradients(ref, rctx, tie_embeddings=True, sequence_parallel=sp)
-        finalize_gradients(ours, ctx, tie_embeddings=True, sequence_parallel=sp)
+        rgrads.finalize_gradients(ref, rctx, tie_embeddings=tied, sequence_parallel=sp)
+        finalize_gradients(ours, ctx, tie_embeddings=tied, sequence_parallel=sp)
         ref_params = dict(ref.named_parameters())
         for name, p in ours.named_parameters():
             r = ref_params.get(name)
@@ -68,8 +69,8 @@ def _rank(rank, world, init_file, tp, pp, sp, ref_path, results):
                 failures.append(f"{name}: missing gradient")
             elif not torch.allclose(p.grad, r.grad, **TOL):
                 failures.append(f"{name}: max |diff| {(p.grad - r.grad).abs().max().item():.3e}")
-        n_ref = rgrads.clip_grad_norm(ref, rctx, 1.0, tie_embeddings=True)
-        n_ours = clip_grad_norm(ours, ctx, 1.0, tie_embeddings=True)
+        n_ref = rgrads.clip_grad_norm(ref, rctx, 1.0, tie_embeddings=tied)
+        n_ours = clip_grad_norm(ours, ctx, 1.0, tie_embeddings=tied)
         if not torch.allclose(n_ours.double(), n_ref.double(), **TOL):
             failures.append(f"clip norm {n_ours.item():.7f} != {n_ref.item():.7f}")
     except Exception as e:  # reported to the parent as a failure of this rank
@@ -79,13 +80,13 @@ def _rank(rank, world, init_file, tp, pp, sp, ref_path, results):
         dist.destroy_process_group()
 
 
-def _run(tp, pp, dp, sp):
+def _run(tp, pp, dp, sp, tied=True, recompute=False):
     world = tp * pp * dp
     spawn = mp.get_context("spawn")
     results = spawn.Queue()
     with tempfile.TemporaryDirectory() as tmp:
         init_file = os.path.join(tmp, "init")
-        procs = [spawn.Process(target=_rank, args=(r, world, init_file, tp, pp, sp, REF, results))
+        procs = [spawn.Process(target=_rank, args=(r, world, init_file, tp, pp, sp, tied, recompute, REF, results))
                  for r in range(world)]
         for p in procs:
             p.start()
@@ -113,3 +114,10 @@ def test_sharded_parity_with_reference(tp, pp, dp, sp):
     if not os.path.isdir(os.path.join(REF, "nano_megatron")):
         pytest.skip(f"reference package not found under {REF}")
     _run(tp, pp, dp, sp)
+
+
+def test_sharded_parity_untied_with_recompute():
+    """Untied embeddings (no tied-group sum) and whole-block recompute, at TP2 x PP2 with SP."""
+    if not os.path.isdir(os.path.join(REF, "nano_megatron")):
+        pytest.skip(f"reference package not found under {REF}")
+    _run(2, 2, 1, True, tied=False, recompute=True)
