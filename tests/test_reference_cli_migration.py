@@ -28,7 +28,7 @@ pytestmark = pytest.mark.distributed
 
 COMMON = ["--sequence-parallel", "--num-microbatches=2", "--micro-batch-size=2", "--n-layer=2",
           "--n-head=4", "--n-embd=32", "--vocab-size=64", "--seq-len=8", "--lr=0.001"]
-LAYOUTS = {"tp2-sp": (["--tp=2"], 2), "tp2xpp2-sp": (["--tp=2", "--pp=2"], 4)}
+LAYOUTS = {"tp2-sp": (["--tp=2"], 2), "tp2xpp2-sp": (["--tp=2", "--pp=2"], 4), "dp2": (["--dp=2"], 2)}
 
 
 def _port():
