@@ -95,3 +95,16 @@ def test_a_layout_the_model_does_not_divide_over_is_refused(source):
     with pytest.raises(ValueError):
         reshard(step, tmp / "tp3", tp=3, pp=1)
     assert not (tmp / "tp3").exists()
+
+
+def test_untied_embeddings_round_trip(source, tmp_path):
+    _, tokens, _ = source
+    _train(4, ["--tp=2", "--pp=2", "--steps=1", "--untie-embeddings", f"--save={tmp_path / 'run'}"],
+           tmp_path, tokens)
+    step = tmp_path / "run" / "step_00000001"
+    back = reshard(reshard(step, tmp_path / "tp1", tp=1, pp=1), tmp_path / "back", tp=2, pp=2)
+    one = _shards(tmp_path / "tp1")[0]["model"]
+    assert not torch.equal(one["embedding.weight"], one["lm_head.weight"])
+    for a, b in zip(_shards(step), _shards(back)):
+        assert all(torch.equal(a["model"][k], b["model"][k]) for k in a["model"])
+        assert torch.equal(a["optimizer"]["state"]["exp_avg_sq"], b["optimizer"]["state"]["exp_avg_sq"])
