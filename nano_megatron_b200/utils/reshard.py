@@ -123,9 +123,18 @@ def _read_step(src: Path):
     configs = {repr(s.get("model_config")) for s in shards.values()}
     if len(configs) > 1:
         problems.append("the shards hold different model configurations")
+    layout = (sizes.get("tp"), sizes.get("pp"), sizes.get("dp"))
+    if not all(isinstance(n, int) and n > 0 for n in layout) or layout[0] * layout[1] * layout[2] != len(shards):
+        problems.append(f"parallel sizes {sizes!r} do not describe {len(shards)} shards")
+    else:
+        for ctx in contexts(*layout):
+            saved = shards[ctx.rank].get("topology") if ctx.rank in shards else None
+            if saved != ckpt.topology(ctx):
+                problems.append(f"{ckpt.shard_name(ctx.rank)}: topology {saved!r}, the manifest's layout "
+                                f"gives {ckpt.topology(ctx)!r}")
     if problems:
         ckpt._fail(src, problems)
-    return manifest, (sizes["tp"], sizes["pp"], sizes["dp"]), shards
+    return manifest, layout, shards
 
 
 def _logical_state(config: GPTConfig, layout, shards):

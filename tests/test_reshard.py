@@ -108,3 +108,18 @@ def test_untied_embeddings_round_trip(source, tmp_path):
     for a, b in zip(_shards(step), _shards(back)):
         assert all(torch.equal(a["model"][k], b["model"][k]) for k in a["model"])
         assert torch.equal(a["optimizer"]["state"]["exp_avg_sq"], b["optimizer"]["state"]["exp_avg_sq"])
+
+
+def test_a_manifest_that_disagrees_with_its_shards_is_refused(source, tmp_path):
+    import shutil
+
+    from nano_megatron_b200.utils.checkpoint import CheckpointError
+    _, _, step = source
+    copy = tmp_path / "copy"
+    shutil.copytree(step, copy)
+    manifest = torch.load(copy / "manifest.pt", weights_only=False)
+    manifest["parallel_sizes"] = {"tp": 4, "pp": 1, "dp": 1}
+    torch.save(manifest, copy / "manifest.pt")
+    with pytest.raises(CheckpointError, match="topology"):
+        reshard(copy, tmp_path / "out", tp=1, pp=1)
+    assert not (tmp_path / "out").exists()
