@@ -131,8 +131,9 @@ class ParallelAttention(nn.Module):
     """MHA sharded over heads; one fused QKV GEMM, one row-parallel output GEMM.
 
     Parity: ``nano_megatron/model.py:92-128``. ``forward(x, cos, sin)`` is the
-    reference's call (batch-first ``[b, s, H]``); the model runs
-    :meth:`forward_rows` on its sequence-major token rows.
+    reference's call (batch-first ``[b, s, H]``); the model calls
+    ``forward(rows, cos, sin, batch, dtype)`` on its sequence-major token rows
+    (:meth:`forward_rows`), so module hooks see both.
     """
 
     def __init__(self, config: GPTConfig, ctx: ParallelContext):
@@ -152,8 +153,11 @@ class ParallelAttention(nn.Module):
     def fused_groups(self, prefix: str):
         return [[f"{prefix}q.weight", f"{prefix}k.weight", f"{prefix}v.weight"]]
 
-    def forward(self, x, cos, sin):
-        """``x [b, s, H]`` (``s = S/tp`` under sequence parallelism) -> ``[b, s, H]``."""
+    def forward(self, x, cos, sin, *rows_form):
+        """``x [b, s, H]`` (``s = S/tp`` under sequence parallelism) -> ``[b, s, H]``;
+        with ``rows_form = (batch, dtype)``, :meth:`forward_rows`."""
+        if rows_form:
+            return self.forward_rows(x, rows_form[0], cos, sin, rows_form[1])
         return _batch_first_call(self.forward_rows, x, cos, sin, _compute_dtype(x))
 
     def forward_rows(self, x, batch, cos, sin, dtype):
@@ -170,7 +174,8 @@ class ParallelMLP(nn.Module):
 
     Parity: ``nano_megatron/model.py:131-153`` (with a configurable width;
     the reference's is ``4 * n_embd``). ``forward(x)`` is the reference's call
-    (batch-first ``[b, s, H]``); the model runs :meth:`forward_rows`.
+    (batch-first ``[b, s, H]``); the model calls ``forward(rows, dtype)``
+    (:meth:`forward_rows`).
     """
 
     def __init__(self, config: GPTConfig, ctx: ParallelContext):
@@ -186,8 +191,11 @@ class ParallelMLP(nn.Module):
     def fused_groups(self, prefix: str):
         return [[f"{prefix}gate.weight", f"{prefix}up.weight"]]
 
-    def forward(self, x):
-        """``x [b, s, H]`` (``s = S/tp`` under sequence parallelism) -> ``[b, s, H]``."""
+    def forward(self, x, *rows_form):
+        """``x [b, s, H]`` (``s = S/tp`` under sequence parallelism) -> ``[b, s, H]``;
+        with ``rows_form = (dtype,)``, :meth:`forward_rows`."""
+        if rows_form:
+            return self.forward_rows(x, rows_form[0])
         return _batch_first_call(lambda rows, _b, dtype: self.forward_rows(rows, dtype), x,
                                  _compute_dtype(x))
 
@@ -208,9 +216,9 @@ class TransformerLayer(nn.Module):
     """Pre-norm block: ``x + attn(norm(x))`` then ``x + mlp(norm(x))``.
 
     Parity: ``nano_megatron/model.py:156-166``. ``forward(x, cos, sin)`` is the
-    reference's call (batch-first ``[b, s, H]``); the model runs
-    :meth:`forward_rows`, where the first residual add and the MLP's norm are
-    one kernel.
+    reference's call (batch-first ``[b, s, H]``); the model calls
+    ``forward(rows, cos, sin, batch, dtype)`` (:meth:`forward_rows`), where the
+    first residual add and the MLP's norm are one kernel.
     """
 
     def __init__(self, config: GPTConfig, ctx: ParallelContext):
@@ -220,16 +228,19 @@ class TransformerLayer(nn.Module):
         self.mlp_norm = RMSNorm(config.n_embd)
         self.mlp = ParallelMLP(config, ctx)
 
-    def forward(self, x, cos, sin):
-        """``x [b, s, H]`` -> ``[b, s, H]``."""
+    def forward(self, x, cos, sin, *rows_form):
+        """``x [b, s, H]`` -> ``[b, s, H]``; with ``rows_form = (batch, dtype)``,
+        :meth:`forward_rows`."""
+        if rows_form:
+            return self.forward_rows(x, rows_form[0], cos, sin, rows_form[1])
         return _batch_first_call(self.forward_rows, x, cos, sin, _compute_dtype(x))
 
     def forward_rows(self, x, batch, cos, sin, dtype):
         """``x [s*b, H]`` (sequence-major rows) -> ``[s*b, H]``."""
-        a = self.attn.forward_rows(self.attn_norm(x), batch, cos, sin, dtype)
+        a = self.attn(self.attn_norm(x), cos, sin, batch, dtype)
         # residual add and the MLP's norm in one pass
         x, h = add_rms_norm(x, a.reshape(-1, a.shape[-1]), self.mlp_norm.weight, self.mlp_norm.eps)
-        return x + self.mlp.forward_rows(h, dtype)
+        return x + self.mlp(h, dtype)
 
 
 class ParallelLMHead(nn.Module):
@@ -362,10 +373,10 @@ class GPT(nn.Module):
                 # drops; the second is the recomputation before backward
                 calls[0] += 1
                 with discarded_forward(calls[0] == 1):
-                    return layer.forward_rows(h, batch, cos, sin, dtype)
+                    return layer(h, cos, sin, batch, dtype)
 
             return checkpoint(run, h, batch, cos, sin, dtype, use_reentrant=False)
-        return layer.forward_rows(h, batch, cos, sin, dtype)
+        return layer(h, cos, sin, batch, dtype)
 
     def forward(self, x, labels=None):
         """Token ids ``[b, S]`` on the first stage, hidden ``[s, b, H]`` elsewhere.
@@ -384,8 +395,8 @@ class GPT(nn.Module):
             self._cuda_checked = True
         if self.first_stage:
             batch = x.shape[0]
-            ids = x.t().reshape(-1)  # sequence-major token order
-            h = self.embedding.embed_rows(ids, sequence_parallel=sp, out_dtype=dtype)
+            ids = x.t().reshape(-1)  # sequence-major token order: 1-D ids are token rows
+            h = self.embedding(ids, sequence_parallel=sp, out_dtype=dtype)
         else:
             s_local = cfg.seq_len // ctx.tp_size if sp else cfg.seq_len
             if x.dim() != 3 or x.shape[0] != s_local or x.shape[2] != cfg.n_embd:

@@ -137,6 +137,8 @@ def worker(rank, world, init_file, args, results):
 
         failures = list(failures_pre)
         seq = config.seq_len // (args.tp if config.sequence_parallel else 1)
+        if not shapes:
+            failures.append("no layer forward was seen by the forward hooks")
         if any(s[0] != seq * args.micro_batch_size for s in shapes):
             failures.append(f"activation rows {[s[0] for s in shapes]} != {seq * args.micro_batch_size}")
         if ctx.is_last_stage:

@@ -1,6 +1,7 @@
-"""A non-first pipeline stage takes its hidden state sequence-first
-``[s, b, H]``; any other layout is refused with the expected shape instead of
-being read with the batch and sequence axes swapped."""
+"""What a stage's forward accepts and exposes: a non-first pipeline stage takes
+its hidden state sequence-first ``[s, b, H]`` and refuses any other layout with
+the expected shape (instead of reading swapped axes); forward hooks on the
+model's modules fire."""
 
 import pytest
 import torch
@@ -31,3 +32,20 @@ def test_other_layouts_are_refused(shape):
     model, _ = _last_stage()
     with pytest.raises(ValueError, match=r"sequence-first \[8, batch, 32\]"):
         model(torch.randn(*shape))
+
+
+def test_forward_hooks_on_the_model_modules_fire():
+    """The model calls its modules (row form), so hooks registered on them run,
+    as they do on the reference's modules."""
+    torch.manual_seed(0)
+    cfg = GPTConfig(vocab_size=64, n_layer=2, n_head=4, n_embd=32, seq_len=8)
+    model = GPT(cfg, ParallelContext.single())
+    seen = []
+    modules = [model.embedding, *model.layers, model.layers[0].attn, model.layers[0].mlp, model.final_norm]
+    for m in modules:
+        m.register_forward_hook(lambda mod, _i, out, seen=seen: seen.append((type(mod).__name__, tuple(out.shape))))
+    model(torch.randint(0, 64, (3, 8)), torch.randint(0, 64, (3, 8)))
+    names = [n for n, _ in seen]
+    assert names.count("TransformerLayer") == 2 and "VocabParallelEmbedding" in names
+    assert "ParallelAttention" in names and "ParallelMLP" in names and "RMSNorm" in names
+    assert all(shape == (8 * 3, 32) for _, shape in seen)
