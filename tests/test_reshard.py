@@ -63,7 +63,9 @@ def test_round_trips_are_exact(source):
     original = _shards(step)
     assert len(_shards(one)) == 1 and len(_shards(tmp / "tp2dp2")) == 4
     for copy in (back, via_dp):
-        for a, b in zip(original, _shards(copy)):
+        copied = _shards(copy)
+        assert len(copied) == len(original) == 4
+        for a, b in zip(original, copied):
             assert a["topology"] == b["topology"] and a["step"] == b["step"] and a["extra"] == b["extra"]
             assert a["data"] == b["data"]
             assert a["model"].keys() == b["model"].keys()
@@ -105,7 +107,10 @@ def test_untied_embeddings_round_trip(source, tmp_path):
     back = reshard(reshard(step, tmp_path / "tp1", tp=1, pp=1), tmp_path / "back", tp=2, pp=2)
     one = _shards(tmp_path / "tp1")[0]["model"]
     assert not torch.equal(one["embedding.weight"], one["lm_head.weight"])
-    for a, b in zip(_shards(step), _shards(back)):
+    original, copied = _shards(step), _shards(back)
+    assert len(original) == len(copied) == 4
+    for a, b in zip(original, copied):
+        assert a["model"].keys() == b["model"].keys()
         assert all(torch.equal(a["model"][k], b["model"][k]) for k in a["model"])
         assert torch.equal(a["optimizer"]["state"]["exp_avg_sq"], b["optimizer"]["state"]["exp_avg_sq"])
 
