@@ -4,10 +4,11 @@ A stage builds only its own layers: the embedding on the first stage, the final
 norm and LM head on the last. A non-first stage takes a hidden state, a
 non-last stage returns one, so the pipeline schedule stays outside the model.
 
-Layout: activations are sequence-first and token-major. A stage boundary
-carries ``[s, b, H]`` (``s = S/tp`` under sequence parallelism); inside a
-stage the residual stream is the flattened ``[s*b, H]``. Token ids and labels
-are given batch-first ``[b, S]`` as in the reference and transposed once.
+Layout: inside a stage the residual stream is sequence-first and token-major,
+``[s*b, H]`` (``s = S/tp`` under sequence parallelism), so a sequence shard is
+a contiguous row range. At the stage's edges everything is batch-first as in
+the reference: token ids and labels ``[b, S]``, hidden states ``[b, s, H]``
+(for one sequence per microbatch the two layouts are the same memory).
 
 Attention uses one fused ``[H, 3H/tp]`` QKV weight and the MLP one fused
 ``[H, 2F/tp]`` gate|up weight; the separate ``q``/``k``/``v`` and ``gate``/``up``
@@ -274,9 +275,8 @@ class GPT(nn.Module):
     Parity: ``nano_megatron/model.py:200-281`` (size checks, stage split, tie
     at one stage, RoPE tables as non-persistent buffers, whole-block
     recompute in training). Differences: parameters are views of flat fp32
-    buffers (``flat_buffers``), compute is in ``config.activation_dtype``
-    without autocast, and a non-last stage returns its hidden state
-    sequence-first ``[s, b, H]``.
+    buffers (``flat_buffers``), and compute is in ``config.activation_dtype``
+    without autocast.
     """
 
     def __init__(self, config: GPTConfig, ctx: ParallelContext | None = None,
@@ -379,11 +379,11 @@ class GPT(nn.Module):
         return layer(h, cos, sin, batch, dtype)
 
     def forward(self, x, labels=None):
-        """Token ids ``[b, S]`` on the first stage, hidden ``[s, b, H]`` elsewhere.
+        """Token ids ``[b, S]`` on the first stage, hidden ``[b, s, H]`` elsewhere.
 
         Returns the mean loss on the last stage when ``labels [b, S]`` is
         given, the vocab-sharded logits ``[b, S, V/tp]`` when it is not, and
-        the hidden state ``[s, b, H]`` on every other stage.
+        the hidden state ``[b, s, H]`` on every other stage.
         """
         cfg, ctx = self.config, self.ctx
         dtype = cfg.activation_dtype
@@ -399,11 +399,11 @@ class GPT(nn.Module):
             h = self.embedding(ids, sequence_parallel=sp, out_dtype=dtype)
         else:
             s_local = cfg.seq_len // ctx.tp_size if sp else cfg.seq_len
-            if x.dim() != 3 or x.shape[0] != s_local or x.shape[2] != cfg.n_embd:
-                raise ValueError(f"a non-first pipeline stage takes its hidden state sequence-first "
-                                 f"[{s_local}, batch, {cfg.n_embd}]; got {tuple(x.shape)}")
-            batch = x.shape[1]
-            h = x.reshape(-1, cfg.n_embd)
+            if x.dim() != 3 or x.shape[1] != s_local or x.shape[2] != cfg.n_embd:
+                raise ValueError(f"a non-first pipeline stage takes its hidden state batch-first "
+                                 f"[batch, {s_local}, {cfg.n_embd}]; got {tuple(x.shape)}")
+            batch = x.shape[0]
+            h = x.transpose(0, 1).reshape(-1, cfg.n_embd)  # a view for one sequence per microbatch
         if h.dtype != dtype:
             h = h.to(dtype)
 
@@ -411,7 +411,7 @@ class GPT(nn.Module):
             h = self._layer_call(layer, h, batch, dtype)
 
         if not self.last_stage:
-            return h.view(-1, batch, cfg.n_embd)
+            return h.view(-1, batch, cfg.n_embd).transpose(0, 1)
 
         hn = self.final_norm(h)
         head = WeightRef.of(self.lm_head.weight)

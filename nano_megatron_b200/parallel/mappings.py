@@ -11,8 +11,8 @@ function                                    forward                backward
 ``reduce_scatter_to_sequence_parallel_...`` reduce-scatter (SUM)   all-gather along seq
 ==========================================  =====================  =====================
 
-Activations in this framework are stored sequence-first (``[s, b, H]`` or the
-flattened ``[s*b, H]``), so a sequence shard is one contiguous slab and the
+Inside a stage, activations in this framework are token rows in
+sequence-major order (``[s*b, H]``), so a sequence shard is one contiguous slab and the
 model's own gather/scatter (``all_gather_sequence`` and
 ``reduce_scatter_sequence``, sequence on dim 0 by default) need no transposes.
 The four public functions keep the reference's batch-first convention: the

@@ -13,7 +13,8 @@ sides always post matching pairs (deadlock-free by construction). On NCCL the
 receives are waited on by the compute stream only (no host blocking) and sends
 are not waited on at all until the end of the step: the compute stream runs on
 while the NCCL stream carries the activation to the next stage.
-Activations cross stages sequence-first as ``[s, b, H]``.
+Activations cross stages batch-first as ``[b, s, H]`` (``s = S/tp`` under
+sequence parallelism), the reference's exchange shape.
 
 Parity: ``nano_megatron/pipeline.py:22-224`` (schedule, warm-up depth, P2P
 order, loss scaling by ``1/M``).
@@ -149,7 +150,7 @@ def forward_backward_1f1b(model: nn.Module, batches: Sequence[Batch], config, de
     device = torch.device(device)
     sp = config.sequence_parallel and ctx.tp_size > 1
     seq = config.seq_len // (ctx.tp_size if sp else 1)
-    p2p = _P2P(ctx, (seq, micro_batch_size, config.n_embd), config.activation_dtype, device)
+    p2p = _P2P(ctx, (micro_batch_size, seq, config.n_embd), config.activation_dtype, device)
     hook = before_last_backward
     if hook is None:
         method = getattr(model, "before_last_backward", None)

@@ -28,7 +28,7 @@ pytestmark = pytest.mark.distributed
 TOL = dict(rtol=1e-4, atol=1e-6)
 
 
-def _rank(rank, world, init_file, tp, pp, sp, tied, recompute, ref_path, results):
+def _rank(rank, world, init_file, tp, pp, sp, tied, recompute, driver, ref_path, results):
     sys.path.insert(0, ref_path)
     import nano_megatron.grads as rgrads
     import nano_megatron.model as rmodel
@@ -55,7 +55,10 @@ def _rank(rank, world, init_file, tp, pp, sp, tied, recompute, ref_path, results
         ours.train()
         batches = synthetic_batches(cfg, 2, 4, 0, ctx.dp_rank)
         l_ref = rpipe.forward_backward_1f1b(ref, batches, rcfg, "cpu", rctx)
-        l_ours = forward_backward_1f1b(ours, batches, cfg, "cpu", ctx)
+        if driver == "reference":  # the reference's own schedule drives this package's stage model
+            l_ours = rpipe.forward_backward_1f1b(ours, batches, cfg, "cpu", rctx)
+        else:
+            l_ours = forward_backward_1f1b(ours, batches, cfg, "cpu", ctx)
         if ctx.is_last_stage:
             a, b = torch.stack(l_ours).sum(), torch.stack(l_ref).sum()
             if not torch.allclose(a, b, **TOL):
@@ -80,13 +83,14 @@ def _rank(rank, world, init_file, tp, pp, sp, tied, recompute, ref_path, results
         dist.destroy_process_group()
 
 
-def _run(tp, pp, dp, sp, tied=True, recompute=False):
+def _run(tp, pp, dp, sp, tied=True, recompute=False, driver="ours"):
     world = tp * pp * dp
     spawn = mp.get_context("spawn")
     results = spawn.Queue()
     with tempfile.TemporaryDirectory() as tmp:
         init_file = os.path.join(tmp, "init")
-        procs = [spawn.Process(target=_rank, args=(r, world, init_file, tp, pp, sp, tied, recompute, REF, results))
+        procs = [spawn.Process(target=_rank, args=(r, world, init_file, tp, pp, sp, tied, recompute, driver, REF,
+                                                        results))
                  for r in range(world)]
         for p in procs:
             p.start()
@@ -121,3 +125,12 @@ def test_sharded_parity_untied_with_recompute():
     if not os.path.isdir(os.path.join(REF, "nano_megatron")):
         pytest.skip(f"reference package not found under {REF}")
     _run(2, 2, 1, True, tied=False, recompute=True)
+
+
+def test_the_reference_schedule_drives_this_package_stages():
+    """Stage models exchange the reference's activation shapes, so the
+    reference's forward_backward_1f1b runs this package's stages at TP2 x PP2
+    with SP and gets the reference's losses, gradients and clip norm."""
+    if not os.path.isdir(os.path.join(REF, "nano_megatron")):
+        pytest.skip(f"reference package not found under {REF}")
+    _run(2, 2, 1, True, driver="reference")
