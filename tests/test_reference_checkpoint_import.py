@@ -20,12 +20,6 @@ import numpy as np
 import pytest
 import torch
 
-
-def zip_strict(*seqs):
-    """zip that fails when the sequences differ in length."""
-    return zip(*seqs, strict=True)
-
-
 REF = os.environ.get("NMB_REFERENCE_PATH") or os.path.join(
     os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "baseline", "_ref")
 
@@ -106,16 +100,16 @@ def test_resume_a_reference_run(ref, tmp_path):
     step, extra = import_reference_checkpoint(step_dir, m, m_opt, ctx, data=m_stream)
     assert step == 2 and extra == {"note": "ref"}
     assert m_opt.param_groups[0]["lr"] == 1e-3 and m_opt.step_count == 2
-    for (n1, p1), (n2, p2) in zip_strict(r.named_parameters(), m.named_parameters()):
+    for (n1, p1), (n2, p2) in zip(r.named_parameters(), m.named_parameters(), strict=True):
         assert n1 == n2 and torch.equal(p1, p2)
 
     for _ in range(2):
         lr_, br = _ref_step(ref, r, r_opt, r_stream, rcfg, rctx)
         lo, bo = _our_step(m, m_opt, m_stream, cfg, ctx)
-        for (x1, y1), (x2, y2) in zip_strict(br, bo):
+        for (x1, y1), (x2, y2) in zip(br, bo, strict=True):
             assert torch.equal(x1, x2) and torch.equal(y1, y2)
         torch.testing.assert_close(lo, lr_, rtol=1e-5, atol=1e-6)
-    for p1, p2 in zip_strict(r.parameters(), m.parameters()):
+    for p1, p2 in zip(r.parameters(), m.parameters(), strict=True):
         torch.testing.assert_close(p2, p1, rtol=1e-4, atol=1e-6)
 
 
@@ -134,7 +128,7 @@ def test_refuses_a_checkpoint_of_another_configuration(ref, tmp_path):
     before = [p.detach().clone() for p in other.parameters()]
     with pytest.raises(CheckpointError, match="n_layer"):
         import_reference_checkpoint(tmp_path / "s", other, FusedAdamW(other), ParallelContext.single())
-    assert all(torch.equal(a, p) for a, p in zip_strict(before, other.parameters()))
+    assert all(torch.equal(a, p) for a, p in zip(before, other.parameters(), strict=True))
     theta = GPT(GPTConfig(**KW, rope_theta=500000.0), ParallelContext.single())
     with pytest.raises(CheckpointError, match="RoPE theta"):
         import_reference_checkpoint(tmp_path / "s", theta, FusedAdamW(theta), ParallelContext.single())
@@ -170,16 +164,16 @@ def test_reference_resumes_an_exported_checkpoint(ref, tmp_path):
     step, extra = rckpt.load_checkpoint(step_dir, r, r_opt, rctx, data=r_stream)
     assert step == 2 and extra == {"note": "ours"}
     assert r_opt.param_groups[0]["lr"] == 1e-3
-    for (n1, p1), (n2, p2) in zip_strict(r.named_parameters(), m.named_parameters()):
+    for (n1, p1), (n2, p2) in zip(r.named_parameters(), m.named_parameters(), strict=True):
         assert n1 == n2 and torch.equal(p1, p2)
 
     for _ in range(2):
         lr_, br = _ref_step(ref, r, r_opt, r_stream, rcfg, rctx)
         lo, bo = _our_step(m, m_opt, m_stream, cfg, ctx)
-        for (x1, y1), (x2, y2) in zip_strict(br, bo):
+        for (x1, y1), (x2, y2) in zip(br, bo, strict=True):
             assert torch.equal(x1, x2) and torch.equal(y1, y2)
         torch.testing.assert_close(lr_, lo, rtol=1e-5, atol=1e-6)
-    for p1, p2 in zip_strict(r.parameters(), m.parameters()):
+    for p1, p2 in zip(r.parameters(), m.parameters(), strict=True):
         torch.testing.assert_close(p1, p2, rtol=1e-4, atol=1e-6)
 
 
@@ -203,7 +197,7 @@ def test_export_then_import_is_exact(ref, tmp_path):
     b_opt = FusedAdamW(b)
     b_stream = TokenStream(tokens, dtype="uint16", seq_len=KW["seq_len"])
     assert import_reference_checkpoint(tmp_path / "s", b, b_opt, ctx, data=b_stream)[0] == 3
-    assert all(torch.equal(p, q) for p, q in zip_strict(a.parameters(), b.parameters()))
+    assert all(torch.equal(p, q) for p, q in zip(a.parameters(), b.parameters(), strict=True))
     assert torch.equal(a_opt.exp_avg, b_opt.exp_avg) and torch.equal(a_opt.exp_avg_sq, b_opt.exp_avg_sq)
     assert b_opt.step_count == 3 and b_opt.param_groups == a_opt.param_groups
     assert b_stream.cursor == a_stream.cursor

@@ -10,12 +10,6 @@ import sys
 import pytest
 import torch
 
-
-def zip_strict(*seqs):
-    """zip that fails when the sequences differ in length."""
-    return zip(*seqs, strict=True)
-
-
 REF = os.environ.get("NMB_REFERENCE_PATH") or os.path.join(
     os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "baseline", "_ref")
 
@@ -41,7 +35,7 @@ def test_same_init_logits_loss_grads(ref):
     r = model_mod.GPT(model_mod.GPTConfig(**kw))
     torch.manual_seed(0)
     m = GPT(GPTConfig(**kw))
-    for (n1, p1), (n2, p2) in zip_strict(r.named_parameters(), m.named_parameters()):
+    for (n1, p1), (n2, p2) in zip(r.named_parameters(), m.named_parameters(), strict=True):
         assert n1 == n2 and torch.equal(p1, p2)
     x, y = torch.randint(0, 64, (2, 8)), torch.randint(0, 64, (2, 8))
     torch.testing.assert_close(m(x), r(x), rtol=0, atol=0)
@@ -49,7 +43,7 @@ def test_same_init_logits_loss_grads(ref):
     torch.testing.assert_close(lm, lr, rtol=1e-6, atol=1e-6)
     lr.backward()
     lm.backward()
-    for (n, p1), (_, p2) in zip_strict(r.named_parameters(), m.named_parameters()):
+    for (n, p1), (_, p2) in zip(r.named_parameters(), m.named_parameters(), strict=True):
         torch.testing.assert_close(p2.grad, p1.grad, rtol=1e-5, atol=1e-7, msg=n)
 
 
@@ -75,7 +69,7 @@ def test_training_steps_match(ref):
         o1.step()
         o2.step()
         torch.testing.assert_close(sum(l2), sum(l1), rtol=1e-5, atol=1e-6)
-    for p1, p2 in zip_strict(r.parameters(), m.parameters()):
+    for p1, p2 in zip(r.parameters(), m.parameters(), strict=True):
         torch.testing.assert_close(p2, p1, rtol=1e-4, atol=1e-5)
 
 
