@@ -184,6 +184,8 @@ def reshard(src, dst, tp: int, pp: int, dp: int = 1) -> Path:
     returns ``dst``. Nothing is written when the source fails its checks or
     the model does not divide over the target layout."""
     src, dst = Path(src), Path(dst)
+    if dst.resolve() == src.resolve():
+        raise ValueError(f"reshard writes a new step directory; {dst} is the source")
     manifest, layout, shards = _read_step(src)
     config = GPTConfig(**shards[0]["model_config"])
     targets = contexts(tp, pp, dp)

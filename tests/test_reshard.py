@@ -97,6 +97,9 @@ def test_a_layout_the_model_does_not_divide_over_is_refused(source):
     with pytest.raises(ValueError):
         reshard(step, tmp / "tp3", tp=3, pp=1)
     assert not (tmp / "tp3").exists()
+    with pytest.raises(ValueError, match="source"):
+        reshard(step, step, tp=1, pp=1)
+    assert (step / "manifest.pt").exists()
 
 
 def test_untied_embeddings_round_trip(source, tmp_path):
