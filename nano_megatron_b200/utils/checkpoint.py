@@ -228,6 +228,15 @@ def _fail(directory: Path, problems: list[str]):
     raise CheckpointError(f"cannot resume from {directory}:\n  - " + "\n  - ".join(problems))
 
 
+def _no_manifest(directory: Path) -> str:
+    """The missing-manifest problem, naming the latest complete step directory
+    inside ``directory`` when it is a save root rather than a step."""
+    steps = sorted(p for p in directory.glob("step_*") if (p / MANIFEST).is_file()) if directory.is_dir() else []
+    if steps:
+        return f"no manifest.pt here; this looks like a save directory, pass a step such as {steps[-1]}"
+    return "no manifest.pt: the save did not complete"
+
+
 def load_checkpoint(directory, model, optimizer, ctx: ParallelContext, *, data=None,
                     map_location="cpu") -> tuple[int, dict]:
     """Validate ``directory`` for this rank, then restore model, optimizer, RNG and
@@ -237,7 +246,7 @@ def load_checkpoint(directory, model, optimizer, ctx: ParallelContext, *, data=N
     problems: list[str] = []
     manifest_path = directory / MANIFEST
     if not manifest_path.is_file():
-        _fail(directory, ["no manifest.pt: the save did not complete"])
+        _fail(directory, [_no_manifest(directory)])
     manifest = _read(manifest_path, "manifest", "cpu", problems)
     if manifest is None:
         _fail(directory, problems)
@@ -360,7 +369,7 @@ def import_reference_checkpoint(directory, model, optimizer, ctx: ParallelContex
     directory = Path(directory)
     problems: list[str] = []
     if not (directory / MANIFEST).is_file():
-        _fail(directory, ["no manifest.pt: the save did not complete"])
+        _fail(directory, [_no_manifest(directory)])
     manifest = _read(directory / MANIFEST, "manifest", "cpu", problems)
     if manifest is None:
         _fail(directory, problems)

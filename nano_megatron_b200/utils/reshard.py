@@ -106,7 +106,7 @@ def _read_step(src: Path):
     problems: list[str] = []
     manifest = ckpt._read(src / ckpt.MANIFEST, "manifest", "cpu", problems)
     if manifest is None:
-        ckpt._fail(src, problems or ["no manifest.pt: the save did not complete"])
+        ckpt._fail(src, [ckpt._no_manifest(src)] if not (src / ckpt.MANIFEST).exists() else problems)
     if manifest.get("version") != ckpt.FORMAT_VERSION:
         ckpt._fail(src, [f"format version {manifest.get('version')!r}: this tool reads "
                          f"{ckpt.FORMAT_VERSION} (save_checkpoint's format)"])

@@ -166,3 +166,16 @@ def test_step_must_be_a_non_negative_int(tmp_path):
     for bad in (-1, 1.0, True):
         with pytest.raises(ValueError, match="step"):
             ck.save_checkpoint(tmp_path / "x", model, opt, SOLO, step=bad)
+
+
+def test_a_save_root_is_answered_with_its_latest_step(tmp_path):
+    model, opt, stream = _run(5, tmp_path)
+    root = tmp_path / "ckpt"
+    for step in (1, 2):
+        _train(model, opt, stream, 1)
+        ck.save_checkpoint(root / f"step_{step:08d}", model, opt, SOLO, step=step, data=stream)
+    (root / "step_00000003").mkdir()  # an incomplete step (no manifest) is not suggested
+    with pytest.raises(ck.CheckpointError, match="step_00000002"):
+        ck.load_checkpoint(root, model, opt, SOLO, data=stream)
+    with pytest.raises(ck.CheckpointError, match="the save did not complete"):
+        ck.load_checkpoint(root / "step_00000003", model, opt, SOLO, data=stream)
