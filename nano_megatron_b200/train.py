@@ -29,7 +29,7 @@ from .parallel.grads import (GradBucketer, clip_coefficient, clip_grad_norm, fin
                              grad_norm_squared, synchronize_model_parameters)
 from .parallel.pipeline import forward_backward_1f1b
 from .utils.checkpoint import (export_reference_checkpoint, import_reference_checkpoint, load_checkpoint,
-                               save_checkpoint)
+                               reference_config_problems, save_checkpoint)
 from .utils.data import TokenStream, synthetic_batches
 
 
@@ -189,6 +189,8 @@ def _train_loop(args, rank, watch, fault):
     device = (torch.device("cuda", int(os.environ["LOCAL_RANK"])) if args.device == "cuda"
               else torch.device(args.device))
     config = config_from_args(args)
+    if args.save and args.save_format == "reference" and reference_config_problems(config):
+        raise ValueError("--save-format reference: " + "; ".join(reference_config_problems(config)))
     trainer = Trainer(config, ctx, device, lr=args.lr, clip=args.clip, seed=args.seed,
                       init_device=args.init_device, fused_tp=not args.no_fused_tp,
                       dp_bucket_mb=args.dp_bucket_mb)

@@ -421,6 +421,19 @@ def import_reference_checkpoint(directory, model, optimizer, ctx: ParallelContex
 _EXTENSION_FIELDS = ("ffn_hidden_size", "rope_theta", "init_std")
 
 
+def reference_config_problems(config) -> list[str]:
+    """Why the reference could not describe a model of ``config`` (empty when
+    it can): its models fix the SwiGLU width at 4 x n_embd and RoPE theta at
+    10000."""
+    problems = []
+    if config.ffn_size != 4 * config.n_embd:
+        problems.append(f"SwiGLU width {config.ffn_size}: the reference's models use 4 x n_embd = "
+                        f"{4 * config.n_embd}")
+    if config.rope_theta != 10000.0:
+        problems.append(f"RoPE theta {config.rope_theta}: the reference's models use 10000")
+    return problems
+
+
 def _adamw_state_dict(model, optimizer) -> dict:
     """FusedAdamW's flat moments as a ``torch.optim.AdamW`` state dict over
     ``model.parameters()`` (the inverse of :func:`_load_adamw`): each
@@ -457,15 +470,7 @@ def export_reference_checkpoint(directory, model, optimizer, ctx: ParallelContex
     if not _valid_step(step):
         raise ValueError(f"export_reference_checkpoint: step {step!r} is not a non-negative int")
     config = getattr(model, "config", None)
-    problems = []
-    if config is None:
-        problems.append("the model has no GPTConfig")
-    else:
-        if config.ffn_size != 4 * config.n_embd:
-            problems.append(f"SwiGLU width {config.ffn_size}: the reference's models use 4 x n_embd = "
-                            f"{4 * config.n_embd}")
-        if config.rope_theta != 10000.0:
-            problems.append(f"RoPE theta {config.rope_theta}: the reference's models use 10000")
+    problems = ["the model has no GPTConfig"] if config is None else reference_config_problems(config)
     if not hasattr(optimizer, "exp_avg") or not hasattr(optimizer, "flat"):
         problems.append("optimizer: only a FusedAdamW state converts to torch AdamW")
     if problems:

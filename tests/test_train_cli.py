@@ -1,8 +1,9 @@
 """End-to-end ``torchrun`` CLI: two steps straight through must produce
 bit-identical rank shards (model, optimizer, RNG, data cursor) to one step,
 save, restart from the checkpoint, one more step (TP=2 PP=2 SP recompute
-bf16); and DP=2 x PP=2 with the gradient bucketer must match one average
-after backward bit for bit."""
+bf16); DP=2 x PP=2 with the gradient bucketer must match one average after
+backward bit for bit; a save format the model does not fit is refused at
+startup."""
 
 import socket
 import struct
@@ -80,3 +81,15 @@ def test_dp_buckets_match_one_average_after_backward(tmp_path):
     for r in range(4):
         name = f"rank_{r:05d}.pt"
         _equal(torch.load(b / name, weights_only=False), torch.load(a / name, weights_only=False))
+
+
+def test_reference_save_format_is_checked_before_training(tmp_path):
+    """A model the reference cannot describe is refused at startup, not at the first save."""
+    import os
+    env = dict(os.environ, OMP_NUM_THREADS="1", RANK="0", LOCAL_RANK="0", WORLD_SIZE="1",
+               MASTER_ADDR="127.0.0.1", MASTER_PORT=str(_port()))
+    cmd = [sys.executable, "-m", "nano_megatron_b200.train", "--steps=3", "--ffn-hidden-size=96",
+           "--save-format=reference", f"--save={tmp_path / 'out'}"]
+    r = subprocess.run(cmd, cwd=ROOT, capture_output=True, text=True, timeout=120, env=env)
+    assert r.returncode != 0 and "SwiGLU width 96" in r.stderr
+    assert "step   0" not in r.stdout and not (tmp_path / "out").exists()
