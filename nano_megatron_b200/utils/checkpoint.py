@@ -304,12 +304,7 @@ def _reference_config_problems(saved: dict | None, model) -> list[str]:
         return [f"model configuration: checkpoint {saved!r}, this model {ours!r}"]
     problems = [f"model configuration {key}: checkpoint {value!r}, this model {ours.get(key)!r}"
                 for key, value in saved.items() if ours.get(key) != value]
-    config = model.config
-    if config.ffn_size != 4 * config.n_embd:
-        problems.append(f"SwiGLU width {config.ffn_size}: the reference's models use 4 x n_embd = {4 * config.n_embd}")
-    if config.rope_theta != 10000.0:
-        problems.append(f"RoPE theta {config.rope_theta}: the reference's models use 10000")
-    return problems
+    return problems + reference_config_problems(model.config)
 
 
 def _adamw_problems(state: dict, model, optimizer) -> list[str]:
